@@ -1,0 +1,455 @@
+"""Decode throughput of the Qwen2.5-0.5B continuous-batching hot path on B200.
+
+Workload (one engine replica per GPU, weak scaling): 256 ragged sequences per GPU, context
+lengths seeded uniform in [128, 2048], KV pool pre-filled with N(0,1) values, random-init bf16
+weights (std 0.02, tied embeddings), greedy decoding.  A step is one decode step for all 256
+sequences: block-table update, 24 layers, final norm, lm_head + argmax, seq_len advance.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+  python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+
+Prints one JSON line (rank 0).  `value` is device-timed with inputs resident in HBM (tokens fed
+back on the device, no host round trip between steps); `e2e` is the same metric through the
+public per-step API (`DecodeEngine.step`: host token lists in and out, pinned H2D/D2H copies and
+a sync every step).  `--impl reference` times the oracle (numpy restatement of the reference's
+CPU PyTorch path) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "decode tokens/sec @256 ragged seqs per B200 (1/2/4/8); paged-attn HBM GB/s"
+SEQS = 256
+CTX_LO, CTX_HI = 128, 2048
+CPU_SAMPLE_SEQS = 32
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def _dist():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def _config(world, extra=None):
+    c = {"workload": "qwen2.5-0.5b decode step, 256 ragged seqs/GPU, ctx U[128,2048], greedy, "
+                     "random-init bf16 weights (std 0.02, tied), KV pre-filled N(0,1)",
+         "seqs_per_gpu": SEQS, "ctx_range": [CTX_LO, CTX_HI], "block_size": 16,
+         "parallelism": f"replicas x{world} (no collectives)",
+         "l2": "inputs larger than L2 (~4.4 GB read per step), no flush"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+def _peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_from_profiles():
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary, scaled to
+    this workload's algorithmic bytes when the capture was a smaller case."""
+    p = os.path.join(REPO, "profiles", "paged_attention_decode_256seqs.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":")[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled in the background during a timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.5)
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        mhz, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------------------------
+def build_workload(device, seed, steps_total):
+    """Engine replica with 256 sequences at their sampled context lengths, KV pre-filled."""
+    import torch
+    from tiny_infra_b200.cache_manager import KVCacheManager
+    from tiny_infra_b200.config import QwenConfig
+    from tiny_infra_b200.engine import DecodeEngine
+    from tiny_infra_b200.qwen2 import Qwen2ForCausalLM
+
+    cfg = QwenConfig()
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, SEQS).astype(np.int32)
+    max_seq = CTX_HI + steps_total + 16
+    blocks = int(sum((int(c) + steps_total + 15) // 16 for c in ctx)) + 64
+    sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=seed, tied=True, device=device)
+    model = Qwen2ForCausalLM(cfg, device=device).load_reference_state_dict(sd)
+    kv = KVCacheManager(SEQS, max_seq, cfg.num_layers, cfg.num_key_value_heads, cfg.head_dim,
+                        device=device, num_blocks=blocks)
+    slots = list(range(SEQS))
+    kv.plan_tokens(slots, [int(c) for c in ctx])            # reference allocation order
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    for li in range(cfg.num_layers):                         # N(0,1) K/V everywhere
+        kv.key_cache[li].normal_(generator=g)
+        kv.value_cache[li].normal_(generator=g)
+    kv.advance_device(slots, ctx)
+    engine = DecodeEngine(model, kv)
+    first = torch.from_numpy(rng.integers(0, cfg.vocab_size, SEQS).astype(np.int32)).to(device)
+    return cfg, sd, model, kv, engine, slots, ctx, first
+
+
+def attention_roofline(engine, kv, cfg, ctx, reps, peak_gbs):
+    """Time the paged-attention kernel alone (layer 0 of this workload) with CUDA events on its
+    stream; achieved = algorithmic bytes per launch / mean launch time."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    D, NH, KVH = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+    lib = N.lib()
+    n = len(ctx)
+    q = torch.randn(n, NH * D, device=kv.device, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    slots = torch.arange(n, dtype=torch.int32, device=kv.device)
+    lens = kv.seq_len[:n].clone()
+    s = torch.cuda.current_stream().cuda_stream
+
+    def launch():
+        N.check(lib.ti_paged_attention_decode(
+            out.data_ptr(), NH * D, q.data_ptr(), NH * D, kv.key_cache[0].data_ptr(),
+            kv.value_cache[0].data_ptr(), kv.total_physical_blocks, kv.block_tables.data_ptr(),
+            kv.block_tables.stride(0), slots.data_ptr(), lens.data_ptr(), n, NH, KVH, D,
+            kv.block_size, kv.max_blocks_per_seq, N.TI_DTYPE_BF16, 0, engine.ws.data_ptr(),
+            engine.ws.numel(), s))
+
+    for _ in range(5):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / reps / 1e3
+    tot = int(lens.sum().item())
+    algo = tot * KVH * D * 2 * 2 + 2 * n * NH * D * 2      # K+V of every context token, q, out
+    achieved = algo / t / 1e9
+    return {"bound": "hbm", "kernel": "ti::attn::decode_kernel (paged decode attention)",
+            "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": _traffic_from_profiles(),
+            "algorithmic_bytes_per_launch": algo, "us_per_launch": round(t * 1e6, 2)}
+
+
+# ---------------------------------------------------------------------------------------------
+def oracle_sample(sd, kv, ctx, seed):
+    """The oracle (CPU restatement of the reference path) set up on CPU_SAMPLE_SEQS of the
+    workload's sequences: fp32 copies of the weights and of those sequences' KV."""
+    import torch
+    from oracle import kernels as OK
+    from oracle import model as OM
+    from oracle.cache import OracleKVCache
+
+    cfg = OM.OracleConfig()
+    W = {k: v.float().cpu().numpy() for k, v in sd.items()}
+    W["lm_head.weight"] = W["model.embed_tokens.weight"]
+    n = CPU_SAMPLE_SEQS
+    bs = 16
+    need = [(int(c) + 1 + bs - 1) // bs + 1 for c in ctx[:n]]
+    cache = OracleKVCache(n, int(max(ctx[:n])) + 64, cfg.num_layers, cfg.num_key_value_heads,
+                          cfg.head_dim, bs, num_blocks=int(sum(need)) + 8)
+    bt = kv.block_tables[:n].cpu().numpy()
+    k_dev, v_dev = [], []
+    nxt = 0
+    for i in range(n):
+        nb = (int(ctx[i]) + bs - 1) // bs
+        phys = torch.from_numpy(bt[i, :nb].astype(np.int64)).to(kv.device)
+        k_dev.append(kv.key_cache[:, phys])
+        v_dev.append(kv.value_cache[:, phys])
+        cache.block_tables[i, :nb] = np.arange(nxt, nxt + nb)
+        nxt += nb
+    cache.key_cache[:, :nxt] = torch.cat(k_dev, 1).float().cpu().numpy()
+    cache.value_cache[:, :nxt] = torch.cat(v_dev, 1).float().cpu().numpy()
+    cache.free_blocks = list(range(nxt, cache.total_physical_blocks))
+    cache.seq_len[:] = ctx[:n]
+    cos, sin = OK.rope_table(cache.max_seq_len, cfg.head_dim, cfg.rope_theta)
+    tokens = np.random.default_rng(seed).integers(0, cfg.vocab_size, n)
+    return W, cfg, cache, cos, sin, tokens
+
+
+def oracle_decode_steps(state, steps, min_seconds=0.0):
+    """Run oracle decode steps (greedy, tokens fed back); returns (steps run, seconds)."""
+    from oracle import model as OM
+    W, cfg, cache, cos, sin, tokens = state
+    n = len(tokens)
+    idx = np.arange(n)
+    t0 = time.perf_counter()
+    done = 0
+    while done < steps or (time.perf_counter() - t0) < min_seconds:
+        logits = OM.forward(W, cfg, tokens[:, None], idx, cache, cos, sin)
+        cache.seq_len[idx] += 1
+        tokens = np.argmax(logits[:, -1], axis=-1)
+        done += 1
+        if min_seconds and done >= 2 and (time.perf_counter() - t0) >= min_seconds:
+            break
+    state[5][:] = tokens
+    return done, time.perf_counter() - t0
+
+
+def _cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count()
+
+
+# ---------------------------------------------------------------------------------------------
+def run_reference(a, rank, world):
+    """CPU reference arm: the oracle restatement of the reference's PyTorch path on the host
+    cores, same metric and workload (a bounded sample of it per step)."""
+    if rank != 0:
+        return 0
+    import torch
+    torch.set_num_threads(_cores())
+    from oracle import model as OM
+    from oracle.cache import OracleKVCache
+    from oracle import kernels as OK
+    cfg = OM.OracleConfig()
+    W = OM.init_weights(cfg, seed=a.seed, tied=True, bf16=True)
+    rng = np.random.default_rng(a.seed)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, SEQS).astype(np.int32)[:CPU_SAMPLE_SEQS]
+    n = CPU_SAMPLE_SEQS
+    steps_total = a.warmup + a.steps
+    cache = OracleKVCache(n, CTX_HI + steps_total + 16, cfg.num_layers, cfg.num_key_value_heads,
+                          cfg.head_dim, 16, allocate_pool=False,
+                          num_blocks=int(sum((int(c) + steps_total + 15) // 16 for c in ctx)) + 8)
+    shape = (cfg.num_layers, cache.total_physical_blocks, cfg.num_key_value_heads, 16,
+             cfg.head_dim)
+    kr = np.random.default_rng(a.seed + 1)
+    cache.key_cache = kr.standard_normal(shape, dtype=np.float32)
+    cache.value_cache = kr.standard_normal(shape, dtype=np.float32)
+    for i, c in enumerate(ctx):          # FIFO allocation of each context's blocks
+        nb = (int(c) + 15) // 16
+        for lb in range(nb):
+            cache.block_tables[i, lb] = cache.free_blocks.pop(0)
+    cache.seq_len[:] = ctx
+    cos, sin = OK.rope_table(cache.max_seq_len, cfg.head_dim, cfg.rope_theta)
+    state = [W, cfg, cache, cos, sin, rng.integers(0, cfg.vocab_size, n)]
+    oracle_decode_steps(state, a.warmup)
+    done, secs = oracle_decode_steps(state, a.steps)
+    value = n * done / secs
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(secs / done * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": _config(1, {"sample": f"{n} of the 256 sequences per step"}),
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": _cores(),
+                             "kind": "port",
+                             "sample": f"{n} sequences of the workload per decode step, "
+                                       f"{done} steps, numpy fp32 restatement of the reference path"},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(a, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    from tiny_infra_b200 import _native as N
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+    steps_total = a.warmup + a.steps
+    # the engine is built for warm-up + timed + e2e steps
+    cfg, sd, model, kv, engine, slots, ctx, first = build_workload(device, a.seed + rank,
+                                                                    2 * steps_total + 4)
+    peak, peak_kind = _peaks()
+
+    # ---- device-resident decode (value) ----
+    plan = engine.plan_steps(slots, steps_total)
+    rows = plan.shape[1]
+    engine.d_in[1, :SEQS].copy_(torch.arange(SEQS, dtype=torch.int32))
+    engine.d_in[0, :SEQS].copy_(first)
+    sampler = ClockSampler(local)
+    sampler.start()
+    # warm-up (also captures the graph)
+    for k in range(a.warmup):
+        engine.d_in[2, :rows].copy_(plan[k])
+        engine._replay(rows)
+        engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = N.launch_count()
+    e0.record()
+    for k in range(a.warmup, steps_total):
+        engine.d_in[2, :rows].copy_(plan[k])
+        engine._replay(rows)
+        engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    secs = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    launches = engine.launches_per_step.get(rows, 0) * a.steps
+    value = world * SEQS * a.steps / secs
+
+    # ---- e2e through the public per-step API (host tokens in/out) ----
+    toks = engine.next_tok[:SEQS].cpu().numpy()
+    for _ in range(2):
+        toks = engine.step(slots, toks)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2 = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+    e2[0].record()
+    for _ in range(a.steps):
+        toks = engine.step(slots, toks)
+    e2[1].record()
+    torch.cuda.synchronize()
+    esecs = e2[0].elapsed_time(e2[1]) / 1e3
+    if world > 1:
+        t = torch.tensor([esecs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        esecs = float(t.item())
+    e2e = world * SEQS * a.steps / esecs
+
+    roof = attention_roofline(engine, kv, cfg, ctx, 50, peak) if rank == 0 else None
+    status = N.device_status()
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        torch.set_num_threads(_cores())
+        st = list(oracle_sample(sd, kv, ctx, a.seed))
+        oracle_decode_steps(st, 1)
+        done, csecs = oracle_decode_steps(st, 2, min_seconds=10.0)
+        cpu = {"value": round(CPU_SAMPLE_SEQS * done / csecs, 2), "unit": "tokens/s",
+               "cores": _cores(), "kind": "port",
+               "sample": f"{CPU_SAMPLE_SEQS} of the 256 sequences, {done} greedy decode steps, "
+                         "numpy fp32 restatement of the reference path (oracle/)"}
+    if world > 1:
+        dist.barrier()
+    engine.graphs.clear()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    kv_bytes = int(ctx.sum() + SEQS * (a.warmup + a.steps / 2)) * cfg.num_layers * 2 * 2 * 64 * 2
+    step_bytes = model.weight_bytes() + kv_bytes
+    ms = secs / a.steps * 1e3
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, random token ids, N(0,1) KV)",
+        "config": _config(world, {"global_batch": SEQS * world}),
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 3 * SEQS * 4,
+                "d2h_bytes_per_step": SEQS * 4,
+                "api": "tiny_infra_b200.engine.DecodeEngine.step (host lists in/out)"},
+        "roofline": roof,
+        "step_roofline": {"bytes_per_step": step_bytes,
+                          "achieved_gbs": round(step_bytes / (secs / a.steps) / 1e9, 1),
+                          "peak_gbs": peak, "frac": round(step_bytes / (secs / a.steps) / 1e9 / peak, 4),
+                          "peak_kind": peak_kind},
+        "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": int(launches),
+        "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    a = _args()
+    rank, world, local = _dist()
+    if a.impl == "reference":
+        return run_reference(a, rank, world)
+    return run_ours(a, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,73 @@
+"""Build the reference project's own CUDA kernels from its sources into ``oracle/_ref/``.
+
+TEST INFRASTRUCTURE ONLY (the checker, never the product).  Compiles, unmodified and where they
+lie in the reference checkout, the three kernel/binding pairs the reference ships:
+
+    src/attention.cu  + src/attention_binding.cpp -> oracle/_ref/custom_paged_attn/*.so
+    src/fused_rope.cu + src/rope_binding.cpp      -> oracle/_ref/custom_rope/*.so
+    src/fused_swiglu.cu + src/swiglu_binding.cpp  -> oracle/_ref/custom_swiglu/*.so
+
+as PyTorch extensions for sm_100a (the reference builds with ``-arch=native``, setup.py:18).
+The built modules travel with the repository to the GPU box (``oracle/_ref`` is git-ignored but
+not excluded from the snapshot); there ``load_ref(name)`` imports them so that
+``tests/golden/make_kernel_golden.py`` can record the reference kernels' outputs.
+
+    python oracle/build_ref.py --ref /root/reference
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import importlib.util
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_OUT = os.path.join(HERE, "_ref")
+MODULES = {
+    "custom_paged_attn": ("src/attention.cu", "src/attention_binding.cpp"),
+    "custom_rope": ("src/fused_rope.cu", "src/rope_binding.cpp"),
+    "custom_swiglu": ("src/fused_swiglu.cu", "src/swiglu_binding.cpp"),
+}
+
+
+def build(ref_root: str, verbose: bool = False) -> list[str]:
+    from torch.utils.cpp_extension import load
+
+    built = []
+    for name, srcs in MODULES.items():
+        paths = [os.path.join(ref_root, s) for s in srcs]
+        if not all(os.path.exists(p) for p in paths):
+            raise FileNotFoundError(f"reference sources missing for {name}: {paths}")
+        out = os.path.join(REF_OUT, name)
+        os.makedirs(out, exist_ok=True)
+        load(name=name, sources=paths, build_directory=out, verbose=verbose,
+             extra_cflags=["-O3"],
+             extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"])
+        built.append(out)
+    return built
+
+
+def load_ref(name: str):
+    """Import a module built by :func:`build` (works without the reference checkout)."""
+    so = glob.glob(os.path.join(REF_OUT, name, f"{name}*.so"))
+    if not so:
+        raise FileNotFoundError(f"{name} not built under {REF_OUT}")
+    import torch  # noqa: F401  (the extension links against libtorch)
+    spec = importlib.util.spec_from_file_location(name, so[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("TINY_INFRA_REF", "/root/reference"))
+    ap.add_argument("--verbose", action="store_true")
+    a = ap.parse_args()
+    for p in build(a.ref, a.verbose):
+        print("built", p)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

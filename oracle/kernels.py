@@ -29,8 +29,9 @@ def paged_attention(out: np.ndarray, q: np.ndarray, k_cache: np.ndarray, v_cache
       * ctx == 0 returns early and leaves ``out`` untouched (attention.cu:62);
       * reading stops at the first negative block-table entry (attention.cu:90); if that leaves
         no token at all, the kernel's final ``o / d`` is 0/0, i.e. NaN (attention.cu:150);
-      * block-table columns beyond ``max_blocks`` are treated as absent (the reference kernel would
-        read the next row there, which is undefined for a caller).
+      * block-table columns beyond ``max_blocks`` and block ids outside the pool are treated as
+        absent (the reference kernel would read outside the table / pool there, which is
+        undefined for a caller).
     """
     B, NH, D = q.shape
     KVH = k_cache.shape[1]
@@ -46,7 +47,7 @@ def paged_attention(out: np.ndarray, q: np.ndarray, k_cache: np.ndarray, v_cache
         ks, vs = [], []
         for bi in range(min(nblk, max_blocks)):
             phys = int(block_tables[b, bi])
-            if phys < 0:
+            if phys < 0 or phys >= k_cache.shape[0]:
                 break
             ntok = min(block_size, ctx - bi * block_size)
             ks.append(k_cache[phys, :, :ntok, :])

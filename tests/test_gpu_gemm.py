@@ -1,0 +1,131 @@
+"""GPU parity of the tcgen05 projection GEMM and its fused epilogues against a float32 matmul
+of the same bf16/fp16-representable operands.
+
+Tolerance: fp32 accumulation in a different order, then one rounding of the output dtype:
+|err| <= 2^-8 |ref| + 1e-3 * rms(ref) (bf16 outputs); float32 outputs (residual epilogue):
+|err| <= 1e-4 * rms(ref) + 1e-6.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle.numerics import bf16_round
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(x, dt=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda().to(dt)
+
+
+def _gemm(epi, A, B, M, N, K, out=None, ldo=0, bias=None, aux_val=None, aux_idx=None,
+          block_n=128, split_k=1):
+    from tiny_infra_b200 import _native as N_
+    N_.check(N_.lib().ti_gemm(
+        epi, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K,
+        out.data_ptr() if out is not None else None, ldo,
+        bias.data_ptr() if bias is not None else None,
+        aux_val.data_ptr() if aux_val is not None else None,
+        aux_idx.data_ptr() if aux_idx is not None else None,
+        N_.dtype_code(A.dtype), block_n, split_k, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert N_.device_status() == 0
+
+
+def _operands(seed, M, N, K, wstd=0.05):
+    rng = np.random.default_rng(seed)
+    a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    b = bf16_round((rng.standard_normal((N, K)) * wstd).astype(np.float32))
+    return a, b
+
+
+def _close_bf16(got, ref):
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2))) + 1e-12
+    err = np.abs(got - ref)
+    assert (err <= 2.0 ** -8 * np.abs(ref) + 1e-3 * rms).all(), float(err.max())
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(256, 1152, 896, 64), (256, 1152, 896, 128),
+                                      (37, 256, 128, 64), (4096, 1152, 896, 128),
+                                      (300, 512, 896, 256)])
+def test_store_bias(cuda_device, M, N, K, bn):
+    from tiny_infra_b200 import _native as N_
+    a, b = _operands(M * 7 + N, M, N, K)
+    bias = bf16_round(np.random.default_rng(1).standard_normal(N).astype(np.float32) * 0.1)
+    A, B, Bi = _dev(a), _dev(b), _dev(bias)
+    out = torch.full((M, N), 9.0, dtype=torch.bfloat16, device="cuda")
+    _gemm(N_.TI_EPI_STORE, A, B, M, N, K, out=out, ldo=N, bias=Bi, block_n=bn)
+    _close_bf16(out.float().cpu().numpy(), a @ b.T + bias)
+
+
+def test_store_fp16(cuda_device):
+    from tiny_infra_b200 import _native as N_
+    M, N, K = 200, 384, 640
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((M, K)).astype(np.float16).astype(np.float32)
+    b = (rng.standard_normal((N, K)) * 0.05).astype(np.float16).astype(np.float32)
+    A, B = _dev(a, torch.float16), _dev(b, torch.float16)
+    out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    _gemm(N_.TI_EPI_STORE, A, B, M, N, K, out=out, ldo=N)
+    ref = a @ b.T
+    err = np.abs(out.float().cpu().numpy() - ref)
+    assert (err <= 2.0 ** -11 * np.abs(ref) + 1e-3).all()
+
+
+def test_swiglu_epilogue(cuda_device):
+    """gate/up projection with SwiGLU fused in the epilogue (weights interleaved per tile)."""
+    from tiny_infra_b200 import _native as N_
+    M, I, K, bn = 256, 1024, 896, 128
+    rng = np.random.default_rng(4)
+    a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    wg = bf16_round((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
+    wu = bf16_round((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
+    h = bn // 2
+    inter = np.concatenate([np.concatenate([wg[j:j + h], wu[j:j + h]]) for j in range(0, I, h)])
+    out = torch.empty((M, I), dtype=torch.bfloat16, device="cuda")
+    _gemm(N_.TI_EPI_SWIGLU, _dev(a), _dev(inter), M, 2 * I, K, out=out, ldo=I, block_n=bn)
+    g, u = a @ wg.T, a @ wu.T
+    _close_bf16(out.float().cpu().numpy(), g / (1 + np.exp(-g)) * u)
+
+
+@pytest.mark.parametrize("split", [1, 3, 6])
+def test_residual_split_k(cuda_device, split):
+    """x_f32 += A W^T with split-K partial sums reduced by red.global.add."""
+    from tiny_infra_b200 import _native as N_
+    M, N, K = 256, 896, 4864
+    a, b = _operands(5, M, N, K, wstd=0.02)
+    x0 = np.random.default_rng(6).standard_normal((M, N)).astype(np.float32)
+    x = torch.from_numpy(x0).cuda()
+    _gemm(N_.TI_EPI_RESIDUAL, _dev(a), _dev(b), M, N, K, out=x, ldo=N, block_n=64, split_k=split)
+    ref = x0 + a @ b.T
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    assert np.abs(x.cpu().numpy() - ref).max() <= 1e-4 * rms + 1e-6
+
+
+def test_argmax_epilogue(cuda_device):
+    """Per-tile (max, first argmax) of each row; reduced over tiles it is the row argmax.
+    Exact ties are planted to check the lowest-index rule."""
+    from tiny_infra_b200 import _native as N_
+    M, N, K, bn = 130, 32768, 896, 128
+    a, b = _operands(7, M, N, K)
+    b[5000] = b[123]                 # duplicate rows -> identical logits in columns 123, 5000
+    a[0] = bf16_round(b[123] * 64.0)  # ... and make them row 0's maximum
+    A, B = _dev(a), _dev(b)
+    nt = N // bn
+    val = torch.empty((M, nt), dtype=torch.float32, device="cuda")
+    idx = torch.empty((M, nt), dtype=torch.int32, device="cuda")
+    logits = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    _gemm(N_.TI_EPI_ARGMAX, A, B, M, N, K, out=logits, ldo=N, aux_val=val, aux_idx=idx, block_n=bn)
+    ref = a @ b.T
+    v, ix = val.cpu().numpy(), idx.cpu().numpy()
+    t = np.argmax(v, axis=1)
+    got = ix[np.arange(M), t]
+    want = np.argmax(ref, axis=1)
+    # where the top two logits are within accumulation noise the order may legitimately differ
+    srt = np.sort(ref, axis=1)
+    clear = (srt[:, -1] - srt[:, -2]) > 1e-3
+    assert (got[clear] == want[clear]).all()
+    np.testing.assert_allclose(v.max(axis=1), ref.max(axis=1), rtol=1e-5, atol=1e-4)
+    _close_bf16(logits.float().cpu().numpy(), ref)
+    assert got[0] == 123             # exact tie across tiles: lowest index wins
+    assert (ix >= 0).all() and (ix < N).all()

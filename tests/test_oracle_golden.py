@@ -153,3 +153,35 @@ def test_chunked_prefill_matches_whole_prefill():
     parts = [OK.paged_prefill_attention(q[0, a:b], kc, vc, table, a, bs)
              for a, b in ((0, 10), (10, 31), (31, 37))]
     np.testing.assert_allclose(np.concatenate(parts), whole, atol=1e-5, rtol=1e-5)
+
+
+def test_reference_kernels(golden_dir):
+    """The oracle restatements of src/attention.cu, src/fused_rope.cu and src/fused_swiglu.cu
+    against the reference kernels themselves, compiled from the reference sources
+    (oracle/build_ref.py) and run on a B200 by tests/golden/make_kernel_golden.py.  The
+    reference kernels compute in fp32 and store fp16: tolerance is fp16 rounding of the output
+    (2^-11 relative) plus 1e-3 absolute for fp32 summation order (the reference sums q.k with
+    a block tree reduction and uses __expf)."""
+    path = os.path.join(golden_dir, "kernel_golden.npz")
+    if not os.path.exists(path):
+        pytest.skip("kernel_golden.npz not generated")
+    from tests.golden.make_kernel_golden import inputs
+    g = np.load(path)
+    x = inputs()
+    for name in ("attn64", "attn128"):
+        q, k, v, bt, ctx = x[name]
+        ref = g[f"{name}_out"].astype(np.float32)
+        out = np.full(q.shape, 7.0, np.float32)
+        OK.paged_attention(out, q.astype(np.float32), k.astype(np.float32),
+                           v.astype(np.float32), bt, ctx, 16)
+        live = ctx > 0
+        assert (ref[~live] == 7.0).all()           # ctx == 0: untouched (attention.cu:62)
+        np.testing.assert_allclose(out[live], ref[live], atol=1e-3, rtol=2.0 ** -10)
+    rq, rk, pos = x["rope"]
+    qf, kf = rq.astype(np.float32).copy(), rk.astype(np.float32).copy()
+    cos, sin = OK.rope_table(4096, 64, 1e6)
+    OK.rope_inplace(qf, kf, cos, sin, pos)
+    np.testing.assert_allclose(qf, g["rope_q"].astype(np.float32), atol=1e-3, rtol=2.0 ** -10)
+    np.testing.assert_allclose(kf, g["rope_k"].astype(np.float32), atol=1e-3, rtol=2.0 ** -10)
+    sw = OK.swiglu(x["swiglu"].astype(np.float32))
+    np.testing.assert_allclose(sw, g["swiglu_out"].astype(np.float32), atol=1e-3, rtol=2.0 ** -10)

@@ -1,0 +1,328 @@
+"""Qwen2 (Qwen2.5-0.5B architecture) forward on the sm_100a kernels of this package.
+
+Drop-in for the reference's ``Qwen2ForCausalLM`` (models/qwen_25.py:232-251): same call
+``model(input_ids [B, S] int32, batch_indices [B], kv_cache, cos, sin) -> logits [B, S, V]``,
+same semantics (positions start at ``kv_cache.seq_len[batch_indices]``, the cache is written
+for every layer, ``seq_len`` is NOT advanced -- the caller does that, engine/scheduler.py:234,266;
+decode attends over seq_len + 1 tokens, models/qwen_25.py:115), and weights load from the
+reference's state-dict names (``load_reference_state_dict``).
+
+Per layer the forward is 6 kernel launches:
+  rmsnorm -> QKV GEMM (+bias, RoPE, KV append) -> paged attention (decode or prefill)
+  -> O GEMM (+residual, split-K) -> rmsnorm -> gate/up GEMM (+SwiGLU) -> down GEMM (+residual)
+with the residual stream kept in float32 (the reference keeps it in the model dtype; float32
+is closer to the float32 oracle).  The lm_head runs only on the rows whose logits are needed
+and, for greedy decoding, reduces to one token per row inside the GEMM epilogue.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .config import QwenConfig
+
+GATE_UP_TILE = 128          # block_n of the gate/up GEMM: 64 gate rows then 64 up rows
+LM_TILE = 128               # block_n of the lm_head GEMM (argmax partials per 128 columns)
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+@dataclass
+class PackedBatch:
+    """One forward call over packed tokens.  ``decode``: every sequence has exactly one new
+    token; otherwise prefill chunks (query tiles of 16 tokens)."""
+    input_ids: torch.Tensor        # int32 [T]
+    positions: torch.Tensor        # int32 [T]
+    slot_mapping: torch.Tensor     # int64 [T]
+    seq_slots: torch.Tensor        # int32 [nseq] block-table row of each sequence
+    start_pos: torch.Tensor        # int32 [nseq]
+    cu_seqlens: torch.Tensor       # int32 [nseq + 1]
+    ctx_lens: torch.Tensor         # int32 [nseq] (decode: start + 1)
+    tile_seq: torch.Tensor | None  # int32 [tiles] (prefill)
+    tile_q0: torch.Tensor | None
+    num_tokens: int
+    num_seqs: int
+    decode: bool
+    last_rows: torch.Tensor        # int64 [nseq] row of each sequence's last token
+
+
+class Qwen2ForCausalLM:
+    def __init__(self, config: QwenConfig | None = None, device="cuda",
+                 dtype: torch.dtype = torch.bfloat16) -> None:
+        self.config = config or QwenConfig()
+        self.device = torch.device(device)
+        self.dtype = dtype
+        if self.device.type != "cuda":
+            raise RuntimeError("tiny_infra_b200 runs on a CUDA device only")
+        c = self.config
+        if c.hidden_size % c.num_attention_heads or c.intermediate_size % (GATE_UP_TILE // 2):
+            raise RuntimeError("unsupported model dimensions")
+        self.weights: dict[str, torch.Tensor] = {}
+        self._ws = N.Workspace()
+        self._bufs: dict[str, torch.Tensor] = {}
+        self.tied = False
+
+    # ---- weights -------------------------------------------------------------------------
+    def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
+        """Load weights named as the reference module's state dict (models/qwen_25.py), fusing
+        q/k/v (+biases) into one [(NH+2KVH)*D, H] matrix and interleaving gate/up rows per
+        GEMM tile for the SwiGLU epilogue.  A missing ``lm_head.weight`` or one identical to the
+        embedding means tied embeddings."""
+        c, dev, dt = self.config, self.device, self.dtype
+
+        def get(name):
+            t = sd[name]
+            if isinstance(t, np.ndarray):
+                t = torch.from_numpy(np.ascontiguousarray(t))
+            return t.to(device=dev, dtype=dt).contiguous()
+
+        W = {}
+        W["embed"] = get("model.embed_tokens.weight")
+        lm = sd.get("lm_head.weight")
+        self.tied = lm is None or lm is sd["model.embed_tokens.weight"]
+        W["lm_head"] = W["embed"] if self.tied else get("lm_head.weight")
+        W["norm"] = get("model.norm.weight")
+        h = GATE_UP_TILE // 2
+        for i in range(c.num_layers):
+            p = f"model.layers.{i}"
+            W[f"{i}.qkv"] = torch.cat([get(f"{p}.self_attn.q_proj.weight"),
+                                       get(f"{p}.self_attn.k_proj.weight"),
+                                       get(f"{p}.self_attn.v_proj.weight")]).contiguous()
+            W[f"{i}.qkv_bias"] = torch.cat([get(f"{p}.self_attn.q_proj.bias"),
+                                            get(f"{p}.self_attn.k_proj.bias"),
+                                            get(f"{p}.self_attn.v_proj.bias")]).contiguous()
+            W[f"{i}.o"] = get(f"{p}.self_attn.o_proj.weight")
+            g, u = get(f"{p}.mlp.gate_proj.weight"), get(f"{p}.mlp.up_proj.weight")
+            I, H = g.shape
+            W[f"{i}.gate_up"] = torch.stack([g.view(I // h, h, H), u.view(I // h, h, H)],
+                                            dim=1).reshape(2 * I, H).contiguous()
+            W[f"{i}.down"] = get(f"{p}.mlp.down_proj.weight")
+            W[f"{i}.ln1"] = get(f"{p}.input_layernorm.weight")
+            W[f"{i}.ln2"] = get(f"{p}.post_attention_layernorm.weight")
+        self.weights = W
+        return self
+
+    @staticmethod
+    def random_state_dict(config: QwenConfig, seed: int = 0, std: float = 0.02,
+                          tied: bool = True, device="cuda",
+                          dtype: torch.dtype = torch.bfloat16) -> dict:
+        """Seeded random-init weights N(0, std) in the reference's state-dict naming, generated
+        on ``device`` (RMSNorm weights are ones, as the reference initialises them)."""
+        c = config
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        H, D, NH, KVH, I, V = (c.hidden_size, c.head_dim, c.num_attention_heads,
+                               c.num_key_value_heads, c.intermediate_size, c.vocab_size)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * std).to(dtype)
+
+        sd = {"model.embed_tokens.weight": rnd(V, H)}
+        for i in range(c.num_layers):
+            p = f"model.layers.{i}"
+            sd[f"{p}.self_attn.q_proj.weight"] = rnd(NH * D, H)
+            sd[f"{p}.self_attn.q_proj.bias"] = rnd(NH * D)
+            sd[f"{p}.self_attn.k_proj.weight"] = rnd(KVH * D, H)
+            sd[f"{p}.self_attn.k_proj.bias"] = rnd(KVH * D)
+            sd[f"{p}.self_attn.v_proj.weight"] = rnd(KVH * D, H)
+            sd[f"{p}.self_attn.v_proj.bias"] = rnd(KVH * D)
+            sd[f"{p}.self_attn.o_proj.weight"] = rnd(H, NH * D)
+            sd[f"{p}.mlp.gate_proj.weight"] = rnd(I, H)
+            sd[f"{p}.mlp.up_proj.weight"] = rnd(I, H)
+            sd[f"{p}.mlp.down_proj.weight"] = rnd(H, I)
+            sd[f"{p}.input_layernorm.weight"] = torch.ones(H, device=device, dtype=dtype)
+            sd[f"{p}.post_attention_layernorm.weight"] = torch.ones(H, device=device, dtype=dtype)
+        sd["model.norm.weight"] = torch.ones(H, device=device, dtype=dtype)
+        sd["lm_head.weight"] = sd["model.embed_tokens.weight"] if tied else rnd(V, H)
+        return sd
+
+    def weight_bytes(self) -> int:
+        """Bytes of weights one decode step streams (the tied lm_head counted once)."""
+        seen, total = set(), 0
+        for t in self.weights.values():
+            if t.data_ptr() not in seen:
+                seen.add(t.data_ptr())
+                total += t.numel() * t.element_size()
+        return total
+
+    # ---- scratch buffers ---------------------------------------------------------------------
+    def _buf(self, name: str, shape, dtype) -> torch.Tensor:
+        n = int(np.prod(shape))
+        b = self._bufs.get(name)
+        if b is None or b.numel() < n or b.dtype != dtype:
+            b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
+            self._bufs[name] = b
+        return b[:n].view(*shape)
+
+    # ---- packed-batch planning (host) -----------------------------------------------------------
+    def plan(self, kv_cache, slots, counts, token_ids) -> PackedBatch:
+        """Allocate the new tokens' blocks (reference order) and build the batch metadata."""
+        dev = self.device
+        mapping, _ = kv_cache.plan_tokens(slots, counts)
+        nseq = len(slots)
+        start = np.array([kv_cache.seq_len_host(s) for s in slots], np.int32)
+        counts = np.asarray(counts, np.int32)
+        cu = np.zeros(nseq + 1, np.int32)
+        cu[1:] = np.cumsum(counts)
+        T = int(cu[-1])
+        pos = np.concatenate([start[i] + np.arange(counts[i], dtype=np.int32)
+                              for i in range(nseq)]) if T else np.zeros(0, np.int32)
+        decode = bool((counts == 1).all())
+        tseq, tq0 = None, None
+        if not decode:
+            ts, tq = [], []
+            for i in range(nseq):
+                for q0 in range(0, int(counts[i]), 16):
+                    ts.append(i)
+                    tq.append(q0)
+            tseq = torch.tensor(ts, dtype=torch.int32, device=dev)
+            tq0 = torch.tensor(tq, dtype=torch.int32, device=dev)
+        as_dev = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)  # noqa: E731
+        return PackedBatch(
+            input_ids=as_dev(np.asarray(token_ids, np.int32), torch.int32),
+            positions=as_dev(pos, torch.int32), slot_mapping=as_dev(mapping, torch.int64),
+            seq_slots=as_dev(np.asarray(slots, np.int32), torch.int32),
+            start_pos=as_dev(start, torch.int32), cu_seqlens=as_dev(cu, torch.int32),
+            ctx_lens=as_dev(start + counts, torch.int32), tile_seq=tseq, tile_q0=tq0,
+            num_tokens=T, num_seqs=nseq, decode=decode,
+            last_rows=as_dev(cu[1:] - 1, torch.int64))
+
+    # ---- forward -----------------------------------------------------------------------------
+    def scratch(self, rows: int, owner: dict | None = None) -> dict:
+        """Per-call activation buffers for ``rows`` tokens.  With ``owner`` (a dict kept by the
+        caller, e.g. a graph-captured engine) the buffers are allocated once there and never
+        move; otherwise the model's own growable buffers are used."""
+        c = self.config
+        D, NH, KVH = c.head_dim, c.num_attention_heads, c.num_key_value_heads
+        shapes = {"xn": (rows, c.hidden_size), "qkv": (rows, (NH + 2 * KVH) * D),
+                  "attn": (rows, NH * D), "act": (rows, c.intermediate_size)}
+        if owner is None:
+            return {k: self._buf(k, v, self.dtype) for k, v in shapes.items()}
+        for k, v in shapes.items():
+            if k not in owner:
+                owner[k] = torch.empty(*v, dtype=self.dtype, device=self.device)
+        return owner
+
+    @staticmethod
+    def _splits(rows: int, n: int, k: int) -> int:
+        """split-K factor for the residual GEMMs: enough CTAs to cover the SMs once."""
+        tiles = ((rows + 127) // 128) * (n // 64)
+        return int(max(1, min(8, k // 64 // 2, (2 * 148 + tiles - 1) // tiles)))
+
+    def _layers(self, pb: PackedBatch, kv_cache, cos: torch.Tensor, sin: torch.Tensor,
+                hidden: torch.Tensor, stream: int, num_layers: int | None = None,
+                bufs: dict | None = None, ws: torch.Tensor | None = None) -> None:
+        c, W, lib = self.config, self.weights, N.lib()
+        dt = N.dtype_code(self.dtype)
+        T, H, D = pb.num_tokens, c.hidden_size, c.head_dim
+        NH, KVH, I = c.num_attention_heads, c.num_key_value_heads, c.intermediate_size
+        QKV = (NH + 2 * KVH) * D
+        bufs = bufs or self.scratch(T)
+        xn, qkv, attn, act = bufs["xn"], bufs["qkv"], bufs["attn"], bufs["act"]
+        nb = kv_cache.total_physical_blocks
+        bt = kv_cache.block_tables
+        maxb = kv_cache.max_blocks_per_seq
+        if pb.decode and ws is None:
+            need = lib.ti_paged_attention_workspace_bytes(pb.num_seqs, NH, KVH, D, maxb, 0)
+            ws = self._ws.get(self.device, need)
+        split_o = self._splits(T, H, NH * D)
+        split_d = self._splits(T, H, I)
+        for li in range(c.num_layers if num_layers is None else num_layers):
+            kc, vc = kv_cache.key_cache[li], kv_cache.value_cache[li]
+            N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
+                                   W[f"{li}.ln1"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
+            N.check(lib.ti_gemm_qkv_rope(
+                xn.data_ptr(), H, W[f"{li}.qkv"].data_ptr(), H, W[f"{li}.qkv_bias"].data_ptr(),
+                T, H, NH, KVH, D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(),
+                pb.slot_mapping.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                pb.positions.data_ptr(), kv_cache.block_size, dt, stream))
+            if pb.decode:
+                N.check(lib.ti_paged_attention_decode(
+                    attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
+                    bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
+                    pb.num_seqs, NH, KVH, D, kv_cache.block_size, maxb, dt, 0, ws.data_ptr(),
+                    ws.numel(), stream))
+            else:
+                N.check(lib.ti_paged_prefill_attention(
+                    attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
+                    bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.start_pos.data_ptr(),
+                    pb.cu_seqlens.data_ptr(), pb.tile_seq.data_ptr(), pb.tile_q0.data_ptr(),
+                    pb.tile_seq.numel(), NH, KVH, D, kv_cache.block_size, dt, stream))
+            N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
+                                NH * D, T, H, NH * D, hidden.data_ptr(), H, None, None, None, dt,
+                                64, split_o, stream))
+            N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
+                                   W[f"{li}.ln2"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
+            N.check(lib.ti_gemm(N.TI_EPI_SWIGLU, xn.data_ptr(), H, W[f"{li}.gate_up"].data_ptr(),
+                                H, T, 2 * I, H, act.data_ptr(), I, None, None, None, dt,
+                                GATE_UP_TILE, 1, stream))
+            N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
+                                I, T, H, I, hidden.data_ptr(), H, None, None, None, dt, 64,
+                                split_d, stream))
+
+    def _final_norm(self, hidden_rows: torch.Tensor, stream: int) -> torch.Tensor:
+        c = self.config
+        R = hidden_rows.shape[0]
+        xf = self._buf("xf", (R, c.hidden_size), self.dtype)
+        N.check(N.lib().ti_rmsnorm(xf.data_ptr(), hidden_rows.data_ptr(), N.TI_DTYPE_FP32,
+                                   self.weights["norm"].data_ptr(), c.rms_norm_eps, R,
+                                   c.hidden_size, N.dtype_code(self.dtype), stream))
+        return xf
+
+    def lm_head_logits(self, xf: torch.Tensor, stream: int) -> torch.Tensor:
+        c = self.config
+        R = xf.shape[0]
+        logits = torch.empty(R, c.vocab_size, dtype=self.dtype, device=self.device)
+        N.check(N.lib().ti_gemm(N.TI_EPI_STORE, xf.data_ptr(), c.hidden_size,
+                                self.weights["lm_head"].data_ptr(), c.hidden_size, R,
+                                c.vocab_size, c.hidden_size, logits.data_ptr(), c.vocab_size,
+                                None, None, None, N.dtype_code(self.dtype), LM_TILE, 1, stream))
+        return logits
+
+    def forward_packed(self, pb: PackedBatch, kv_cache, cos, sin, *, rows: str = "all",
+                       num_layers: int | None = None, return_hidden: bool = False):
+        """Run the layers over a packed batch; returns logits of every token (rows='all') or of
+        each sequence's last token (rows='last')."""
+        c = self.config
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        hidden = torch.empty(pb.num_tokens, c.hidden_size, dtype=torch.float32, device=self.device)
+        N.check(N.lib().ti_embedding(hidden.data_ptr(), self.weights["embed"].data_ptr(),
+                                     pb.input_ids.data_ptr(), pb.num_tokens, c.hidden_size,
+                                     c.vocab_size, N.dtype_code(self.dtype), stream))
+        self._layers(pb, kv_cache, cos, sin, hidden, stream, num_layers)
+        if return_hidden:
+            return hidden
+        h = hidden if rows == "all" else hidden.index_select(0, pb.last_rows).contiguous()
+        return self.lm_head_logits(self._final_norm(h, stream), stream)
+
+    def __call__(self, input_ids, batch_indices, kv_cache, cos_cache, sin_cache):
+        return self.forward(input_ids, batch_indices, kv_cache, cos_cache, sin_cache)
+
+    def forward(self, input_ids: torch.Tensor, batch_indices: torch.Tensor, kv_cache,
+                cos_cache: torch.Tensor, sin_cache: torch.Tensor) -> torch.Tensor:
+        """Reference-compatible forward (models/qwen_25.py:239-251): logits [B, S, V] for every
+        position; KV written for every layer; ``kv_cache.seq_len`` left unchanged."""
+        kv_cache.sync_from_device()   # callers may have advanced seq_len on the device
+        B, S = input_ids.shape
+        slots = [int(x) for x in batch_indices.reshape(-1).tolist()]
+        ids = input_ids.reshape(-1).to(torch.int32).cpu().numpy()
+        pb = self.plan(kv_cache, slots, [S] * B, ids)
+        cos = cos_cache.to(self.device, torch.float32).contiguous()
+        sin = sin_cache.to(self.device, torch.float32).contiguous()
+        logits = self.forward_packed(pb, kv_cache, cos, sin, rows="all")
+        return logits.view(B, S, -1)
+
+    # ---- RoPE tables -------------------------------------------------------------------------
+    def rope_tables(self, max_positions: int):
+        """cos/sin [max_positions, D/2] float32, built like engine/scheduler.py:36-48."""
+        D = self.config.head_dim
+        inv_freq = 1.0 / (self.config.rope_theta ** (
+            torch.arange(0, D, 2, device=self.device).float() / D))
+        t = torch.arange(max_positions, device=self.device, dtype=torch.float32)
+        freqs = torch.einsum("i,j->ij", t, inv_freq)
+        return freqs.cos().contiguous(), freqs.sin().contiguous()
