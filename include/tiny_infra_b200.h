@@ -61,11 +61,13 @@ int ti_device_status(unsigned int* bits, int clear, void* stream);
  * Same semantics as the reference kernel: ctx 0 leaves the row untouched, reading stops at the
  * first negative entry, and a sequence with no readable token gets NaN.  Block ids >=
  * num_blocks are treated like -1.  head_dim 64 or 128, block_size 16, at most 16 query heads
- * per kv head.  `partition_blocks` (1..16, 0 = 16) KV blocks per split-K partition; when
- * max_blocks_per_seq > partition_blocks a workspace of ti_paged_attention_workspace_bytes()
- * bytes is required.  Its first 64 KiB hold split-K arrival counters (one per sequence and kv
- * head, batch * num_kv_heads <= 16384): they must be zero before the first call and every call
- * leaves them zero; the rest is scratch.  Calls that share a workspace must not overlap. */
+ * per kv head.  head_dim 64 with batch <= 4096 runs a persistent kernel that splits the whole
+ * batch's KV blocks evenly over the GPU's warps (split-K only where a sequence is cut);
+ * otherwise one CTA per `partition_blocks` (1..16, 0 = 16) KV blocks.  A workspace of
+ * ti_paged_attention_workspace_bytes() bytes is required.  Its first 64 KiB hold split-K
+ * arrival counters (one per sequence and kv head, batch * num_kv_heads <= 16384): they must be
+ * zero before the first call and every call leaves them zero; the rest is scratch.  Calls
+ * that share a workspace must not overlap on the GPU. */
 size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, int num_kv_heads,
                                           int head_dim, int max_blocks_per_seq,
                                           int partition_blocks);

@@ -349,24 +349,26 @@ decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ 
 struct MapKey {
   const void* ptr;
   int64_t rows;
-  int hd, dtype;
+  int hd, dtype, box_rows;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && hd == o.hd && dtype == o.dtype;
+    return ptr == o.ptr && rows == o.rows && hd == o.hd && dtype == o.dtype &&
+           box_rows == o.box_rows;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<const void*>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) * 31u) ^
-           (size_t)(k.hd * 7 + k.dtype);
+           (size_t)(k.hd * 7 + k.dtype + k.box_rows * 131);
   }
 };
 
 // Tensor map over one layer's pool viewed as a 2-D [rows = NB*KVH*16, HD] matrix, box 64 x 16,
 // SWIZZLE_128B.  Cached per (pointer, rows, HD, dtype).
-static int kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int hd, int dtype) {
+static int kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int hd, int dtype,
+                         int box_rows = kBlock) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  MapKey key{base, rows, hd, dtype};
+  MapKey key{base, rows, hd, dtype, box_rows};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -374,7 +376,7 @@ static int kv_tensor_map(CUtensorMap* out, const void* base, int64_t rows, int h
   }
   cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)kBlock};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   int rc = encode_tensor_map_2d(out,
                                 dtype == TI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -411,16 +413,491 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
   return TI_OK;
 }
 
+
+// ==========================================================================================
+// v2: persistent, load-balanced streaming kernel (head_dim 64, batch <= 4096)
+//
+// Work unit: one sequence and HP consecutive kv heads.  With HP = 2 (GQA groups of <= 8 query
+// heads, an even number of kv heads) the 16 MMA rows hold the query heads of both kv heads --
+// rows 0..G-1 for the first, 8..8+G-1 for the second -- so no MMA row is padding for
+// Qwen2.5-0.5B's 7-head groups, and one 32-row TMA box fetches both heads' K (4 KB contiguous)
+// and one fetches their V.  HP = 1 is the general layout (16 rows, G <= 16).
+//
+// All KV blocks of all units form one stream (unit-major, blocks in logical order); every warp
+// of the grid gets an equal contiguous chunk of it.  A chunk covers a few "pieces" (the part
+// of one unit inside the chunk); a unit cut by chunk boundaries is split-K merged by the last
+// of its pieces to finish (atomic arrival counter, no waiting), other units write their output
+// directly.  Each CTA rebuilds the block offsets with a prefix scan over sequences.
+//
+// Per warp: a STAGES-deep TMA ring that lane 0 keeps full across piece boundaries while the
+// warp computes, piece metadata in a 4-entry ring and a 32-entry window of block ids.
+// ==========================================================================================
+constexpr int kV2Meta = 4;
+constexpr int kV2MaxBatch = 4096;
+constexpr int kV2MaxPieces = 17;                           // pieces per unit (bounded by the chunk)
+
+struct PieceV2 {
+  int row, unit, j0, len, ctx, piece, pieces;
+  int nvalid;      // blocks to read (len until a negative entry is met)
+  int issued;      // blocks issued so far
+  int scanned;     // issue cursor is done with this piece (nvalid final)
+  int stop;        // met a negative entry
+};
+
+template <int HP>
+struct CfgV2 {
+  static constexpr int kWarps = HP == 2 ? 12 : 6;
+  static constexpr int kStages = HP == 2 ? 2 : 8;
+  static constexpr int kTile = HP * kBlock * 64 * 2;          // K (or V) of one block, HP heads
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kRing = kWarps * kStages * kStage;     // 192 KB
+  static constexpr int kBars = kWarps * kStages * 8;
+  static constexpr int kMeta = kWarps * kV2Meta * (int)sizeof(PieceV2);
+  static constexpr int kWin = kWarps * 32 * 4;
+  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
+  static constexpr int kTotal = kRing + kBars + kMeta + kWin + kOffBytes + 1024;
+  static_assert(kTotal <= 227 * 1024, "v2 shared memory");
+};
+
+// chunk of the block stream per warp: balanced, but at least max_blocks / 16 (so that a unit is
+// cut into at most kV2MaxPieces pieces, which bounds the split-K workspace) and at least 4
+__host__ __device__ inline int v2_chunk(int64_t total_blocks, int warps, int max_blocks) {
+  int64_t c = (total_blocks + warps - 1) / warps;
+  const int lo = max(4, (max_blocks + 15) / 16);
+  return (int)(c < lo ? lo : c);
+}
+
+// One KV block (16 tokens) of the unit's HP kv heads: S = QK^T, online softmax, O += PV for the
+// 16-row tile.  kb / vb: shared addresses of the SWIZZLE_128B K and V tiles (HP * 16 rows).
+template <typename T, int HP>
+__device__ __forceinline__ void v2_block(uint32_t kb, uint32_t vb, uint8_t* vt, int valid,
+                                         int lane, const uint32_t (&qa)[4][4], float scale_log2,
+                                         float (&m_r)[2], float (&l_r)[2], float (&o)[8][4]) {
+  const int t4 = lane & 3;
+  if (valid < kBlock) {
+    // zero the V rows past the context so that 0 * (stale value) cannot produce NaN
+    for (int i = lane; i < HP * (kBlock - valid) * 8; i += 32) {
+      const int h = i / ((kBlock - valid) * 8), r = i % ((kBlock - valid) * 8);
+      *reinterpret_cast<uint4*>(vt + swz128(h * kBlock + valid + r / 8, r & 7)) =
+          make_uint4(0, 0, 0, 0);
+    }
+    __syncwarp();
+  }
+  // scores: rows g from kv sub-head 0, rows g+8 from kv sub-head HP-1
+  float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  float sd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const int mi = lane >> 3;
+    const int tok = ((mi & 2) ? 8 : 0) + (lane & 7);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(kb + swz128(tok, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+    Mma<T>::run(sc[0], qa[ks], b0, b1);
+    Mma<T>::run(sc[1], qa[ks], b2, b3);
+    if constexpr (HP == 2) {
+      ldsm_x4(kb + swz128(kBlock + tok, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+      Mma<T>::run(sd[0], qa[ks], b0, b1);
+      Mma<T>::run(sd[1], qa[ks], b2, b3);
+    }
+  }
+  if constexpr (HP == 2) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      sc[nt][2] = sd[nt][2];
+      sc[nt][3] = sd[nt][3];
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tk = nt * 8 + 2 * t4 + (e & 1);
+      sc[nt][e] = (tk < valid) ? sc[nt][e] * scale_log2 : -INFINITY;
+    }
+  float mx[2];
+  mx[0] = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+  mx[1] = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+  }
+  float alpha[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float mn = fmaxf(m_r[h], mx[h]);
+    alpha[h] = fast_exp2(m_r[h] - mn);
+    m_r[h] = mn;
+  }
+  float pr[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[nt][e] = fast_exp2(sc[nt][e] - m_r[e >> 1]);
+  l_r[0] = l_r[0] * alpha[0] + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+  l_r[1] = l_r[1] * alpha[1] + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
+    o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
+  }
+  uint32_t pa[4], pl[4];
+  split_p<T>(pr, pa, pl);
+  // A fragments: registers 0/2 hold rows g, 1/3 rows g+8.  With HP == 2 rows g multiply the
+  // first kv head's V and rows g+8 the second's, so each product uses half of the fragment.
+  const uint32_t mask_lo[4] = {0xffffffffu, 0u, 0xffffffffu, 0u};
+#pragma unroll
+  for (int sub = 0; sub < HP; ++sub) {
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t keep = HP == 1 ? 0xffffffffu : (sub == 0 ? mask_lo[i] : ~mask_lo[i]);
+      ah[i] = pa[i] & keep;
+      al[i] = pl[i] & keep;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; nt += 2) {
+      const int mi = lane >> 3;
+      const int tok = sub * kBlock + ((mi & 1) ? 8 : 0) + (lane & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vb + swz128(tok, nt + (mi >> 1)), b0, b1, b2, b3);
+      Mma<T>::run(o[nt], ah, b0, b1);
+      Mma<T>::run(o[nt + 1], ah, b2, b3);
+      if constexpr (kSplitP<T>) {
+        Mma<T>::run(o[nt], al, b0, b1);
+        Mma<T>::run(o[nt + 1], al, b2, b3);
+      }
+    }
+  }
+}
+
+// Query heads of the 16 MMA rows: row r < 8 -> first kv head of the unit, r >= 8 -> the last
+// (HP == 2), or r -> r (HP == 1).  Returns -1 for a padding row.
+template <int HP>
+__device__ __forceinline__ int v2_row_head(int unit, int r, int G) {
+  if constexpr (HP == 2) {
+    const int sub = r >> 3, i = r & 7;
+    return i < G ? (unit * 2 + sub) * G + i : -1;
+  } else {
+    return r < G ? unit * G + r : -1;
+  }
+}
+
+// Merge the published pieces of one unit and write its HP*G output rows.  Lane l owns columns
+// 2l, 2l+1 of every head; loads of the pieces are independent and issued together.
+template <typename T>
+__device__ __forceinline__ void v2_merge(const Params& p, int row, int unit, int nheads,
+                                         int pieces, int lane, T* outp) {
+  const int h0 = unit * nheads;
+  const int units = p.num_heads / nheads;
+  const int64_t pair = (int64_t)row * units + unit;
+  const int32_t* stops = p.ws_stop + pair * p.max_parts;
+  int use = pieces;
+  {
+    const int st = lane < pieces ? __ldcg(stops + lane) : 0;   // pieces <= 17 < 32
+    const unsigned b = __ballot_sync(0xffffffffu, st != 0);
+    if (b) use = __ffs(b);                                     // up to and including the first stop
+  }
+  for (int h = 0; h < nheads; ++h) {
+    const int64_t base = ((int64_t)row * p.num_heads + h0 + h) * p.max_parts;
+    const float2 ml = lane < use ? __ldcg(reinterpret_cast<const float2*>(p.ws_ml) + base + lane)
+                                 : make_float2(-INFINITY, 0.f);
+    const float M = warp_max(ml.x);
+    const float f = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - M);
+    const float L = warp_sum(ml.y * f);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int q = 0; q < use; ++q) {
+      const float fq = __shfl_sync(0xffffffffu, f, q);
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(p.ws_o + (base + q) * 64) + lane);
+      acc.x += fq * v.x;
+      acc.y += fq * v.y;
+    }
+    *reinterpret_cast<uint32_t*>(outp + (h0 + h) * 64 + 2 * lane) =
+        Elem<T>::pack2(acc.x / L, acc.y / L);                   // L == 0 -> NaN (attention.cu:150)
+  }
+}
+
+template <typename T, int HP>
+__global__ void __launch_bounds__(CfgV2<HP>::kWarps * 32, 1)
+decode_kernel_v2(const __grid_constant__ CUtensorMap kmap,
+                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  using C = CfgV2<HP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t bar_all = smem_u32(smem + C::kRing);
+  PieceV2* meta_all = reinterpret_cast<PieceV2*>(smem + C::kRing + C::kBars);
+  int* win_all = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kMeta);
+  int* s_off = win_all + C::kWarps * 32;      // s_off[r] = KVU * blocks of rows before r
+  __shared__ int s_wsum[C::kWarps];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVH = p.num_kv_heads;
+  const int KVU = KVH / HP;                   // units per sequence
+  auto nblk_of = [&](int r) {
+    const int ctx = p.context_lens[r];
+    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
+  };
+
+  // ---- exclusive prefix sum of KVU * blocks per sequence into s_off[0..batch]
+  const int per = (batch + blockDim.x - 1) / blockDim.x;
+  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
+  int local = 0;
+  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  if (tid < C::kWarps * C::kStages) {
+    mbar_init(bar_all + 8 * tid, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_wsum[w];
+  for (int r = r0; r < r1; ++r) {
+    s_off[r] = run;
+    run += KVU * nblk_of(r);
+  }
+  if (tid == 0) {
+    int tot = 0;
+    for (int w = 0; w < C::kWarps; ++w) tot += s_wsum[w];
+    s_off[batch] = tot;
+  }
+  __syncthreads();
+  const int total = s_off[batch];
+  const int W = gridDim.x * C::kWarps;
+  const int chunk = v2_chunk(total, W, p.max_blocks);
+  const int wid = blockIdx.x * C::kWarps + warp;
+  const int begin = wid * chunk;
+  if (begin >= total) return;
+  const int end = min(total, begin + chunk);
+
+  uint8_t* ring = smem + warp * C::kStages * C::kStage;
+  const uint32_t bar = bar_all + warp * C::kStages * 8;
+  PieceV2* meta = meta_all + warp * kV2Meta;
+  int* win = win_all + warp * 32;
+  const int G = p.group;
+  const int NHU = HP * G;                     // query heads per unit
+  const int g = lane >> 2, t4 = lane & 3;
+  const uint64_t pol = l2_policy_evict_first();
+
+  uint32_t phase = 0;                 // expected parity of each stage's barrier
+  int issued = 0, consumed = 0;       // blocks of this warp
+  int ik = 0, ij = 0, started = 0;    // issue cursor: piece, block within piece; pieces started
+  int ipos = begin;                   // stream position of piece ik's first block
+  int win_lo = 0, win_hi = 0;         // block-id window [win_lo, win_hi) of piece ik (unit-relative)
+  bool idone = false;
+  int ck = 0, cj = 0;                 // consume cursor
+  bool open = false;                  // softmax state belongs to piece ck
+  uint32_t qa[4][4];
+  float m_r[2], l_r[2], o[8][4];
+
+  while (true) {
+    // ---- issue: keep up to kStages blocks in flight, at most kV2Meta pieces ahead
+    __syncwarp();
+    while (!idone) {
+      if (ik == started) {
+        if (ik - ck >= kV2Meta) break;
+        int lo = 0, hi = batch;                  // largest row with s_off[row] <= ipos
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (s_off[mid] <= ipos) lo = mid; else hi = mid;
+        }
+        const int row = lo;
+        const int nb = (s_off[row + 1] - s_off[row]) / KVU;
+        const int rel = ipos - s_off[row];
+        const int unit = rel / nb, j0 = rel - unit * nb;
+        const int pstart = s_off[row] + unit * nb;
+        const int len = min(nb - j0, end - ipos);
+        if (lane == 0) {
+          PieceV2& m = meta[ik % kV2Meta];
+          m.row = row; m.unit = unit; m.j0 = j0; m.len = len; m.ctx = p.context_lens[row];
+          m.piece = ipos / chunk - pstart / chunk;
+          m.pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
+          m.nvalid = len; m.issued = 0; m.scanned = 0; m.stop = 0;
+        }
+        __syncwarp();
+        ++started;
+        win_lo = win_hi = j0;
+      }
+      PieceV2& m = meta[ik % kV2Meta];
+      if (ij < m.nvalid) {
+        if (issued - consumed >= C::kStages) break;
+        const int j = m.j0 + ij;
+        if (j >= win_hi) {                       // next 32 block ids of this piece
+          const int lim = m.j0 + m.len;
+          const int brow = p.row_index ? p.row_index[m.row] : m.row;
+          const int jj = j + lane;
+          const int phys = jj < lim ? p.block_tables[(int64_t)brow * p.bt_stride + jj] : 0;
+          const bool bad = jj < lim && (phys < 0 || (int64_t)phys >= p.num_blocks);
+          const unsigned neg = __ballot_sync(0xffffffffu, bad);
+          win[lane] = phys;
+          if (neg && lane == 0) {                // stop at the first negative (attention.cu:90)
+            m.nvalid = (j - m.j0) + __ffs(neg) - 1;
+            m.stop = 1;
+          }
+          win_lo = j;
+          win_hi = j + 32;
+          __syncwarp();
+          if (ij >= m.nvalid) continue;
+        }
+        if (lane == 0) {
+          const int st = issued % C::kStages;
+          const uint32_t dst = smem_u32(ring + st * C::kStage);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive_expect_tx(bar + 8 * st, C::kStage);
+          const int y = (win[j - win_lo] * KVH + m.unit * HP) * kBlock;
+          tma_load_2d_hint(dst, &kmap, bar + 8 * st, 0, y, pol);
+          tma_load_2d_hint(dst + C::kTile, &vmap, bar + 8 * st, 0, y, pol);
+          m.issued = ij + 1;
+        }
+        __syncwarp();
+        ++ij;
+        ++issued;
+      } else {
+        if (lane == 0) m.scanned = 1;
+        __syncwarp();
+        ipos += m.len;
+        ++ik;
+        ij = 0;
+        if (ipos >= end) idone = true;
+      }
+    }
+    if (ck == started && idone) break;
+    const PieceV2& m = meta[ck % kV2Meta];
+    if (!open) {                      // start a piece: its query rows, fresh softmax state
+      const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)m.row * p.q_stride;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int head = v2_row_head<HP>(m.unit, g + ((r & 1) ? 8 : 0), G);
+          const int col = ks * 16 + 2 * t4 + ((r & 2) ? 8 : 0);
+          qa[ks][r] = head >= 0 ? *reinterpret_cast<const uint32_t*>(qb + head * 64 + col) : 0u;
+        }
+      m_r[0] = m_r[1] = -INFINITY;
+      l_r[0] = l_r[1] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      open = true;
+    }
+    if (cj < m.issued) {
+      const int st = consumed % C::kStages;
+      if (!mbar_wait(bar + 8 * st, (phase >> st) & 1u, TI_DEVERR_ATTN_WAIT)) return;
+      phase ^= 1u << st;
+      uint8_t* kt = ring + st * C::kStage;
+      const int valid = min(kBlock, m.ctx - (m.j0 + cj) * kBlock);
+      v2_block<T, HP>(smem_u32(kt), smem_u32(kt + C::kTile), kt + C::kTile, valid, lane, qa,
+                      p.scale_log2, m_r, l_r, o);
+      ++cj;
+      ++consumed;
+      continue;
+    }
+    if (!m.scanned) continue;         // more blocks of this piece still to issue
+    // ---- piece finished
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 1);
+      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 2);
+    }
+    const int row = m.row;
+    const int hA = v2_row_head<HP>(m.unit, g, G), hB = v2_row_head<HP>(m.unit, g + 8, G);
+    T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
+    if (m.pieces == 1) {
+      const float inv0 = 1.f / l_r[0], inv1 = 1.f / l_r[1];   // l == 0 -> NaN (attention.cu:150)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int col = i * 8 + 2 * t4;
+        if (hA >= 0)
+          *reinterpret_cast<uint32_t*>(outp + hA * 64 + col) =
+              Elem<T>::pack2(o[i][0] * inv0, o[i][1] * inv0);
+        if (hB >= 0)
+          *reinterpret_cast<uint32_t*>(outp + hB * 64 + col) =
+              Elem<T>::pack2(o[i][2] * inv1, o[i][3] * inv1);
+      }
+    } else {
+      const int64_t rb = (int64_t)row * p.num_heads;
+      const int64_t s0 = (rb + (hA >= 0 ? hA : 0)) * p.max_parts + m.piece;
+      const int64_t s1 = (rb + (hB >= 0 ? hB : 0)) * p.max_parts + m.piece;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int col = i * 8 + 2 * t4;
+        if (hA >= 0) *reinterpret_cast<float2*>(p.ws_o + s0 * 64 + col) = make_float2(o[i][0], o[i][1]);
+        if (hB >= 0) *reinterpret_cast<float2*>(p.ws_o + s1 * 64 + col) = make_float2(o[i][2], o[i][3]);
+      }
+      if (t4 == 0) {
+        if (hA >= 0) *reinterpret_cast<float2*>(p.ws_ml + s0 * 2) = make_float2(m_r[0], l_r[0]);
+        if (hB >= 0) *reinterpret_cast<float2*>(p.ws_ml + s1 * 2) = make_float2(m_r[1], l_r[1]);
+      }
+      const int64_t pair = (int64_t)row * KVU + m.unit;
+      if (lane == 0) p.ws_stop[pair * p.max_parts + m.piece] = m.stop;
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.ws_count[pair], 1) == m.pieces - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        v2_merge<T>(p, row, m.unit, NHU, m.pieces, lane, outp);
+        if (lane == 0) p.ws_count[pair] = 0;     // ready for the next launch
+      }
+    }
+    open = false;
+    ++ck;
+    cj = 0;
+  }
+}
+
+template <typename T, int HP>
+static int launch_v2(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
+                     cudaStream_t stream) {
+  using C = CfgV2<HP>;
+  static int set_dev = -1;
+  static int sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v2<T, HP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v2)");
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    set_dev = dev;
+  }
+  decode_kernel_v2<T, HP><<<sms, C::kWarps * 32, C::kTotal, stream>>>(km, vm, p, batch);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v2 launch");
+  return TI_OK;
+}
+
+// Partition size (KV blocks per split-K CTA of the v1 kernel) used when the caller passes 0.
+static int default_partition(int /*max_blocks*/) { return kMaxPart; }
+
+// The v2 kernel serves head_dim 64 and batches up to kV2MaxBatch.
+static bool use_v2(int head_dim, int batch) { return head_dim == 64 && batch <= kV2MaxBatch; }
 }  // namespace attn
 }  // namespace ti
 
 using namespace ti;
 
+// Split-K slots per sequence: the v2 kernel cuts a (sequence, kv head) into at most
+// kV2MaxPieces pieces; the v1 kernel into ceil(max_blocks / partition_blocks) partitions.
+static int64_t attn_parts(int batch, int head_dim, int max_blocks, int partition_blocks) {
+  if (attn::use_v2(head_dim, batch)) return attn::kV2MaxPieces;
+  if (partition_blocks <= 0) partition_blocks = attn::default_partition(max_blocks);
+  return (max_blocks + partition_blocks - 1) / partition_blocks;
+}
+
 extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, int num_kv_heads,
                                                       int head_dim, int max_blocks_per_seq,
                                                       int partition_blocks) {
-  if (partition_blocks <= 0) partition_blocks = attn::kMaxPart;
-  const int64_t parts = (max_blocks_per_seq + partition_blocks - 1) / partition_blocks;
+  const int64_t parts = attn_parts(batch, head_dim, max_blocks_per_seq, partition_blocks);
   const int64_t slots = (int64_t)batch * num_heads * parts;
   size_t bytes = attn::kCounterBytes;                           // arrival counters (kept zero)
   bytes += (size_t)slots * head_dim * 4;                        // ws_o
@@ -451,14 +928,16 @@ extern "C" int ti_paged_attention_decode(
     return set_error(TI_ERR_UNSUPPORTED, "paged attention: dtype must be bf16 or fp16");
   if (max_blocks_per_seq <= 0 || num_blocks <= 0)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: empty pool or block table");
-  if (partition_blocks <= 0) partition_blocks = attn::kMaxPart;
+  if (partition_blocks <= 0) partition_blocks = attn::default_partition(max_blocks_per_seq);
   if (partition_blocks > attn::kMaxPart)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: partition_blocks must be <= 16");
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: pool base must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_seq_stride & 1))
-    return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: q must be 4-byte aligned with an even row stride");
-  const int max_parts = (max_blocks_per_seq + partition_blocks - 1) / partition_blocks;
+  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_seq_stride & 1) ||
+      (reinterpret_cast<uintptr_t>(out) & 3) || (out_seq_stride & 1))
+    return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: q/out must be 4-byte aligned with even row strides");
+  const bool v2 = attn::use_v2(head_dim, batch);
+  const int max_parts = (int)attn_parts(batch, head_dim, max_blocks_per_seq, partition_blocks);
   const size_t need = ti_paged_attention_workspace_bytes(batch, num_heads, num_kv_heads, head_dim,
                                                           max_blocks_per_seq, partition_blocks);
   if (max_parts > 1 && (!workspace || workspace_bytes < need))
@@ -485,12 +964,20 @@ extern "C" int ti_paged_attention_decode(
     p.ws_stop = reinterpret_cast<int32_t*>(w);
   }
   const int64_t rows = num_blocks * num_kv_heads * attn::kBlock;
+  // two kv heads per MMA tile when both GQA groups fit the 16 rows
+  const int hp = (v2 && num_kv_heads % 2 == 0 && p.group <= 8) ? 2 : 1;
   CUtensorMap km, vm;
-  int rc = attn::kv_tensor_map(&km, k_cache, rows, head_dim, dtype);
+  int rc = attn::kv_tensor_map(&km, k_cache, rows, head_dim, dtype, hp * attn::kBlock);
   if (rc) return rc;
-  rc = attn::kv_tensor_map(&vm, v_cache, rows, head_dim, dtype);
+  rc = attn::kv_tensor_map(&vm, v_cache, rows, head_dim, dtype, hp * attn::kBlock);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (v2 && hp == 2)
+    return dtype == TI_DTYPE_BF16 ? attn::launch_v2<__nv_bfloat16, 2>(p, km, vm, batch, s)
+                                  : attn::launch_v2<__half, 2>(p, km, vm, batch, s);
+  if (v2)
+    return dtype == TI_DTYPE_BF16 ? attn::launch_v2<__nv_bfloat16, 1>(p, km, vm, batch, s)
+                                  : attn::launch_v2<__half, 1>(p, km, vm, batch, s);
   if (dtype == TI_DTYPE_BF16)
     return head_dim == 64 ? attn::launch<__nv_bfloat16, 64>(p, km, vm, batch, s)
                           : attn::launch<__nv_bfloat16, 128>(p, km, vm, batch, s);
