@@ -507,13 +507,20 @@ __device__ __forceinline__ void v2_block(uint32_t kb, uint32_t vb, uint8_t* vt, 
       sc[nt][3] = sd[nt][3];
     }
   }
+  if (valid < kBlock) {
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int tk = nt * 8 + 2 * t4 + (e & 1);
-      sc[nt][e] = (tk < valid) ? sc[nt][e] * scale_log2 : -INFINITY;
-    }
+      for (int e = 0; e < 4; ++e) {
+        const int tk = nt * 8 + 2 * t4 + (e & 1);
+        sc[nt][e] = (tk < valid) ? sc[nt][e] * scale_log2 : -INFINITY;
+      }
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] *= scale_log2;
+  }
   float mx[2];
   mx[0] = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
   mx[1] = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
@@ -523,9 +530,11 @@ __device__ __forceinline__ void v2_block(uint32_t kb, uint32_t vb, uint8_t* vt, 
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
   }
   float alpha[2];
+  bool moved = false;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const float mn = fmaxf(m_r[h], mx[h]);
+    moved |= mn != m_r[h];
     alpha[h] = fast_exp2(m_r[h] - mn);
     m_r[h] = mn;
   }
@@ -536,10 +545,12 @@ __device__ __forceinline__ void v2_block(uint32_t kb, uint32_t vb, uint8_t* vt, 
     for (int e = 0; e < 4; ++e) pr[nt][e] = fast_exp2(sc[nt][e] - m_r[e >> 1]);
   l_r[0] = l_r[0] * alpha[0] + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
   l_r[1] = l_r[1] * alpha[1] + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+  if (__any_sync(0xffffffffu, moved)) {       // rescale only when some row's max moved
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
-    o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= alpha[0]; o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1]; o[i][3] *= alpha[1];
+    }
   }
   uint32_t pa[4], pl[4];
   split_p<T>(pr, pa, pl);
@@ -583,8 +594,9 @@ __device__ __forceinline__ int v2_row_head(int unit, int r, int G) {
   }
 }
 
-// Merge the published pieces of one unit and write its HP*G output rows.  Lane l owns columns
-// 2l, 2l+1 of every head; loads of the pieces are independent and issued together.
+// Merge the published pieces of one unit and write its nheads (<= 16) output rows.  Lane l
+// owns head l/2, dims 32*(l%2) .. +31; every load of a lane is independent of the others, so
+// the merge costs a few memory round trips instead of one per head.
 template <typename T>
 __device__ __forceinline__ void v2_merge(const Params& p, int row, int unit, int nheads,
                                          int pieces, int lane, T* outp) {
@@ -598,24 +610,71 @@ __device__ __forceinline__ void v2_merge(const Params& p, int row, int unit, int
     const unsigned b = __ballot_sync(0xffffffffu, st != 0);
     if (b) use = __ffs(b);                                     // up to and including the first stop
   }
-  for (int h = 0; h < nheads; ++h) {
-    const int64_t base = ((int64_t)row * p.num_heads + h0 + h) * p.max_parts;
-    const float2 ml = lane < use ? __ldcg(reinterpret_cast<const float2*>(p.ws_ml) + base + lane)
-                                 : make_float2(-INFINITY, 0.f);
-    const float M = warp_max(ml.x);
-    const float f = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - M);
-    const float L = warp_sum(ml.y * f);
-    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll 4
-    for (int q = 0; q < use; ++q) {
-      const float fq = __shfl_sync(0xffffffffu, f, q);
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(p.ws_o + (base + q) * 64) + lane);
-      acc.x += fq * v.x;
-      acc.y += fq * v.y;
+  for (int hb = 0; hb < nheads; hb += 16) {
+    const int h = hb + (lane >> 1), half = lane & 1;
+    const bool live = h < nheads;
+    const int64_t base = ((int64_t)row * p.num_heads + h0 + (live ? h : 0)) * p.max_parts;
+    float mq[kV2MaxPieces], lq[kV2MaxPieces];
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kV2MaxPieces; ++q) {
+      if (q < use && live) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml) + base + q);
+        mq[q] = ml.x;
+        lq[q] = ml.y;
+      } else {
+        mq[q] = -INFINITY;
+        lq[q] = 0.f;
+      }
+      M = fmaxf(M, mq[q]);
     }
-    *reinterpret_cast<uint32_t*>(outp + (h0 + h) * 64 + 2 * lane) =
-        Elem<T>::pack2(acc.x / L, acc.y / L);                   // L == 0 -> NaN (attention.cu:150)
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    float L = 0.f;
+#pragma unroll
+    for (int q = 0; q < kV2MaxPieces; ++q) {
+      if (q < use && live) {
+        const float f = (mq[q] == -INFINITY) ? 0.f : fast_exp2(mq[q] - M);
+        L += lq[q] * f;
+        const float4* src = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64 + half * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = __ldcg(src + i);
+          acc[4 * i] += f * v.x; acc[4 * i + 1] += f * v.y;
+          acc[4 * i + 2] += f * v.z; acc[4 * i + 3] += f * v.w;
+        }
+      }
+    }
+    if (live) {
+      const float inv = 1.f / L;                               // L == 0 -> NaN (attention.cu:150)
+      T* dst = outp + (int64_t)(h0 + h) * 64 + half * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 u;
+        u.x = Elem<T>::pack2(acc[i] * inv, acc[i + 1] * inv);
+        u.y = Elem<T>::pack2(acc[i + 2] * inv, acc[i + 3] * inv);
+        u.z = Elem<T>::pack2(acc[i + 4] * inv, acc[i + 5] * inv);
+        u.w = Elem<T>::pack2(acc[i + 6] * inv, acc[i + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + i) = u;
+      }
+    }
   }
+}
+
+// Split-K arrival: every lane's partial-result stores are ordered before lane 0's acq_rel
+// increment (warp barrier + cumulative release); the last arriver acquires the others'.
+__device__ __forceinline__ bool arrive_last(int32_t* counter, int expected, int lane) {
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    int prev;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+    last = prev == expected - 1;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  __syncwarp();
+  return last != 0;
 }
 
 template <typename T, int HP>
@@ -853,6 +912,698 @@ decode_kernel_v2(const __grid_constant__ CUtensorMap kmap,
   }
 }
 
+// ==========================================================================================
+// v3: persistent, load-balanced, warp-specialised kernel (head_dim 64)
+//
+// Same work split as v2 (the whole batch's KV blocks as one stream, an equal chunk per compute
+// warp, split-K only where a unit is cut), but each CTA has one producer warp and kV3Consumers
+// compute warps.  In the prologue the CTA resolves every position of its range of the stream
+// to a pool block id and a valid-token count (shared memory, no global metadata loads after
+// that); the producer then keeps every consumer's 2-stage ring full with TMA loads, and the
+// consumers only wait, compute and finish pieces.  Both walk the same position sequence
+// (skipping the rest of a unit after a negative block-table entry), so no per-block
+// descriptors are exchanged.
+// ==========================================================================================
+constexpr int kV3Consumers = 8;
+constexpr int kV3Stages = 3;
+constexpr int kV3IdCap = 2048;                             // stream positions per CTA
+
+template <int HP>
+struct CfgV3 {
+  static constexpr int kTile = HP * kBlock * 64 * 2;
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kRing = kV3Consumers * kV3Stages * kStage;        // 128 KB with HP = 2
+  static constexpr int kBars = 2 * kV3Consumers * kV3Stages * 8;
+  static constexpr int kIds = kV3IdCap * 4;
+  static constexpr int kVtok = kV3IdCap;
+  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
+  static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
+  static_assert(kTotal <= 227 * 1024, "v3 shared memory");
+};
+
+// Sequence of stream positions a consumer handles: [pos, end), skipping the remainder of a unit
+// once a position's block id is negative.  Shared by producer and consumer.
+struct V3Walk {
+  int pos, end;
+  __device__ __forceinline__ int unit_end(const int* s_off, int batch, int kvu, int p) const {
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= p) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / kvu;
+    const int unit = (p - s_off[lo]) / nb;
+    return s_off[lo] + (unit + 1) * nb;
+  }
+};
+
+// One KV block of ONE kv head with the tokens as the MMA M dimension and the (<= 8) query heads
+// of its GQA group as N: S^T[16 tokens x 8 heads] = K . Q^T (4 MMAs over head_dim 64), online
+// softmax per head (column), O^T[64 dims x 8 heads] += V^T . P^T (4 MMAs; with bf16 P split into
+// hi + lo, 8).  No padding rows: 7 of the 8 columns carry a query head for Qwen2.5-0.5B.
+//   kb / vb   shared addresses of the 16 x 64 K and V tiles (SWIZZLE_128B rows)
+//   qb[ks]    B fragments of Q^T for the four 16-wide head_dim steps
+//   m, l      running max / sum of heads 2*t4, 2*t4+1 (this lane's two columns)
+//   o[mt]     C fragments of O^T for dims 16*mt .. 16*mt+15
+template <typename T>
+__device__ __forceinline__ void swapped_block(uint32_t kb, uint32_t vb, uint8_t* vt, int valid,
+                                              int lane, const uint32_t (&qb)[4][2],
+                                              float scale_log2, float (&m)[2], float (&l)[2],
+                                              float (&o)[4][4]) {
+  const int g = lane >> 2, t4 = lane & 3;
+  if (valid < kBlock) {
+    // zero the V rows past the context so that 0 * (stale value) cannot produce NaN
+    for (int i = lane; i < (kBlock - valid) * 8; i += 32)
+      *reinterpret_cast<uint4*>(vt + swz128(valid + i / 8, i & 7)) = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+  }
+  // ---- S^T = K Q^T : rows = tokens g, g+8; columns = heads 2t4, 2t4+1
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int mi = lane >> 3;
+    const int tok = ((mi & 1) ? 8 : 0) + (lane & 7);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(kb + swz128(tok, ks * 2 + (mi >> 1)), a[0], a[1], a[2], a[3]);
+      Mma<T>::run(s, a, qb[ks][0], qb[ks][1]);
+    }
+  }
+  if (valid < kBlock) {
+    s[0] = g < valid ? s[0] * scale_log2 : -INFINITY;
+    s[1] = g < valid ? s[1] * scale_log2 : -INFINITY;
+    s[2] = g + 8 < valid ? s[2] * scale_log2 : -INFINITY;
+    s[3] = g + 8 < valid ? s[3] * scale_log2 : -INFINITY;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] *= scale_log2;
+  }
+  // ---- online softmax per column (head): reduce over the 16 tokens = lanes sharing t4
+  float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+  const bool moved = (mn0 != m[0]) | (mn1 != m[1]);
+  const float al0 = fast_exp2(m[0] - mn0), al1 = fast_exp2(m[1] - mn1);
+  m[0] = mn0;
+  m[1] = mn1;
+  const float p0 = fast_exp2(s[0] - mn0), p1 = fast_exp2(s[1] - mn1);
+  const float p2 = fast_exp2(s[2] - mn0), p3 = fast_exp2(s[3] - mn1);
+  l[0] = l[0] * al0 + p0 + p2;           // per-lane partial over its tokens; reduced at the end
+  l[1] = l[1] * al1 + p1 + p3;
+  if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      o[mt][0] *= al0; o[mt][1] *= al1;
+      o[mt][2] *= al0; o[mt][3] *= al1;
+    }
+  }
+  // ---- P^T from C layout (token rows, head columns) to the B layout of V^T P^T:
+  // lane (g, t4) needs P^T[2t4][g], P^T[2t4+1][g] (b0) and P^T[2t4+8][g], P^T[2t4+9][g] (b1),
+  // held by lanes 8t4 + g/2 and 8t4 + 4 + g/2, in the half of their word chosen by g % 2.
+  const uint32_t x01 = Elem<T>::pack2(p0, p1), x23 = Elem<T>::pack2(p2, p3);
+  const int src0 = 8 * t4 + (g >> 1), src1 = src0 + 4;
+  const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
+  uint32_t bh[2], bl[2] = {0u, 0u};
+  bh[0] = __byte_perm(__shfl_sync(0xffffffffu, x01, src0), __shfl_sync(0xffffffffu, x01, src1), sel);
+  bh[1] = __byte_perm(__shfl_sync(0xffffffffu, x23, src0), __shfl_sync(0xffffffffu, x23, src1), sel);
+  if constexpr (kSplitP<T>) {
+    const float2 h01 = Elem<T>::unpack2(x01), h23 = Elem<T>::unpack2(x23);
+    const uint32_t y01 = Elem<T>::pack2(p0 - h01.x, p1 - h01.y);
+    const uint32_t y23 = Elem<T>::pack2(p2 - h23.x, p3 - h23.y);
+    bl[0] = __byte_perm(__shfl_sync(0xffffffffu, y01, src0), __shfl_sync(0xffffffffu, y01, src1), sel);
+    bl[1] = __byte_perm(__shfl_sync(0xffffffffu, y23, src0), __shfl_sync(0xffffffffu, y23, src1), sel);
+  }
+  // ---- O^T += V^T P^T : A = V^T (rows = dims, k = tokens) via ldmatrix.trans of the V tile
+  {
+    const int mi = lane >> 3;
+    const int tok = ((mi >> 1) ? 8 : 0) + (lane & 7);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      uint32_t a[4];
+      ldsm_x4_t(vb + swz128(tok, mt * 2 + (mi & 1)), a[0], a[1], a[2], a[3]);
+      Mma<T>::run(o[mt], a, bh[0], bh[1]);
+      if constexpr (kSplitP<T>) Mma<T>::run(o[mt], a, bl[0], bl[1]);
+    }
+  }
+}
+
+template <typename T, int HP>
+__global__ void __launch_bounds__((kV3Consumers + 1) * 32, 1)
+decode_kernel_v3(const __grid_constant__ CUtensorMap kmap,
+                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  using C = CfgV3<HP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t full_all = smem_u32(smem + C::kRing);
+  const uint32_t empty_all = full_all + kV3Consumers * kV3Stages * 8;
+  int* ids = reinterpret_cast<int*>(smem + C::kRing + C::kBars);
+  uint8_t* vtok = smem + C::kRing + C::kBars + C::kIds;
+  int* s_off = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kIds + C::kVtok);
+  constexpr int kThreads = (kV3Consumers + 1) * 32;
+  __shared__ int s_wsum[kV3Consumers + 1];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVH = p.num_kv_heads;
+  const int KVU = KVH / HP;
+  auto nblk_of = [&](int r) {
+    const int ctx = p.context_lens[r];
+    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
+  };
+
+  // ---- prefix sum of KVU * blocks per sequence
+  const int per = (batch + kThreads - 1) / kThreads;
+  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
+  int local = 0;
+  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  if (tid < 2 * kV3Consumers * kV3Stages) {
+    mbar_init(full_all + 8 * tid, 1);          // full and empty barriers are contiguous
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_wsum[w];
+  for (int r = r0; r < r1; ++r) {
+    s_off[r] = run;
+    run += KVU * nblk_of(r);
+  }
+  if (tid == 0) {
+    int tot = 0;
+    for (int w = 0; w <= kV3Consumers; ++w) tot += s_wsum[w];
+    s_off[batch] = tot;
+  }
+  __syncthreads();
+  const int total = s_off[batch];
+  const int W = gridDim.x * kV3Consumers;
+  const int chunk = v2_chunk(total, W, p.max_blocks);
+  const int cb = blockIdx.x * kV3Consumers * chunk;
+  if (cb >= total) return;
+  const int ce = min(total, cb + kV3Consumers * chunk);
+
+  // ---- resolve the CTA's positions: block id (-1 = stop) and valid tokens
+  for (int q = tid; q < ce - cb; q += kThreads) {
+    const int pos = cb + q;
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
+    const int rel = pos - s_off[lo];
+    const int unit = rel / nb, j = rel - unit * nb;
+    const int brow = p.row_index ? p.row_index[lo] : lo;
+    const int phys = p.block_tables[(int64_t)brow * p.bt_stride + j];
+    const bool bad = phys < 0 || (int64_t)phys >= p.num_blocks;
+    // the TMA row coordinate of the unit's first kv head in this block, or -1 (stop)
+    ids[q] = bad ? -1 : (phys * KVH + unit * HP) * kBlock;
+    vtok[q] = (uint8_t)min(kBlock, p.context_lens[lo] - j * kBlock);
+  }
+  __syncthreads();
+
+  if (warp == kV3Consumers) {
+    // ================= producer =================
+    if (lane != 0) return;
+    const uint64_t pol = l2_policy_evict_first();
+    int pos[kV3Consumers], endp[kV3Consumers], cnt[kV3Consumers];
+    uint32_t ephase = 0;
+#pragma unroll
+    for (int c = 0; c < kV3Consumers; ++c) {
+      pos[c] = min(ce, cb + c * chunk);
+      endp[c] = min(ce, pos[c] + chunk);
+      cnt[c] = 0;
+    }
+    V3Walk wk{0, 0};
+    const long long t0 = clock64();
+    while (true) {
+      bool any = false, progress = false;
+#pragma unroll
+      for (int c = 0; c < kV3Consumers; ++c) {
+        // skip positions after a stop, then issue while the ring has room
+        while (pos[c] < endp[c] && ids[pos[c] - cb] < 0) {
+          // the stop position itself is not read; neither is the rest of its unit
+          pos[c] = min(endp[c], wk.unit_end(s_off, batch, KVU, pos[c]));
+        }
+        if (pos[c] >= endp[c]) continue;
+        any = true;
+        // fill every free stage of this consumer
+        while (pos[c] < endp[c]) {
+          const int y = ids[pos[c] - cb];
+          if (y < 0) break;                       // a stop: skipped on the next pass
+          const int st = cnt[c] % kV3Stages;
+          const int slot = c * kV3Stages + st;
+          if (cnt[c] >= kV3Stages) {
+            if (!mbar_test_wait(empty_all + 8 * slot, (ephase >> slot) & 1u)) break;
+            ephase ^= 1u << slot;
+          }
+          const uint32_t dst = smem_u32(smem + slot * C::kStage);
+          // the consumer's generic-proxy reads / zero-fill of this stage precede the TMA write
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive_expect_tx(full_all + 8 * slot, C::kStage);
+          tma_load_2d_hint(dst, &kmap, full_all + 8 * slot, 0, y, pol);
+          tma_load_2d_hint(dst + C::kTile, &vmap, full_all + 8 * slot, 0, y, pol);
+          ++cnt[c];
+          ++pos[c];
+          progress = true;
+        }
+      }
+      if (!any) break;
+      if (!progress) {
+        if (clock64() - t0 > kWaitCycles) { raise_device_error(TI_DEVERR_ATTN_WAIT); break; }
+        __nanosleep(64);
+      }
+    }
+    return;
+  }
+
+  // ================= consumers =================
+  const int c = warp;
+  int pos = min(ce, cb + c * chunk);
+  const int end = min(ce, pos + chunk);
+  if (pos >= end) return;
+  const int G = p.group;                       // <= 8: the MMA N dimension
+  const int NHU = HP * G;
+  const int g = lane >> 2, t4 = lane & 3;
+  uint32_t fphase = 0;
+  int cnt = 0;
+  uint32_t qb[HP][4][2];
+  float m[HP][2], l[HP][2], o[HP][4][4];
+
+  while (pos < end) {
+    // ---- a piece: positions of one unit inside [pos, end)
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int row = lo;
+    const int nb = (s_off[row + 1] - s_off[row]) / KVU;
+    const int unit = (pos - s_off[row]) / nb;
+    const int pstart = s_off[row] + unit * nb;
+    const int pend = min(end, pstart + nb);
+    const int piece = pos / chunk - pstart / chunk;
+    const int pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
+    {
+      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride;
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub) {
+        const T* qh = qrow + (int64_t)((unit * HP + sub) * G + g) * 64;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          qb[sub][ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t4) : 0u;
+          qb[sub][ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t4) : 0u;
+        }
+        m[sub][0] = m[sub][1] = -INFINITY;
+        l[sub][0] = l[sub][1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) o[sub][mt][0] = o[sub][mt][1] = o[sub][mt][2] = o[sub][mt][3] = 0.f;
+      }
+    }
+    int stop = 0;
+    for (; pos < pend; ++pos) {
+      if (ids[pos - cb] < 0) { stop = 1; pos = pend; break; }
+      const int st = cnt % kV3Stages;
+      const int slot = c * kV3Stages + st;
+      if (!mbar_wait(full_all + 8 * slot, (fphase >> slot) & 1u, TI_DEVERR_ATTN_WAIT)) return;
+      fphase ^= 1u << slot;
+      uint8_t* kt = smem + slot * C::kStage;
+      const int valid = vtok[pos - cb];
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub) {
+        uint8_t* ks_ = kt + sub * kBlock * 128;
+        uint8_t* vs_ = kt + C::kTile + sub * kBlock * 128;
+        swapped_block<T>(smem_u32(ks_), smem_u32(vs_), vs_, valid, lane, qb[sub], p.scale_log2,
+                         m[sub], l[sub], o[sub]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_all + 8 * slot);
+      ++cnt;
+    }
+    // ---- finish the piece: lane holds heads (2t4, 2t4+1) x dims (16mt+g, 16mt+g+8)
+    T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
+    const int64_t pair = (int64_t)row * KVU + unit;
+#pragma unroll
+    for (int sub = 0; sub < HP; ++sub) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1)
+          l[sub][j] += __shfl_xor_sync(0xffffffffu, l[sub][j], off);
+    }
+    if (pieces == 1) {
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int hl = 2 * t4 + j;
+          if (hl >= G) continue;
+          const float inv = 1.f / l[sub][j];           // l == 0 -> NaN (attention.cu:150)
+          T* oh = outp + (int64_t)((unit * HP + sub) * G + hl) * 64;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            oh[mt * 16 + g] = Elem<T>::from_f(o[sub][mt][j] * inv);
+            oh[mt * 16 + g + 8] = Elem<T>::from_f(o[sub][mt][2 + j] * inv);
+          }
+        }
+    } else {
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int hl = 2 * t4 + j;
+          if (hl >= G) continue;
+          const int64_t sl = ((int64_t)row * p.num_heads + (unit * HP + sub) * G + hl) * p.max_parts + piece;
+          float* wo = p.ws_o + sl * 64;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            wo[mt * 16 + g] = o[sub][mt][j];
+            wo[mt * 16 + g + 8] = o[sub][mt][2 + j];
+          }
+          if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[sub][j], l[sub][j]);
+        }
+      if (lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.ws_count[pair], 1) == pieces - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        v2_merge<T>(p, row, unit, NHU, pieces, lane, outp);
+        if (lane == 0) p.ws_count[pair] = 0;     // ready for the next launch
+      }
+    }
+  }
+}
+
+// ==========================================================================================
+// v4: persistent, load-balanced, self-issuing kernel (head_dim 64, GQA groups <= 8)
+//
+// The whole batch's KV blocks form one stream (per sequence, per unit of HP kv heads); every
+// warp gets an equal contiguous chunk; a unit cut by chunk boundaries is split-K merged by the
+// last of its pieces to finish.  In the prologue each CTA resolves its range of the stream to
+// TMA row coordinates and valid-token counts in shared memory, so the main loop does no global
+// metadata loads.  Each warp then streams its own chunk through a kV4Stages-deep ring (lane 0
+// issues the next TMA as soon as a stage is consumed -- issue cost is spread over all warps)
+// and computes each KV block with tokens as the MMA M dimension and the group's query heads as
+// N (swapped_block).
+// ==========================================================================================
+constexpr int kV4Warps = 8;
+constexpr int kV4Stages = 3;
+constexpr int kV4IdCap = 2048;
+
+template <int HP>
+struct CfgV4 {
+  static constexpr int kTile = HP * kBlock * 64 * 2;
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kRing = kV4Warps * kV4Stages * kStage;
+  static constexpr int kBars = kV4Warps * kV4Stages * 8;
+  static constexpr int kIds = kV4IdCap * 4;
+  static constexpr int kVtok = kV4IdCap;
+  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
+  static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
+  static_assert(kTotal <= 227 * 1024, "v4 shared memory");
+};
+
+template <typename T, int HP>
+__global__ void __launch_bounds__(kV4Warps * 32, 1)
+decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
+                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  using C = CfgV4<HP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t bar_all = smem_u32(smem + C::kRing);
+  int* ids = reinterpret_cast<int*>(smem + C::kRing + C::kBars);
+  uint8_t* vtok = smem + C::kRing + C::kBars + C::kIds;
+  int* s_off = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kIds + C::kVtok);
+  constexpr int kThreads = kV4Warps * 32;
+  __shared__ int s_wsum[kV4Warps];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVH = p.num_kv_heads;
+  const int KVU = KVH / HP;
+  auto nblk_of = [&](int r) {
+    const int ctx = p.context_lens[r];
+    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
+  };
+
+  // ---- prefix sum of KVU * blocks per sequence
+  const int per = (batch + kThreads - 1) / kThreads;
+  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
+  int local = 0;
+  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  if (tid < kV4Warps * kV4Stages) {
+    mbar_init(bar_all + 8 * tid, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_wsum[w];
+  for (int r = r0; r < r1; ++r) {
+    s_off[r] = run;
+    run += KVU * nblk_of(r);
+  }
+  if (tid == 0) {
+    int tot = 0;
+    for (int w = 0; w < kV4Warps; ++w) tot += s_wsum[w];
+    s_off[batch] = tot;
+  }
+  __syncthreads();
+  const int total = s_off[batch];
+  const int W = gridDim.x * kV4Warps;
+  const int chunk = v2_chunk(total, W, p.max_blocks);
+  const int cb = blockIdx.x * kV4Warps * chunk;
+  if (cb >= total) return;
+  const int ce = min(total, cb + kV4Warps * chunk);
+
+  // ---- resolve the CTA's positions: TMA row coordinate (-1 = stop) and valid tokens
+  for (int q = tid; q < ce - cb; q += kThreads) {
+    const int pos = cb + q;
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
+    const int rel = pos - s_off[lo];
+    const int unit = rel / nb, j = rel - unit * nb;
+    const int brow = p.row_index ? p.row_index[lo] : lo;
+    const int phys = p.block_tables[(int64_t)brow * p.bt_stride + j];
+    const bool bad = phys < 0 || (int64_t)phys >= p.num_blocks;
+    ids[q] = bad ? -1 : (phys * KVH + unit * HP) * kBlock;
+    vtok[q] = (uint8_t)min(kBlock, p.context_lens[lo] - j * kBlock);
+  }
+  __syncthreads();
+
+  int pos = min(ce, cb + warp * chunk);
+  const int end = min(ce, pos + chunk);
+  if (pos >= end) return;
+  uint8_t* ring = smem + warp * kV4Stages * C::kStage;
+  const uint32_t bar = bar_all + warp * kV4Stages * 8;
+  const uint64_t pol = l2_policy_evict_first();
+  const int G = p.group;
+  const int NHU = HP * G;
+  const int g = lane >> 2, t4 = lane & 3;
+
+  // issue cursor: the next stream position with a readable block (after a negative entry the
+  // rest of its unit is skipped, exactly as the consume cursor below does)
+  auto unit_end = [&](int pp) {
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pp) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
+    return s_off[lo] + ((pp - s_off[lo]) / nb + 1) * nb;
+  };
+  int ip = pos, issued = 0, consumed = 0;
+  auto skip_stops = [&]() {
+    while (ip < end && ids[ip - cb] < 0) ip = min(end, unit_end(ip));
+  };
+  auto issue = [&]() {
+    if (lane == 0) {
+      const int st = issued % kV4Stages;
+      const uint32_t dst = smem_u32(ring + st * C::kStage);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(bar + 8 * st, C::kStage);
+      const int y = ids[ip - cb];
+      tma_load_2d_hint(dst, &kmap, bar + 8 * st, 0, y, pol);
+      tma_load_2d_hint(dst + C::kTile, &vmap, bar + 8 * st, 0, y, pol);
+    }
+    ++issued;
+    ++ip;
+    skip_stops();
+  };
+  skip_stops();
+  while (issued < kV4Stages && ip < end) issue();
+
+  uint32_t phase = 0;
+  uint32_t qb[HP][4][2];
+  float m[HP][2], l[HP][2], o[HP][4][4];
+
+  while (pos < end) {
+    // ---- a piece: positions of one unit inside [pos, end)
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int row = lo;
+    const int nb = (s_off[row + 1] - s_off[row]) / KVU;
+    const int unit = (pos - s_off[row]) / nb;
+    const int pstart = s_off[row] + unit * nb;
+    const int pend = min(end, pstart + nb);
+    const int piece = pos / chunk - pstart / chunk;
+    const int pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
+    {
+      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride;
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub) {
+        const T* qh = qrow + (int64_t)((unit * HP + sub) * G + g) * 64;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          qb[sub][ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t4) : 0u;
+          qb[sub][ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t4) : 0u;
+        }
+        m[sub][0] = m[sub][1] = -INFINITY;
+        l[sub][0] = l[sub][1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) o[sub][mt][0] = o[sub][mt][1] = o[sub][mt][2] = o[sub][mt][3] = 0.f;
+      }
+    }
+    int stop = 0;
+    for (; pos < pend; ++pos) {
+      if (ids[pos - cb] < 0) { stop = 1; pos = pend; break; }
+      const int st = consumed % kV4Stages;
+      if (!mbar_wait(bar + 8 * st, (phase >> st) & 1u, TI_DEVERR_ATTN_WAIT)) return;
+      phase ^= 1u << st;
+      uint8_t* kt = ring + st * C::kStage;
+      const int valid = vtok[pos - cb];
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub) {
+        uint8_t* ksub = kt + sub * kBlock * 128;
+        uint8_t* vsub = kt + C::kTile + sub * kBlock * 128;
+        swapped_block<T>(smem_u32(ksub), smem_u32(vsub), vsub, valid, lane, qb[sub], p.scale_log2,
+                         m[sub], l[sub], o[sub]);
+      }
+      ++consumed;
+      __syncwarp();                    // every lane is done with the stage before it is reused
+      if (ip < end) issue();
+    }
+    // ---- finish the piece: lane holds heads (2t4, 2t4+1) x dims (16mt+g, 16mt+g+8)
+    T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
+    const int64_t pair = (int64_t)row * KVU + unit;
+#pragma unroll
+    for (int sub = 0; sub < HP; ++sub)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1)
+          l[sub][j] += __shfl_xor_sync(0xffffffffu, l[sub][j], off);
+    if (pieces == 1) {
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int hl = 2 * t4 + j;
+          if (hl >= G) continue;
+          const float inv = 1.f / l[sub][j];           // l == 0 -> NaN (attention.cu:150)
+          T* oh = outp + (int64_t)((unit * HP + sub) * G + hl) * 64;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            oh[mt * 16 + g] = Elem<T>::from_f(o[sub][mt][j] * inv);
+            oh[mt * 16 + g + 8] = Elem<T>::from_f(o[sub][mt][2 + j] * inv);
+          }
+        }
+    } else {
+#pragma unroll
+      for (int sub = 0; sub < HP; ++sub)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int hl = 2 * t4 + j;
+          if (hl >= G) continue;
+          const int64_t sl = ((int64_t)row * p.num_heads + (unit * HP + sub) * G + hl) * p.max_parts + piece;
+          float* wo = p.ws_o + sl * 64;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            wo[mt * 16 + g] = o[sub][mt][j];
+            wo[mt * 16 + g + 8] = o[sub][mt][2 + j];
+          }
+          if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[sub][j], l[sub][j]);
+        }
+      if (lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
+      if (arrive_last(&p.ws_count[pair], pieces, lane)) {
+        v2_merge<T>(p, row, unit, NHU, pieces, lane, outp);
+        if (lane == 0) p.ws_count[pair] = 0;     // ready for the next launch
+      }
+    }
+  }
+}
+
+template <typename T, int HP>
+static int launch_v4(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
+                     cudaStream_t stream) {
+  using C = CfgV4<HP>;
+  static int set_dev = -1;
+  static int sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v4<T, HP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v4)");
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    set_dev = dev;
+  }
+  decode_kernel_v4<T, HP><<<sms, kV4Warps * 32, C::kTotal, stream>>>(km, vm, p, batch);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v4 launch");
+  return TI_OK;
+}
+
+template <typename T, int HP>
+static int launch_v3(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
+                     cudaStream_t stream) {
+  using C = CfgV3<HP>;
+  static int set_dev = -1;
+  static int sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v3<T, HP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v3)");
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    set_dev = dev;
+  }
+  decode_kernel_v3<T, HP><<<sms, (kV3Consumers + 1) * 32, C::kTotal, stream>>>(km, vm, p, batch);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v3 launch");
+  return TI_OK;
+}
+
 template <typename T, int HP>
 static int launch_v2(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
                      cudaStream_t stream) {
@@ -972,6 +1723,25 @@ extern "C" int ti_paged_attention_decode(
   rc = attn::kv_tensor_map(&vm, v_cache, rows, head_dim, dtype, hp * attn::kBlock);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (v2) {
+    // v3 needs its CTA's whole stream range in shared memory: check the worst case here
+    static int sms = 0;
+    if (!sms) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (sms <= 0) sms = 148;
+    }
+    const int64_t worst = (int64_t)batch * (num_kv_heads / hp) * max_blocks_per_seq;
+    const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq);
+    if (p.group <= 8 && chunk_ub * attn::kV4Warps <= attn::kV4IdCap) {
+      if (hp == 2)
+        return dtype == TI_DTYPE_BF16 ? attn::launch_v4<__nv_bfloat16, 2>(p, km, vm, batch, s)
+                                      : attn::launch_v4<__half, 2>(p, km, vm, batch, s);
+      return dtype == TI_DTYPE_BF16 ? attn::launch_v4<__nv_bfloat16, 1>(p, km, vm, batch, s)
+                                    : attn::launch_v4<__half, 1>(p, km, vm, batch, s);
+    }
+  }
   if (v2 && hp == 2)
     return dtype == TI_DTYPE_BF16 ? attn::launch_v2<__nv_bfloat16, 2>(p, km, vm, batch, s)
                                   : attn::launch_v2<__half, 2>(p, km, vm, batch, s);
