@@ -79,6 +79,29 @@ int ti_paged_attention_decode(void* out, int64_t out_seq_stride, const void* q,
                               int max_blocks_per_seq, int dtype, int partition_blocks,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- paged decode attention without caller scratch ---------------------------------------------
+ * No counterpart in the reference.  Same computation and arguments as
+ * ti_paged_attention_decode (default partitioning), but the split-K scratch is a static array
+ * inside this library, so the caller allocates nothing.  Meant for callers that cannot call
+ * cudaMalloc: a process whose device memory is already fully handed out (to the KV pool and a
+ * caching allocator it does not own), or code running where a device allocation would
+ * synchronise the device or is forbidden.  The array holds TI_NOALLOC_SCRATCH_BYTES (16 MiB) on
+ * every GPU that loads the library, until the process exits; a batch whose scratch need
+ * (ti_paged_attention_workspace_bytes) exceeds it is rejected with TI_ERR_WORKSPACE.  The first
+ * call on each device looks the array's device address up (cudaGetSymbolAddress) and loads
+ * the library's device code there: make that first call before any stream capture.  All calls
+ * share the array; each clears its arrival counters on `stream` before launching, and calls
+ * that overlap on the GPU race on the array. */
+#define TI_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int ti_paged_attention_decode_noalloc(void* out, int64_t out_seq_stride, const void* q,
+                                      int64_t q_seq_stride, const void* k_cache,
+                                      const void* v_cache, int64_t num_blocks,
+                                      const int32_t* block_tables, int64_t bt_stride,
+                                      const int32_t* row_index, const int32_t* context_lens,
+                                      int batch, int num_heads, int num_kv_heads, int head_dim,
+                                      int block_size, int max_blocks_per_seq, int dtype,
+                                      void* stream);
+
 /* ---- (a2) RoPE in place -------------------------------------------------------------------
  * Replaces custom_rope.apply_inplace (reference src/fused_rope.cu:84-128, binding
  * src/rope_binding.cpp:3-11): rotate-half RoPE on q [T, num_heads, head_dim] and

@@ -29,6 +29,8 @@ SIGNATURES: dict[str, tuple] = {
     "ti_paged_attention_workspace_bytes": (SZ, [I32, I32, I32, I32, I32, I32]),
     "ti_paged_attention_decode": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, I32, I32, I32,
                                         I32, I32, I32, I32, I32, P, SZ, P]),
+    "ti_paged_attention_decode_noalloc": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, I32, I32,
+                                                I32, I32, I32, I32, I32, P]),
     "ti_rope_inplace": (I32, [P, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, P]),
     "ti_rope_kv_append": (I32, [P, I64, P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, P]),
     "ti_swiglu": (I32, [P, P, I64, I32, I32, P]),
