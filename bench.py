@@ -43,6 +43,11 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--kernel", choices=["attention"], default=None,
+                    help="time one kernel alone instead of the decode step")
+    ap.add_argument("--case", choices=["256", "config1"], default="256",
+                    help="attention case: one layer of the 256-sequence workload, or the "
+                         "8-sequence ctx U[1,512] paged-attention op")
     return ap.parse_args()
 
 
@@ -443,9 +448,67 @@ def run_ours(a, rank, world, local):
     return 0
 
 
+def run_attention_kernel(a):
+    """Paged decode attention alone: one layer of the 256-sequence workload (ctx U[128,2048])
+    or the 8-sequence op of ctx U[1,512] over a 512-block pool; HBM GB/s of the kernel."""
+    import torch
+    from tiny_infra_b200 import custom_paged_attn
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(a.seed)
+    B, lo, hi, NB = (SEQS, CTX_LO, CTX_HI, None) if a.case == "256" else (8, 1, 512, 512)
+    NH, KVH, D, bs = 14, 2, 64, 16
+    ctx = rng.integers(lo, hi + 1, B).astype(np.int32)
+    need = int(sum((int(c) + bs - 1) // bs for c in ctx))
+    NB = NB or need + 64
+    mb = (hi + bs - 1) // bs
+    perm = rng.permutation(NB)
+    bt = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        n = (int(ctx[b]) + bs - 1) // bs
+        bt[b, :n] = perm[off:off + n]
+        off += n
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    q = torch.randn(B, NH, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    btt, ct = torch.from_numpy(bt).to(dev), torch.from_numpy(ctx).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > L2 (126 MB)
+    for _ in range(a.warmup):
+        custom_paged_attn.launch_paged_attention(out, q, k, v, btt, ct, bs)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        custom_paged_attn.launch_paged_attention(out, q, k, v, btt, ct, bs)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    t = float(np.mean(ts))
+    algo = int(ctx.sum()) * KVH * D * 2 * 2 + 2 * B * NH * D * 2
+    peak, kind = _peaks()
+    print(json.dumps({
+        "metric": "paged-attn HBM GB/s", "value": round(algo / t / 1e9, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (N(0,1) q/k/v, random block permutation)",
+        "config": {"workload": f"paged decode attention, {B} seqs, ctx U[{lo},{hi}], 14/2 heads, "
+                               f"D=64, pool {NB} blocks x 16", "l2": "flushed between launches"},
+        "roofline": {"bound": "hbm", "achieved": round(algo / t / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(algo / t / 1e9 / peak, 4),
+                     "peak_kind": kind, "algorithmic_bytes_per_launch": algo}}), flush=True)
+    return 0
+
+
 def main():
     a = _args()
     rank, world, local = _dist()
+    if a.kernel == "attention":
+        return run_attention_kernel(a) if rank == 0 else 0
     if a.impl == "reference":
         return run_reference(a, rank, world)
     return run_ours(a, rank, world, local)

@@ -49,7 +49,7 @@ uint64_t ti_launch_count(void);
  * `stream`.  *bits receives the TI_DEVERR_* bits raised since the last clear. */
 int ti_device_status(unsigned int* bits, int clear, void* stream);
 
-/* ---- (a1) paged decode attention ----------------------------------------------------------
+/* ---- paged decode attention ----------------------------------------------------------
  * Replaces custom_paged_attn.launch_paged_attention (reference src/attention.cu:156-197,
  * binding src/attention_binding.cpp:3-13).
  *   out [batch, num_heads, head_dim] (row stride out_seq_stride elements, written in place)
@@ -102,7 +102,7 @@ int ti_paged_attention_decode_noalloc(void* out, int64_t out_seq_stride, const v
                                       int block_size, int max_blocks_per_seq, int dtype,
                                       void* stream);
 
-/* ---- (a2) RoPE in place -------------------------------------------------------------------
+/* ---- RoPE in place -------------------------------------------------------------------
  * Replaces custom_rope.apply_inplace (reference src/fused_rope.cu:84-128, binding
  * src/rope_binding.cpp:3-11): rotate-half RoPE on q [T, num_heads, head_dim] and
  * k [T, num_kv_heads, head_dim] (token strides q_tok_stride / k_tok_stride elements, heads
@@ -111,7 +111,7 @@ int ti_rope_inplace(void* q, int64_t q_tok_stride, void* k, int64_t k_tok_stride
                     const float* cos, const float* sin, const int32_t* pos, int num_tokens,
                     int num_heads, int num_kv_heads, int head_dim, int dtype, void* stream);
 
-/* ---- (a2+a3) RoPE fused with the KV-append write ---------------------------------------------
+/* ---- RoPE fused with the KV-append write ---------------------------------------------
  * q/k/v of T new tokens, as laid out by the fused QKV projection: row t of `qkv` holds
  * [q (num_heads*head_dim) | k (num_kv_heads*head_dim) | v (num_kv_heads*head_dim)], row stride
  * qkv_stride elements.  Applies RoPE to q (in place) and k, then writes k and v into the pool at
@@ -122,13 +122,13 @@ int ti_rope_kv_append(void* qkv, int64_t qkv_stride, void* k_cache, void* v_cach
                       const int32_t* pos, int num_tokens, int num_heads, int num_kv_heads,
                       int head_dim, int block_size, int dtype, void* stream);
 
-/* ---- (a6) SwiGLU ----------------------------------------------------------------------------
+/* ---- SwiGLU ----------------------------------------------------------------------------
  * Replaces custom_swiglu.forward (reference src/fused_swiglu.cu:56-93): out[t, i] =
  * silu(x[t, i]) * x[t, I + i] for x [T, 2I] (gate half first), out [T, I]; I % 8 == 0,
  * contiguous rows. */
 int ti_swiglu(void* out, const void* x, int64_t num_tokens, int inter, int dtype, void* stream);
 
-/* ---- (a5) RMSNorm ----------------------------------------------------------------------------
+/* ---- RMSNorm ----------------------------------------------------------------------------
  * models/qwen_25.py:24-36.  out[t] = w * (x[t] * rsqrt(mean(x[t]^2) + eps)), x float32 or
  * the activation dtype (x_dtype), out and w in `dtype`.  The normalised row is rounded to
  * `dtype` before the weight multiply, as the reference does. */
@@ -140,7 +140,7 @@ int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* weight, float 
 int ti_embedding(float* out, const void* table, const int32_t* ids, int num_tokens, int hidden,
                  int64_t vocab, int dtype, void* stream);
 
-/* ---- (a6/a7/a8) projections on tcgen05 tensor cores -----------------------------------------
+/* ---- projections on tcgen05 tensor cores -----------------------------------------
  * Replaces the reference's nn.Linear calls (models/qwen_25.py:46-49,66-68,130,136-151,237-250)
  * with D[M, N] = A[M, K] . B[N, K]^T (A activations row-major, B an nn.Linear weight
  * [out_features, in_features], both `dtype`, fp32 accumulation in TMEM) and a fused epilogue:
@@ -148,9 +148,16 @@ int ti_embedding(float* out, const void* table, const int32_t* ids, int num_toke
  *   TI_EPI_SWIGLU    out[M, N/2] = silu(gate) * up (fused_swiglu.cu:39-50), where every group
  *                    of block_n weight rows holds block_n/2 gate rows followed by the matching
  *                    block_n/2 up rows
- *   TI_EPI_RESIDUAL  out (float32 [M, N], ldo) += D; split_k > 1 adds partial sums atomically
+ *   TI_EPI_RESIDUAL  out (float32 [M, N], ldo) += D
  *   TI_EPI_ARGMAX    aux_val/aux_idx [M, N/block_n] = (max, first argmax) of each row within each
  *                    block_n column tile; `out` (dtype logits) is also written when not NULL
+ * split_k is an upper bound on the split-K factor; it is lowered until the launch fits one wave
+ * of the GPU and each K slice has at least two 64-wide K blocks.  RESIDUAL (up to 16 slices):
+ * every slice adds its partial sums into `out` with atomic adds, so the order of the fp32
+ * additions -- and the last bits of `out` -- can vary from run to run.  STORE / SWIGLU
+ * (1, 2, 4 or 8 slices; block_n 64 or 128): the slices of a tile run on a thread-block cluster
+ * and are summed in a fixed order through distributed shared memory (deterministic).  ARGMAX
+ * and block_n 256 do not split.
  * Requirements: N % block_n == 0 (block_n 64, 128 or 256; 0 = 128), K % 64 == 0, 16-byte
  * aligned operands with leading dimensions multiple of 8 elements. */
 #define TI_EPI_STORE 0
@@ -161,7 +168,7 @@ int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb
             int K, void* out, int64_t ldo, const void* bias, float* aux_val, int32_t* aux_idx,
             int dtype, int block_n, int split_k, void* stream);
 
-/* ---- (a2+a3+a7) QKV projection fused with RoPE and the KV-append write ----------------------
+/* ---- QKV projection fused with RoPE and the KV-append write ----------------------
  * [q | k | v] = A[M, hidden] . W^T + bias, W = the fused [(NH+2*KVH)*64, hidden] q/k/v weight
  * (models/qwen_25.py:46-48,66-68).  RoPE (src/fused_rope.cu:37-50, tables cos/sin float32
  * [*, 32], positions pos[M]) is applied to q and k on the fp32 accumulators, so each value is
@@ -192,7 +199,7 @@ int ti_paged_prefill_attention(void* out, int64_t out_tok_stride, const void* q,
                                int num_kv_heads, int head_dim, int block_size, int dtype,
                                void* stream);
 
-/* ---- (a9/a11) decode-step packing on the device ---------------------------------------------
+/* ---- decode-step packing on the device ---------------------------------------------
  * For rows r < rows: slot = slots[r] (-1 = padding row).  First writes this step's new block,
  * block_tables[slot][seq_len[slot] / block_size] = new_block[r] when new_block[r] >= 0 (the
  * host allocator decided it, FIFO order of engine/cache_manager.py:86-92), then sets

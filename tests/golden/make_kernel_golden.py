@@ -3,7 +3,7 @@
 Runs on a GPU box, with the reference kernels prebuilt from the reference sources by
 ``oracle/build_ref.py`` (into ``oracle/_ref``):
 
-    python tests/golden/make_kernel_golden.py --out gpurun_out/kernel_golden.npz
+    python tests/golden/make_kernel_golden.py --out tests/golden/kernel_golden.npz
 
 Inputs are regenerated from the seeds in :func:`inputs` (numpy PCG64, stable across
 versions), so the fixture stores only the reference kernels' fp16 outputs.  The CPU test
@@ -64,7 +64,7 @@ def main() -> None:
     from oracle.build_ref import load_ref
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default="gpurun_out/kernel_golden.npz")
+    ap.add_argument("--out", default="tests/golden/kernel_golden.npz")
     a = ap.parse_args()
     dev = torch.device("cuda:0")
     pa, rp, sw = (load_ref("custom_paged_attn"), load_ref("custom_rope"),

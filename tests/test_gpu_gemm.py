@@ -72,10 +72,12 @@ def test_store_fp16(cuda_device):
     assert (err <= 2.0 ** -11 * np.abs(ref) + 1e-3).all()
 
 
-def test_swiglu_epilogue(cuda_device):
-    """gate/up projection with SwiGLU fused in the epilogue (weights interleaved per tile)."""
+@pytest.mark.parametrize("bn", [64, 128])
+def test_swiglu_epilogue(cuda_device, bn):
+    """gate/up projection with SwiGLU fused in the epilogue (weights interleaved per tile;
+    block_n 64 stores 64-byte output rows)."""
     from tiny_infra_b200 import _native as N_
-    M, I, K, bn = 256, 1024, 896, 128
+    M, I, K = 256, 1024, 896
     rng = np.random.default_rng(4)
     a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
     wg = bf16_round((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
@@ -88,18 +90,46 @@ def test_swiglu_epilogue(cuda_device):
     _close_bf16(out.float().cpu().numpy(), g / (1 + np.exp(-g)) * u)
 
 
-@pytest.mark.parametrize("split", [1, 3, 6])
-def test_residual_split_k(cuda_device, split):
-    """x_f32 += A W^T with split-K partial sums reduced by red.global.add."""
+@pytest.mark.parametrize("split,bn", [(1, 64), (2, 64), (3, 64), (5, 64), (8, 128), (16, 128)])
+def test_residual_split_k(cuda_device, split, bn):
+    """x_f32 += A W^T with each split-K slice adding its partial tile into x (red.add); a second
+    run agrees to fp32 rounding of the summation order."""
     from tiny_infra_b200 import _native as N_
     M, N, K = 256, 896, 4864
     a, b = _operands(5, M, N, K, wstd=0.02)
     x0 = np.random.default_rng(6).standard_normal((M, N)).astype(np.float32)
     x = torch.from_numpy(x0).cuda()
-    _gemm(N_.TI_EPI_RESIDUAL, _dev(a), _dev(b), M, N, K, out=x, ldo=N, block_n=64, split_k=split)
+    _gemm(N_.TI_EPI_RESIDUAL, _dev(a), _dev(b), M, N, K, out=x, ldo=N, block_n=bn, split_k=split)
     ref = x0 + a @ b.T
     rms = float(np.sqrt(np.mean(ref ** 2)))
-    assert np.abs(x.cpu().numpy() - ref).max() <= 1e-4 * rms + 1e-6
+    got = x.cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-4 * rms + 1e-6
+    x2 = torch.from_numpy(x0).cuda()
+    _gemm(N_.TI_EPI_RESIDUAL, _dev(a), _dev(b), M, N, K, out=x2, ldo=N, block_n=bn, split_k=split)
+    assert np.abs(x2.cpu().numpy() - got).max() <= 1e-6 * rms
+
+
+@pytest.mark.parametrize("bn,split", [(64, 2), (64, 4), (64, 8), (128, 2), (128, 4), (128, 8)])
+def test_cluster_split_k_store_and_swiglu(cuda_device, bn, split):
+    """STORE (+bias) and SwiGLU epilogues on split-K tiles reduced through distributed shared
+    memory; M = 200 leaves a partial M tile, K = 640 leaves split 8 with three empty splits."""
+    from tiny_infra_b200 import _native as N_
+    M, N, K = 200, 512, 640
+    a, b = _operands(11 + bn + split, M, N, K)
+    bias = bf16_round(np.random.default_rng(12).standard_normal(N).astype(np.float32) * 0.1)
+    out = torch.full((M, N), 9.0, dtype=torch.bfloat16, device="cuda")
+    _gemm(N_.TI_EPI_STORE, _dev(a), _dev(b), M, N, K, out=out, ldo=N, bias=_dev(bias),
+          block_n=bn, split_k=split)
+    _close_bf16(out.float().cpu().numpy(), a @ b.T + bias)
+    # SwiGLU: tile columns [0, bn/2) gate, [bn/2, bn) up
+    I, h = N // 2, bn // 2
+    wg, wu = b[:I], b[I:]
+    inter = np.concatenate([np.concatenate([wg[j:j + h], wu[j:j + h]]) for j in range(0, I, h)])
+    act = torch.full((M, I), 9.0, dtype=torch.bfloat16, device="cuda")
+    _gemm(N_.TI_EPI_SWIGLU, _dev(a), _dev(inter), M, N, K, out=act, ldo=I, block_n=bn,
+          split_k=split)
+    g, u = a @ wg.T, a @ wu.T
+    _close_bf16(act.float().cpu().numpy(), g / (1 + np.exp(-g)) * u)
 
 
 def test_argmax_epilogue(cuda_device):

@@ -224,13 +224,15 @@ def test_rmsnorm(cuda_device):
     assert (np.abs(_f32(out) - ref) <= tol * np.abs(ref) + 1e-5).all()
 
 
-def test_qkv_rope_append_gemm(cuda_device):
+@pytest.mark.parametrize("T", [300, 40, 2048])
+def test_qkv_rope_append_gemm(cuda_device, T):
     """QKV projection with RoPE and the KV append fused in the tcgen05 GEMM epilogue: q and the
     pool's k/v equal the float32 x W^T + b, rotated, rounded once to bf16 (one ulp allowed for
-    accumulation order)."""
+    accumulation order).  300 and 40 tokens run split-K over a cluster of 4, 2048 unsplit."""
     from tiny_infra_b200 import _native as N
     rng = np.random.default_rng(9)
-    T, H, NH, KVH, D, bs, NB = 300, 896, 14, 2, 64, 16, 64
+    H, NH, KVH, D, bs = 896, 14, 2, 64, 16
+    NB = (T + bs - 1) // bs + 48
     QKV = (NH + 2 * KVH) * D
     x = bf16_round(rng.standard_normal((T, H)).astype(np.float32))
     w = bf16_round((rng.standard_normal((QKV, H)) * 0.03).astype(np.float32))

@@ -1,6 +1,7 @@
 // Library-level C ABI: error reporting, launch accounting, device status word, tensor maps.
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -25,6 +26,14 @@ int set_cuda_error(cudaError_t e, const char* what) {
 }
 void clear_error() { t_last_error.clear(); }
 void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TI_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,

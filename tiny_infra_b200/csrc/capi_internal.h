@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 namespace ti {
 
 // Record an error message for ti_last_error() and return `code`.
@@ -11,6 +13,49 @@ int set_error(int code, const char* msg);
 int set_cuda_error(cudaError_t e, const char* what);
 void clear_error();
 void count_launch(unsigned n = 1);
+
+// Programmatic dependent launch: every kernel of this library is launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization, calls griddepcontrol.wait before it
+// touches memory that an earlier kernel may write, and griddepcontrol.launch_dependents once
+// it holds all of its on-chip resources.  The next kernel's CTAs then become resident while
+// this one drains, hiding the launch gap (and, for the GEMMs, the first weight tiles' fetch).
+// On by default; the environment variable TI_PDL=0 turns it off (plain stream ordering).
+bool pdl_enabled();
+
+// Launch `kern` on stream `s` (PDL attribute when enabled; a cluster of `cluster_z` CTAs along
+// grid z when > 1) and count it.  Returns TI_OK or TI_ERR_CUDA with `what` in the message.
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t s, int cluster_z, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = 1;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = (unsigned)cluster_z;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  count_launch();
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_cuda_error(e, what);
+  }
+  return 0;
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 int encode_tensor_map_2d(CUtensorMap* out, CUtensorMapDataType type, void* base,

@@ -27,6 +27,13 @@ __device__ __forceinline__ void raise_device_error(unsigned int bits) {
   atomicOr(&g_device_status, bits);
 }
 
+// Programmatic dependent launch (see launch_kernel): wait until every earlier kernel on the
+// stream has completed and its writes are visible; let the next kernel's CTAs be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Bounded waits give up after this many SM clock cycles (about 2 s at 1.9 GHz).
 constexpr long long kWaitCycles = 4000000000LL;
 

@@ -55,6 +55,8 @@ __global__ void rope_inplace_kernel(T* q, int64_t q_stride, T* k, int64_t k_stri
                                     const float* __restrict__ cos, const float* __restrict__ sin,
                                     const int32_t* __restrict__ pos, int T_, int NH, int KVH,
                                     int HD) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int half = HD / 2, per_head = half / 8;
   const int64_t per_tok = (int64_t)(NH + KVH) * per_head;
   const int64_t total = per_tok * T_;
@@ -90,6 +92,8 @@ __global__ void rope_append_kernel(T* qkv, int64_t stride, T* k_cache, T* v_cach
                                    const float* __restrict__ cos, const float* __restrict__ sin,
                                    const int32_t* __restrict__ pos, int T_, int NH, int KVH,
                                    int HD, int bs) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int half = HD / 2, P = half / 8;
   const int per_tok = (NH + KVH) * P + KVH * 2 * P;
   const int64_t total = (int64_t)per_tok * T_;
@@ -137,6 +141,8 @@ __global__ void rope_append_kernel(T* qkv, int64_t stride, T* k_cache, T* v_cach
 // ---- SwiGLU (drop-in for custom_swiglu.forward) -------------------------------------------
 template <typename T>
 __global__ void swiglu_kernel(T* __restrict__ out, const T* __restrict__ x, int64_t T_, int I) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int per = I / 8;
   const int64_t total = T_ * per;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -162,6 +168,8 @@ __global__ void swiglu_kernel(T* __restrict__ out, const T* __restrict__ x, int6
 template <typename TX, typename T>
 __global__ void rmsnorm_kernel(T* __restrict__ out, const TX* __restrict__ x,
                                const T* __restrict__ w, float eps, int rows, int H) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -196,6 +204,8 @@ __global__ void rmsnorm_kernel(T* __restrict__ out, const TX* __restrict__ x,
 template <typename T>
 __global__ void embedding_kernel(float* __restrict__ out, const T* __restrict__ table,
                                  const int32_t* __restrict__ ids, int rows, int H, int64_t V) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int per = H / 8;
   const int64_t total = (int64_t)rows * per;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -229,12 +239,6 @@ static int grid_for(int64_t work) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * 16));
 }
 
-static int finish(const char* what) {
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TI_OK : set_cuda_error(e, what);
-}
-
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace ew
@@ -258,16 +262,17 @@ extern "C" int ti_rope_inplace(void* q, int64_t q_tok_stride, void* k, int64_t k
   const int64_t work = (int64_t)num_tokens * (num_heads + num_kv_heads) * (head_dim / 16);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    ew::rope_inplace_kernel<__nv_bfloat16><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("rope launch", ew::rope_inplace_kernel<__nv_bfloat16>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__nv_bfloat16*)q, q_tok_stride, (__nv_bfloat16*)k, k_tok_stride, cos, sin, pos,
         num_tokens, num_heads, num_kv_heads, head_dim);
   else if (dtype == TI_DTYPE_FP16)
-    ew::rope_inplace_kernel<__half><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("rope launch", ew::rope_inplace_kernel<__half>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__half*)q, q_tok_stride, (__half*)k, k_tok_stride, cos, sin, pos, num_tokens,
         num_heads, num_kv_heads, head_dim);
   else
     return set_error(TI_ERR_UNSUPPORTED, "rope: dtype must be bf16 or fp16");
-  return ew::finish("rope launch");
 }
 
 extern "C" int ti_rope_kv_append(void* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
@@ -288,16 +293,17 @@ extern "C" int ti_rope_kv_append(void* qkv, int64_t qkv_stride, void* k_cache, v
   const int64_t work = (int64_t)num_tokens * ((num_heads + num_kv_heads) * P + num_kv_heads * 2 * P);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    ew::rope_append_kernel<__nv_bfloat16><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("rope_kv_append launch", ew::rope_append_kernel<__nv_bfloat16>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__nv_bfloat16*)qkv, qkv_stride, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache,
         slot_mapping, cos, sin, pos, num_tokens, num_heads, num_kv_heads, head_dim, block_size);
   else if (dtype == TI_DTYPE_FP16)
-    ew::rope_append_kernel<__half><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("rope_kv_append launch", ew::rope_append_kernel<__half>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__half*)qkv, qkv_stride, (__half*)k_cache, (__half*)v_cache, slot_mapping, cos, sin,
         pos, num_tokens, num_heads, num_kv_heads, head_dim, block_size);
   else
     return set_error(TI_ERR_UNSUPPORTED, "rope_kv_append: dtype must be bf16 or fp16");
-  return ew::finish("rope_kv_append launch");
 }
 
 extern "C" int ti_swiglu(void* out, const void* x, int64_t num_tokens, int inter, int dtype,
@@ -312,14 +318,15 @@ extern "C" int ti_swiglu(void* out, const void* x, int64_t num_tokens, int inter
   const int64_t work = num_tokens * (inter / 8);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    ew::swiglu_kernel<__nv_bfloat16><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("swiglu launch", ew::swiglu_kernel<__nv_bfloat16>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__nv_bfloat16*)out, (const __nv_bfloat16*)x, num_tokens, inter);
   else if (dtype == TI_DTYPE_FP16)
-    ew::swiglu_kernel<__half><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("swiglu launch", ew::swiglu_kernel<__half>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         (__half*)out, (const __half*)x, num_tokens, inter);
   else
     return set_error(TI_ERR_UNSUPPORTED, "swiglu: dtype must be bf16 or fp16");
-  return ew::finish("swiglu launch");
 }
 
 extern "C" int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* weight, float eps,
@@ -335,21 +342,24 @@ extern "C" int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* wei
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int g = ew::grid_for(work);
   if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_FP32)
-    ew::rmsnorm_kernel<float, __nv_bfloat16><<<g, ew::kThreads, 0, s>>>(
+    return launch_kernel("rmsnorm launch", ew::rmsnorm_kernel<float, __nv_bfloat16>,
+                         dim3(g), dim3(ew::kThreads), 0, s, 1,
         (__nv_bfloat16*)out, (const float*)x, (const __nv_bfloat16*)weight, eps, num_tokens, hidden);
   else if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_BF16)
-    ew::rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<g, ew::kThreads, 0, s>>>(
+    return launch_kernel("rmsnorm launch", ew::rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16>,
+                         dim3(g), dim3(ew::kThreads), 0, s, 1,
         (__nv_bfloat16*)out, (const __nv_bfloat16*)x, (const __nv_bfloat16*)weight, eps,
         num_tokens, hidden);
   else if (dtype == TI_DTYPE_FP16 && x_dtype == TI_DTYPE_FP32)
-    ew::rmsnorm_kernel<float, __half><<<g, ew::kThreads, 0, s>>>(
+    return launch_kernel("rmsnorm launch", ew::rmsnorm_kernel<float, __half>,
+                         dim3(g), dim3(ew::kThreads), 0, s, 1,
         (__half*)out, (const float*)x, (const __half*)weight, eps, num_tokens, hidden);
   else if (dtype == TI_DTYPE_FP16 && x_dtype == TI_DTYPE_FP16)
-    ew::rmsnorm_kernel<__half, __half><<<g, ew::kThreads, 0, s>>>(
+    return launch_kernel("rmsnorm launch", ew::rmsnorm_kernel<__half, __half>,
+                         dim3(g), dim3(ew::kThreads), 0, s, 1,
         (__half*)out, (const __half*)x, (const __half*)weight, eps, num_tokens, hidden);
   else
     return set_error(TI_ERR_UNSUPPORTED, "rmsnorm: unsupported dtype combination");
-  return ew::finish("rmsnorm launch");
 }
 
 extern "C" int ti_embedding(float* out, const void* table, const int32_t* ids, int num_tokens,
@@ -362,12 +372,13 @@ extern "C" int ti_embedding(float* out, const void* table, const int32_t* ids, i
   const int64_t work = (int64_t)num_tokens * (hidden / 8);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    ew::embedding_kernel<__nv_bfloat16><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("embedding launch", ew::embedding_kernel<__nv_bfloat16>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         out, (const __nv_bfloat16*)table, ids, num_tokens, hidden, vocab);
   else if (dtype == TI_DTYPE_FP16)
-    ew::embedding_kernel<__half><<<ew::grid_for(work), ew::kThreads, 0, s>>>(
+    return launch_kernel("embedding launch", ew::embedding_kernel<__half>,
+                         dim3(ew::grid_for(work)), dim3(ew::kThreads), 0, s, 1,
         out, (const __half*)table, ids, num_tokens, hidden, vocab);
   else
     return set_error(TI_ERR_UNSUPPORTED, "embedding: dtype must be bf16 or fp16");
-  return ew::finish("embedding launch");
 }

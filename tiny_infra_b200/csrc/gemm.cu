@@ -9,21 +9,33 @@
 //   TI_EPI_SWIGLU    out = silu(gate) * up                   gate/up projection + SwiGLU
 //                    (fused_swiglu.cu:39-50; no [T, 2I] intermediate, no torch.cat)
 //   TI_EPI_RESIDUAL  x_f32 += D                              o_proj / down_proj + residual add
-//                    (models/qwen_25.py:182,191), split-K partials reduced with red.add
+//                    (models/qwen_25.py:182,191), one red.add per element
 //   TI_EPI_ARGMAX    per-row (max, first argmax) of each N tile, logits optionally stored
 //                    (greedy decoding without writing [M, vocab] logits)
+//   TI_EPI_QKV_ROPE  bias + RoPE on q and k, q stored, k and v written into the paged pool
 //
-// Kernel structure (one 128 x BN output tile per CTA, 192 threads):
-//   warp 0    one elected thread issues TMA tile loads (A: 128 x 64, B: BN x 64, SWIZZLE_128B)
-//             into a STAGES-deep shared-memory ring, mbarrier full/empty handshake;
+// Kernel structure (one 128 x BN output tile per cluster of CL CTAs, 192 threads per CTA):
+//   warp 0    set-up (barriers, TMEM allocation);
 //   warp 1    one elected thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN,
 //             K=16 per instruction) from shared-memory descriptors into a TMEM accumulator and
 //             frees each stage with tcgen05.commit;
-//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time from the TMEM lanes of their quadrant
-//             (warp w reads rows 32*(w%4)..+31), apply the fused epilogue, store.
-// Every wait is bounded (about 2 s): on expiry the kernel records TI_DEVERR_GEMM_WAIT, skips
-// the rest of its work, frees its TMEM and returns.
+//   warps 2-5 first the TMA tile loads (A: 128 x 64, B: BN x 64, SWIZZLE_128B) into a ~192 KB
+//             shared-memory ring (mbarrier full/empty handshake), lane 0 of each warp every
+//             4th K block; weight tiles of the first stages are fetched before the wait on the
+//             previous kernel.  Then the epilogue: tcgen05.ld from the TMEM lanes of their
+//             quadrant (warp w reads rows
+//             32*(w%4)..+31).  Split-K: for the residual every K slice red.adds its partial
+//             tile into x; for the other epilogues (nonlinear in the sum) the slices run on a
+//             cluster of CL CTAs, each parks its partial tile in shared memory and finishes
+//             128/CL rows by summing the cluster's partials through distributed shared memory
+//             in a fixed order.  The finished tile is staged in shared memory (swizzled rows) and
+//             written out with every warp store covering whole lines (red.add for the
+//             residual).
+// A kernel that uses TMEM runs one CTA per SM, so the ring is sized for one CTA.  Every wait
+// is bounded (about 2 s): on expiry the kernel records TI_DEVERR_GEMM_WAIT, skips the rest of
+// its work, frees its TMEM and returns.
 #include <algorithm>
+#include <cstring>
 #include <type_traits>
 #include <mutex>
 #include <unordered_map>
@@ -101,6 +113,31 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, bool bf16) {
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// ---- cluster helpers (split-K partial tiles reduced through distributed shared memory) ------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_peer(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_peer_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // ---- epilogues ----------------------------------------------------------------------------
 struct EpiArgs {
   void* out;
@@ -110,7 +147,6 @@ struct EpiArgs {
   int32_t* aux_idx;
   int M, N;
   int ntiles;
-  int atomic;         // residual: split-K > 1
   // QKV + RoPE + KV append (TI_EPI_QKV_ROPE): one 64-wide N tile is one head
   const int32_t* pos;
   const int64_t* slot_mapping;
@@ -121,160 +157,296 @@ struct EpiArgs {
   int num_heads, num_kv_heads, block_size;
 };
 
-template <typename T>
-__device__ __forceinline__ void store_row_chunk(T* dst, const float* v) {   // 32 values
+struct Best {
+  float v;
+  int i;
+  __device__ __forceinline__ void take(float x, int idx) {   // larger value, then lower index
+    if (x > v || (x == v && idx < i)) { v = x; i = idx; }
+  }
+};
+
+// ---- output staging -----------------------------------------------------------------------
+// The finished tile is written to shared memory as panels of R rows x PB bytes (PB = 128, or
+// 64 for 64-byte output rows) with the 16-byte chunk index XORed by row % 8 (PB = 128) or
+// (row / 2) % 4 (PB = 64), so that thread-per-row writes and chunk-per-thread reads are both
+// free of bank conflicts; store_tile then writes it out line by line.
+template <int PB>
+__device__ __forceinline__ uint32_t stage_off(int r, int byte_col, int R) {
+  const int panel = byte_col / PB;
+  const int chunk = (byte_col % PB) >> 4;
+  const int sw = PB == 128 ? (r & 7) : ((r >> 1) & 3);
+  return (uint32_t)(panel * R * PB + r * PB + ((chunk ^ sw) << 4) + (byte_col & 15));
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z,
+                                             uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+// NV values for staged row r, tile columns col..col+NV-1, converted to OT (panels of PB bytes).
+template <typename OT, int NV, int PB>
+__device__ __forceinline__ void stage_vals(uint32_t base, int R, int r, int col, const float* v) {
+  static_assert(NV % 4 == 0, "chunks of 4");
+  if constexpr (sizeof(OT) == 4) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u;
-    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+    for (int g = 0; g < NV; g += 4)
+      st_shared_v4(base + stage_off<PB>(r, (col + g) * 4, R), __float_as_uint(v[g]),
+                   __float_as_uint(v[g + 1]), __float_as_uint(v[g + 2]), __float_as_uint(v[g + 3]));
+  } else if constexpr (NV % 8 == 0) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = Elem<T>::pack2(v[i * 8 + 2 * j], v[i * 8 + 2 * j + 1]);
-    *reinterpret_cast<uint4*>(dst + i * 8) = u;
+    for (int g = 0; g < NV; g += 8)
+      st_shared_v4(base + stage_off<PB>(r, (col + g) * 2, R), Elem<OT>::pack2(v[g], v[g + 1]),
+                   Elem<OT>::pack2(v[g + 2], v[g + 3]), Elem<OT>::pack2(v[g + 4], v[g + 5]),
+                   Elem<OT>::pack2(v[g + 6], v[g + 7]));
+  } else {
+    st_shared_v2(base + stage_off<PB>(r, col * 2, R), Elem<OT>::pack2(v[0], v[1]),
+                 Elem<OT>::pack2(v[2], v[3]));
+  }
+}
+__device__ __forceinline__ void epilogue_bar() {   // the 4 epilogue warps
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Staged tile: columns and element size per epilogue kind.
+template <typename T, int BN, int KIND>
+struct Out {
+  using OT = typename std::conditional<KIND == TI_EPI_RESIDUAL, float, T>::type;
+  static constexpr int kCols = KIND == TI_EPI_SWIGLU ? BN / 2 : BN;
+  static constexpr int kBytes = kCols * (int)sizeof(OT);   // per staged row
+  static constexpr int kPanelBytes = kBytes < 128 ? 64 : 128;
+  static_assert(kBytes % kPanelBytes == 0, "whole panels");
+};
+
+// Epilogue operands that do not depend on the accumulator (bias, RoPE table rows, pool slot),
+// loaded by the epilogue threads while the MMAs still run (split-K path: chunks of NV <= 32).
+template <typename T, int BN, int KIND, int NV>
+struct Pre {
+  static constexpr bool kBias = KIND == TI_EPI_STORE || KIND == TI_EPI_QKV_ROPE;
+  static constexpr bool kRope = KIND == TI_EPI_QKV_ROPE;
+  float a[kBias ? NV : 1], b[kBias ? NV : 1];   // bias for the lo / hi chunk
+  float cs[kRope ? NV : 1], sn[kRope ? NV : 1];
+  bool has_bias;
+
+  __device__ __forceinline__ void load(const EpiArgs& e, int row, int n0, int c) {
+    constexpr int H2 = BN / 2;
+    if constexpr (kBias) {
+      const T* bp = reinterpret_cast<const T*>(e.bias);
+      has_bias = bp != nullptr;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        a[i] = bp ? Elem<T>::to_f(bp[n0 + c + i]) : 0.f;
+        b[i] = bp ? Elem<T>::to_f(bp[n0 + H2 + c + i]) : 0.f;
+      }
+    }
+    if constexpr (kRope) {
+      if (n0 / 64 < e.num_heads + e.num_kv_heads) {
+        const int64_t pr = (int64_t)e.pos[row] * 32 + c;
+#pragma unroll
+        for (int i = 0; i < NV; i += 4) {
+          const float4 cv = *reinterpret_cast<const float4*>(e.cos + pr + i);
+          const float4 sv = *reinterpret_cast<const float4*>(e.sin + pr + i);
+          cs[i] = cv.x; cs[i + 1] = cv.y; cs[i + 2] = cv.z; cs[i + 3] = cv.w;
+          sn[i] = sv.x; sn[i + 1] = sv.y; sn[i + 2] = sv.z; sn[i + 3] = sv.w;
+        }
+      }
+    }
+  }
+};
+
+// silu(g) * u with the reference's formula g / (1 + e^-g) * u and its __expf
+// (src/fused_swiglu.cu:44-48); the division is the fast x * rcp form (a few fp32 ulp, far
+// below the bf16 rounding of the result) -- the IEEE divide costs about 4x the whole epilogue.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+// The epilogue of one output row on two column chunks of the 128 x BN tile: `lo` holds tile
+// columns [c, c + NV), `hi` the columns [BN/2 + c, BN/2 + c + NV) -- the pairs that SwiGLU
+// (gate, up) and rotate-half RoPE (x1, x2) combine.  Values are the finished fp32 sums; the
+// results go to staged row `lr` (R staged rows).  `row` is the global row (< M when live).
+template <typename T, int BN, int KIND, int NV, bool PRE>
+__device__ __forceinline__ void epilogue_chunk(const EpiArgs& e, int row, bool live, int lr, int n0,
+                                               int c, float* lo, float* hi, Best& best,
+                                               const Pre<T, BN, KIND, PRE ? NV : 4>& pre,
+                                               uint32_t stage, int R) {
+  constexpr int H2 = BN / 2;
+  constexpr int PB = Out<T, BN, KIND>::kPanelBytes;
+  if constexpr (KIND == TI_EPI_STORE || KIND == TI_EPI_QKV_ROPE) {
+    if constexpr (PRE) {
+      if (pre.has_bias) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) { lo[i] += pre.a[i]; hi[i] += pre.b[i]; }
+      }
+    } else {
+      const T* b = reinterpret_cast<const T*>(e.bias);
+      if (b) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          lo[i] += Elem<T>::to_f(b[n0 + c + i]);
+          hi[i] += Elem<T>::to_f(b[n0 + H2 + c + i]);
+        }
+      }
+    }
+  }
+  if constexpr (KIND == TI_EPI_QKV_ROPE) {
+    // BN == head_dim == 64: lo = x1 (dims c..), hi = x2 (dims 32 + c..), the rotate-half pairs.
+    // RoPE runs on the fp32 accumulators (+bias) and each value is rounded once, q into `out`,
+    // k and v into the pool (src/fused_rope.cu:37-50, engine/cache_manager.py:95-99).
+    static_assert(BN == 64, "one head per tile");
+    if (n0 / 64 < e.num_heads + e.num_kv_heads) {
+      float cc[NV], ss[NV];
+      if constexpr (PRE) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) { cc[i] = pre.cs[i]; ss[i] = pre.sn[i]; }
+      } else {
+        const int64_t pr = (int64_t)(live ? e.pos[row] : 0) * 32 + c;
+#pragma unroll
+        for (int i = 0; i < NV; i += 4) {
+          const float4 cv = *reinterpret_cast<const float4*>(e.cos + pr + i);
+          const float4 sv = *reinterpret_cast<const float4*>(e.sin + pr + i);
+          cc[i] = cv.x; cc[i + 1] = cv.y; cc[i + 2] = cv.z; cc[i + 3] = cv.w;
+          ss[i] = sv.x; ss[i + 1] = sv.y; ss[i + 2] = sv.z; ss[i + 3] = sv.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const float x1 = lo[i], x2 = hi[i];
+        lo[i] = x1 * cc[i] - x2 * ss[i];
+        hi[i] = x1 * ss[i] + x2 * cc[i];
+      }
+    }
+  }
+  if constexpr (KIND == TI_EPI_SWIGLU) {
+    // tile columns [0, BN/2) are gate rows g0..g0+BN/2-1, [BN/2, BN) the matching up rows
+#pragma unroll
+    for (int i = 0; i < NV; ++i) lo[i] = silu_mul(lo[i], hi[i]);
+    stage_vals<T, NV, PB>(stage, R, lr, c, lo);
+  } else if constexpr (KIND == TI_EPI_ARGMAX) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      best.take(lo[i], n0 + c + i);
+      best.take(hi[i], n0 + H2 + c + i);
+    }
+    if (e.out) {
+      stage_vals<T, NV, PB>(stage, R, lr, c, lo);
+      stage_vals<T, NV, PB>(stage, R, lr, H2 + c, hi);
+    }
+  } else {
+    using OT = typename Out<T, BN, KIND>::OT;
+    stage_vals<OT, NV, PB>(stage, R, lr, c, lo);
+    stage_vals<OT, NV, PB>(stage, R, lr, H2 + c, hi);
   }
 }
 
+// Write the staged tile (R rows starting at global row y0) to global memory: the 128 epilogue
+// threads walk it in 16-byte chunks, consecutive threads on consecutive chunks of a row, so
+// each warp store covers whole lines; the residual adds with red.global.add (one add per
+// element: deterministic).  The k / v heads of the QKV epilogue go to their pool slots, one
+// 128-byte row per token.  Fire-and-forget: the CTA does not wait for the writes.
 template <typename T, int BN, int KIND>
-__device__ __forceinline__ void epilogue(const EpiArgs& e, uint32_t tmem_row, int row, int n0,
-                                         int tile_n) {
-  const bool live = row < e.M;
-  if constexpr (KIND == TI_EPI_STORE) {
-    T* o = reinterpret_cast<T*>(e.out) + (int64_t)row * e.ldo + n0;
-    const T* b = reinterpret_cast<const T*>(e.bias);
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(tmem_row + c, v);
-      if (b) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += Elem<T>::to_f(b[n0 + c + i]);
-      }
-      if (live) store_row_chunk<T>(o + c, v);
-    }
-  } else if constexpr (KIND == TI_EPI_SWIGLU) {
-    // tile columns [0, BN/2) are gate rows g0..g0+BN/2-1, [BN/2, BN) the matching up rows
-    T* o = reinterpret_cast<T*>(e.out) + (int64_t)row * e.ldo + n0 / 2;
-#pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
-      float g[32], u[32];
-      tmem_ld32(tmem_row + c, g);
-      tmem_ld32(tmem_row + BN / 2 + c, u);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
-      if (live) store_row_chunk<T>(o + c, g);
-    }
-  } else if constexpr (KIND == TI_EPI_RESIDUAL) {
-    float* x = reinterpret_cast<float*>(e.out) + (int64_t)row * e.ldo + n0;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(tmem_row + c, v);
-      if (!live) continue;
-      if (e.atomic) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(x + c + i),
-                       "f"(v[i]), "f"(v[i + 1]), "f"(v[i + 2]), "f"(v[i + 3])
-                       : "memory");
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          float4 a = *reinterpret_cast<float4*>(x + c + i);
-          a.x += v[i]; a.y += v[i + 1]; a.z += v[i + 2]; a.w += v[i + 3];
-          *reinterpret_cast<float4*>(x + c + i) = a;
-        }
-      }
-    }
-  } else if constexpr (KIND == TI_EPI_QKV_ROPE) {
-    // BN == head_dim == 64: columns [0,32) and [32,64) of the tile are the rotate-half pairs.
-    // RoPE runs on the fp32 accumulators (+bias) and each value is rounded once, q into `out`,
-    // k and v straight into the pool (src/fused_rope.cu:37-50, engine/cache_manager.py:95-99).
-    static_assert(BN == 64, "one head per tile");
-    const int head = n0 / 64;
-    float x1[32], x2[32];
-    tmem_ld32(tmem_row, x1);
-    tmem_ld32(tmem_row + 32, x2);
-    if (!live) return;
-    const T* b = reinterpret_cast<const T*>(e.bias);
-    if (b) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        x1[i] += Elem<T>::to_f(b[n0 + i]);
-        x2[i] += Elem<T>::to_f(b[n0 + 32 + i]);
-      }
-    }
-    if (head < e.num_heads + e.num_kv_heads) {
-      const float* cs = e.cos + (int64_t)e.pos[row] * 32;
-      const float* sn = e.sin + (int64_t)e.pos[row] * 32;
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 c = *reinterpret_cast<const float4*>(cs + i);
-        const float4 s = *reinterpret_cast<const float4*>(sn + i);
-        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = x1[i + j], bb = x2[i + j];
-          x1[i + j] = a * cc[j] - bb * ss[j];
-          x2[i + j] = a * ss[j] + bb * cc[j];
-        }
-      }
-    }
-    if (head < e.num_heads) {
-      T* o = reinterpret_cast<T*>(e.out) + (int64_t)row * e.ldo + n0;
-      store_row_chunk<T>(o, x1);
-      store_row_chunk<T>(o + 32, x2);
-    } else {
-      const int64_t slot = e.slot_mapping[row];
-      if (slot < 0) return;
+__device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int R, int n0, int y0,
+                                           bool ok) {
+  using O = Out<T, BN, KIND>;
+  constexpr int PB = O::kPanelBytes;
+  constexpr int CPR = O::kBytes / 16;   // 16-byte chunks per staged row
+  epilogue_bar();                       // the whole tile is staged
+  if (!ok) return;
+  const int t = (int)threadIdx.x - 64;
+  if constexpr (KIND == TI_EPI_QKV_ROPE) {
+    if (n0 / 64 >= e.num_heads) {
+      const int head = n0 / 64;
       const bool is_k = head < e.num_heads + e.num_kv_heads;
       const int kh = is_k ? head - e.num_heads : head - e.num_heads - e.num_kv_heads;
       T* pool = reinterpret_cast<T*>(is_k ? e.k_cache : e.v_cache);
-      T* dst = pool + (((slot / e.block_size) * e.num_kv_heads + kh) * e.block_size +
-                       slot % e.block_size) * 64;
-      store_row_chunk<T>(dst, x1);
-      store_row_chunk<T>(dst + 32, x2);
+      for (int idx = t; idx < R * 8; idx += 128) {   // 8 threads per 128-byte row
+        const int r = idx >> 3, ch = idx & 7;
+        const int row = y0 + r;
+        if (row >= e.M) continue;
+        const int64_t slot = e.slot_mapping[row];
+        if (slot < 0) continue;
+        const uint4 v = ld_shared_v4(stage + stage_off<PB>(r, ch * 16, R));
+        T* dst = pool + (((slot / e.block_size) * e.num_kv_heads + kh) * e.block_size +
+                         slot % e.block_size) * 64 + ch * 8;
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+      return;
     }
-  } else {   // TI_EPI_ARGMAX
-    float best = -INFINITY;
-    int bidx = 0x7fffffff;
-    T* o = e.out ? reinterpret_cast<T*>(e.out) + (int64_t)row * e.ldo + n0 : nullptr;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(tmem_row + c, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (v[i] > best) { best = v[i]; bidx = n0 + c + i; }   // first index on ties
-      if (o && live) store_row_chunk<T>(o + c, v);
-    }
-    if (live) {
-      e.aux_val[(int64_t)row * e.ntiles + tile_n] = best;
-      e.aux_idx[(int64_t)row * e.ntiles + tile_n] = bidx;
+  }
+  if constexpr (KIND == TI_EPI_ARGMAX) {
+    if (!e.out) return;
+  }
+  using OT = typename O::OT;
+  const int x0 = KIND == TI_EPI_SWIGLU ? n0 / 2 : n0;
+  uint8_t* base = reinterpret_cast<uint8_t*>(e.out) + (int64_t)x0 * (int64_t)sizeof(OT);
+  const int64_t pitch = e.ldo * (int64_t)sizeof(OT);
+  for (int idx = t; idx < R * CPR; idx += 128) {
+    const int r = idx / CPR, ch = idx % CPR;
+    const int row = y0 + r;
+    if (row >= e.M) continue;
+    const uint4 v = ld_shared_v4(stage + stage_off<PB>(r, ch * 16, R));
+    uint8_t* dst = base + row * pitch + ch * 16;
+    if constexpr (KIND == TI_EPI_RESIDUAL) {
+      asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                   "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                   "f"(__uint_as_float(v.w))
+                   : "memory");
+    } else {
+      *reinterpret_cast<uint4*>(dst) = v;
     }
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CL>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kSmem = STAGES * kStage + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr int kRing = STAGES * kStage;
+  // split-K across a cluster of CL CTAs: each CTA leaves its fp32 partial tile in shared memory
+  // (over the drained stage ring, rows padded by 16 bytes against bank conflicts) and finishes
+  // BM / CL rows of the cluster's tile through distributed shared memory.
+  static constexpr int kRedStride = BN + 4;
+  static constexpr int kRedBytes = CL > 1 ? BM * kRedStride * 4 : 0;
+  static constexpr int kStageOff = (kRedBytes + 1023) / 1024 * 1024;   // output staging
+  static constexpr int kRows = BM / CL;            // rows each CTA of the cluster finishes
+  static constexpr int kW = BN / 2 / CL;           // chunk width per thread
+  // mbarriers (full, empty per stage; accumulator) and the TMEM address slot
+  static constexpr int kBarBytes = (2 * STAGES + 1) * 8 + 8;
+  // The ring starts on a 1024-byte boundary (128-byte swizzle atoms); the barriers go into
+  // the alignment slack below it when that has room, else right after the ring.
+  static constexpr int kSmem = kRing + 1024;
+  static_assert(2 * kBarBytes <= 1024, "barriers fit beside the ring in the 1 KB slack");
+  static_assert(CL == 1 || kW % 4 == 0, "cluster chunks must be multiples of 4 columns");
+  static_assert(kStageOff + kRows * BN * 4 <= kRing, "partials and staged tile fit the ring");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
-template <typename T, int BN, int STAGES, int KIND>
+// One 128 x BN output tile per cluster of CL CTAs (CL = split-K factor along grid z).
+template <typename T, int BN, int STAGES, int KIND, int CL>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
             int K, int kb_per_split, EpiArgs e) {
-  using C = Cfg<BN, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
+  using C = Cfg<BN, STAGES, CL>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  uint8_t* bars = (smem - smem_raw >= C::kBarBytes) ? smem_raw : smem + C::kRing;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t full0 = sbase + STAGES * C::kStage;
+  const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + STAGES * 8;
   const uint32_t accum = empty0 + STAGES * 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * C::kStage + (2 * STAGES + 1) * 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + (2 * STAGES + 1) * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_n = blockIdx.x;
@@ -302,31 +474,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // All on-chip resources are held: the next kernel may be scheduled.
+  pdl_launch_dependents();
 
-  if (warp == 0) {
-    if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_last();    // activations: re-read by many CTAs
-      const uint64_t pol_b = l2_policy_evict_first();   // weights: streamed once
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % STAGES;
-        if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((it / STAGES) & 1) ^ 1, TI_DEVERR_GEMM_WAIT))
-          break;
-        mbar_arrive_expect_tx(full0 + 8 * s, C::kStage);
-        const uint32_t sa = sbase + s * C::kStage;
-        const int kx = (kb0 + it) * BK;
-        tma_load_2d_hint(sa, &amap, full0 + 8 * s, kx, m0, pol_a);
-        tma_load_2d_hint(sa + C::kABytes, &bmap, full0 + 8 * s, kx, n0, pol_b);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
+  // split-K: the row / columns this thread finishes after the cluster reduction
+  const int red_t = (int)threadIdx.x - 64;
+  const uint32_t rank = CL > 1 ? cluster_rank() : 0u;
+  const int red_lr = (red_t >= 0 ? red_t : 0) / CL;   // row within this CTA's kRows
+  const int red_c = ((red_t >= 0 ? red_t : 0) % CL) * C::kW;
+  const int red_row = m0 + (int)rank * C::kRows + red_lr;
+  const bool red_live = red_t >= 0 && red_row < e.M;
+  Pre<T, BN, KIND, (CL > 1 ? C::kW : 4)> pre;
+  bool ok = true;
+
+  if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(BN, std::is_same<T, __nv_bfloat16>::value);
-      bool ok = true;
-      for (int it = 0; it < nk && ok; ++it) {
+      for (int it = 0; it < nk; ++it) {
         const int s = it % STAGES;
-        ok = mbar_wait(full0 + 8 * s, (it / STAGES) & 1, TI_DEVERR_GEMM_WAIT);
-        if (!ok) break;
+        if (!mbar_wait(full0 + 8 * s, (it / STAGES) & 1, TI_DEVERR_GEMM_WAIT)) break;
         tc_fence_after();
         const uint32_t sa = sbase + s * C::kStage;
         const uint64_t da = smem_desc(sa), db = smem_desc(sa + C::kABytes);
@@ -338,12 +504,123 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       tc_commit(accum);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= 2) {
+    // Producers: lane 0 of each epilogue warp issues the TMA loads of every 4th K block (one
+    // issuing thread's loads complete one after another, four streams overlap).
+    if (lane == 0) {
+      const int p = warp - 2;
+      const uint64_t pol_a = l2_policy_evict_last();    // activations: re-read by many CTAs
+      const uint64_t pol_b = l2_policy_evict_first();   // weights: streamed once
+      // Weights do not depend on earlier kernels: fetch the first stages' B tiles before
+      // waiting for the producer of the activations.
+      const int pre_n = min(nk, STAGES);
+      for (int it = p; it < pre_n; it += 4) {
+        mbar_arrive_expect_tx(full0 + 8 * it, C::kStage);
+        tma_load_2d_hint(sbase + it * C::kStage + C::kABytes, &bmap, full0 + 8 * it,
+                         (kb0 + it) * BK, n0, pol_b);
+      }
+      pdl_wait();
+      for (int it = p; it < pre_n; it += 4)
+        tma_load_2d_hint(sbase + it * C::kStage, &amap, full0 + 8 * it, (kb0 + it) * BK, m0, pol_a);
+      for (int it = p; it < nk; it += 4) {
+        if (it < pre_n) continue;
+        const int s = it % STAGES;
+        if (!mbar_wait(empty0 + 8 * s, ((it / STAGES) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
+        mbar_arrive_expect_tx(full0 + 8 * s, C::kStage);
+        const uint32_t sa = sbase + s * C::kStage;
+        const int kx = (kb0 + it) * BK;
+        tma_load_2d_hint(sa, &amap, full0 + 8 * s, kx, m0, pol_a);
+        tma_load_2d_hint(sa + C::kABytes, &bmap, full0 + 8 * s, kx, n0, pol_b);
+      }
+    }
+    __syncwarp();
+    pdl_wait();   // the epilogue reads and writes memory of earlier kernels
     const int quad = warp & 3;
-    const int row = m0 + quad * 32 + lane;
-    const bool ok = mbar_wait(accum, 0, TI_DEVERR_GEMM_WAIT);
+    if constexpr (CL > 1) {
+      if (red_live) pre.load(e, red_row, n0, red_c);
+    }
+    ok = mbar_wait(accum, 0, TI_DEVERR_GEMM_WAIT);
     tc_fence_after();
-    if (ok && nk > 0) epilogue<T, BN, KIND>(e, tmem + ((uint32_t)(quad * 32) << 16), row, n0, tile_n);
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    if constexpr (CL == 1) {
+      const int lr = quad * 32 + lane;
+      const int row = m0 + lr;
+      const bool live = row < e.M;
+      Best best{-INFINITY, 0x7fffffff};
+      if (ok && nk > 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float lo[32], hi[32];
+          tmem_ld32(trow + c, lo);
+          tmem_ld32(trow + BN / 2 + c, hi);
+          epilogue_chunk<T, BN, KIND, 32, false>(e, row, live, lr, n0, c, lo, hi, best,
+                                                 Pre<T, BN, KIND, 4>{}, sbase, BM);
+        }
+        if constexpr (KIND == TI_EPI_ARGMAX) {
+          if (live) {
+            e.aux_val[(int64_t)row * e.ntiles + tile_n] = best.v;
+            e.aux_idx[(int64_t)row * e.ntiles + tile_n] = best.i;
+          }
+        }
+      }
+      store_tile<T, BN, KIND>(e, sbase, BM, n0, m0, ok && nk > 0);
+    } else {
+      // this CTA's fp32 partial tile -> shared memory (zeros for an empty split)
+      float* red = reinterpret_cast<float*>(smem) + (quad * 32 + lane) * C::kRedStride;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        if (ok && nk > 0) {
+          tmem_ld32(trow + c, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(red + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+    }
+  }
+  if constexpr (CL > 1) {
+    static_assert(KIND != TI_EPI_RESIDUAL, "the residual splits K without a cluster");
+    cluster_sync();   // every partial tile of the cluster is in shared memory
+    if (warp >= 2) {
+      float lo[C::kW], hi[C::kW];
+#pragma unroll
+      for (int i = 0; i < C::kW; ++i) lo[i] = hi[i] = 0.f;
+      const uint32_t mine =
+          sbase + (uint32_t)(((int)rank * C::kRows + red_lr) * C::kRedStride + red_c) * 4u;
+#pragma unroll
+      for (int src = 0; src < CL; ++src) {   // fixed order: the sum is deterministic
+        const uint32_t a = map_peer(mine, (uint32_t)src);
+#pragma unroll
+        for (int i = 0; i < C::kW; i += 4) {
+          const float4 x = ld_peer_f4(a + 4u * i);
+          const float4 y = ld_peer_f4(a + 4u * (BN / 2 + i));
+          lo[i] += x.x; lo[i + 1] += x.y; lo[i + 2] += x.z; lo[i + 3] += x.w;
+          hi[i] += y.x; hi[i + 1] += y.y; hi[i + 2] += y.z; hi[i + 3] += y.w;
+        }
+      }
+      Best best{-INFINITY, 0x7fffffff};
+      const uint32_t stage = sbase + C::kStageOff;
+      epilogue_chunk<T, BN, KIND, C::kW, true>(e, red_row, red_live, red_lr, n0, red_c, lo, hi,
+                                               best, pre, stage, C::kRows);
+      if constexpr (KIND == TI_EPI_ARGMAX) {
+#pragma unroll
+        for (int o = CL / 2; o > 0; o >>= 1) {   // the CL threads of a row are adjacent lanes
+          const float v = __shfl_xor_sync(0xffffffffu, best.v, o);
+          const int i = __shfl_xor_sync(0xffffffffu, best.i, o);
+          best.take(v, i);
+        }
+        if (red_live && red_t % CL == 0) {
+          e.aux_val[(int64_t)red_row * e.ntiles + tile_n] = best.v;
+          e.aux_idx[(int64_t)red_row * e.ntiles + tile_n] = best.i;
+        }
+      }
+      store_tile<T, BN, KIND>(e, stage, C::kRows, n0, m0 + (int)rank * C::kRows, ok);
+    }
+    cluster_sync();   // peers have finished reading this CTA's partial tile
   }
   tc_fence_before();
   __syncthreads();
@@ -356,39 +633,39 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
 // ---- host side ----------------------------------------------------------------------------
 struct MapKey {
   const void* p;
-  int64_t rows, cols, ld;
-  int box_rows, dtype;
+  int64_t rows, cols, ld_bytes;
+  int box_cols, box_rows, type;
   bool operator==(const MapKey& o) const {
-    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld &&
-           box_rows == o.box_rows && dtype == o.dtype;
+    return p == o.p && rows == o.rows && cols == o.cols && ld_bytes == o.ld_bytes &&
+           box_cols == o.box_cols && box_rows == o.box_rows && type == o.type;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = std::hash<const void*>()(k.p);
-    h ^= std::hash<int64_t>()(k.rows * 1315423911LL + k.cols * 2654435761LL + k.ld) + 0x9e3779b9 + (h << 6);
-    return h ^ (size_t)(k.box_rows * 131 + k.dtype);
+    h ^= std::hash<int64_t>()(k.rows * 1315423911LL + k.cols * 2654435761LL + k.ld_bytes) +
+         0x9e3779b9 + (h << 6);
+    return h ^ (size_t)(k.box_rows * 131 + k.box_cols * 7 + k.type);
   }
 };
 
-// K-major operand [rows, cols=K] with leading dimension ld elements; box BK x box_rows.
-static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, int64_t ld,
-                       int box_rows, int dtype) {
+// 2-D tile map over a row-major [rows, cols] matrix (row pitch ld_bytes), box box_cols x
+// box_rows with 128-byte rows (SWIZZLE_128B).  Cached per argument set.
+static int tile_map(CUtensorMap* m, const void* p, CUtensorMapDataType type, int64_t rows,
+                    int64_t cols, int64_t ld_bytes, int box_cols, int box_rows) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  MapKey key{p, rows, cols, ld, box_rows, dtype};
+  MapKey key{p, rows, cols, ld_bytes, box_cols, box_rows, (int)type};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) { *m = it->second; return TI_OK; }
   }
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
-  int rc = encode_tensor_map_2d(m, dtype == TI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                const_cast<void*>(p), dims, strides, box, es,
+  int rc = encode_tensor_map_2d(m, type, const_cast<void*>(p), dims, strides, box, es,
                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(mu);
@@ -397,44 +674,120 @@ static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols
   return TI_OK;
 }
 
-template <typename T, int BN, int STAGES, int KIND>
-static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K, int splits,
-                    const EpiArgs& e, cudaStream_t s) {
-  using C = Cfg<BN, STAGES>;
+static CUtensorMapDataType tma_type(int dtype) {
+  return dtype == TI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// K-major operand [rows, K] (leading dimension ld elements): 64 x box_rows boxes.
+static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, int64_t ld,
+                       int box_rows, int dtype) {
+  return tile_map(m, p, tma_type(dtype), rows, cols, ld * 2, BK, box_rows);
+}
+
+template <typename T, int BN, int STAGES, int KIND, int CL>
+static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
+                    const EpiArgs& e, cudaStream_t s, int zsplits = 1) {
+  using C = Cfg<BN, STAGES, CL>;
+  auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
   static int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (set_dev != dev) {
-    cudaError_t err = cudaFuncSetAttribute(gemm_kernel<T, BN, STAGES, KIND>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (err != cudaSuccess) return set_cuda_error(err, "cudaFuncSetAttribute(gemm)");
     set_dev = dev;
   }
   const int nkb = K / BK;
-  const int per = (nkb + splits - 1) / splits;
-  const int z = (nkb + per - 1) / per;   // no empty split
-  dim3 grid(N / BN, (M + BM - 1) / BM, z);
-  gemm_kernel<T, BN, STAGES, KIND><<<grid, kThreads, C::kSmem, s>>>(am, bm, K, per, e);
-  count_launch();
-  cudaError_t err = cudaGetLastError();
-  return err == cudaSuccess ? TI_OK : set_cuda_error(err, "gemm launch");
+  const int zs = CL > 1 ? CL : zsplits;
+  const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
+  dim3 grid(N / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
+  return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, K, per, e);
 }
 
+// How many clusters of CL CTAs of this kernel the GPU keeps resident at once (a cluster needs
+// CL free SMs in one GPC, so this is below 148 / CL); cached per device.
+template <typename T, int BN, int STAGES, int KIND, int CL>
+static int max_clusters() {
+  static int cached_dev = -1, value = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cached_dev != dev) {
+    using C = Cfg<BN, STAGES, CL>;
+    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, CL);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = CL;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = 148 / CL / 2;   // conservative when the query is unavailable
+    }
+    value = n;
+    cached_dev = dev;
+  }
+  return value;
+}
+
+// split-K factor -> cluster size: 1, 2, 4 or 8 (the largest power of two <= split, at most 8)
+static int cluster_for(int split) {
+  return split >= 8 ? 8 : split >= 4 ? 4 : split >= 2 ? 2 : 1;
+}
+constexpr int kMaxResidualSplit = 16;
+
+// Launch with the largest cluster size <= `cl` whose clusters for all `tiles` output tiles are
+// resident at once (a second wave would double the time) and that leaves at least two K blocks
+// per split.
+template <typename T, int BN, int STAGES, int KIND>
+static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
+                       const EpiArgs& e, cudaStream_t s) {
+  if constexpr (KIND == TI_EPI_ARGMAX) {   // argmax tiles are never split
+    return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
+  } else if constexpr (KIND == TI_EPI_RESIDUAL) {
+    // The residual is linear: every K slice adds its partial tile into x on its own (red.add),
+    // no cluster needed.  At most `cl` slices, at least two K blocks each, one wave.
+    const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
+    int z = std::max(1, std::min(cl, K / BK / 2));
+    while (z > 1 && tiles * z > 148) --z;
+    return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s, z);
+  } else {
+    const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
+    const int nkb = K / BK;
+    if (cl >= 8 && nkb >= 16 && tiles <= max_clusters<T, BN, STAGES, KIND, 8>())
+      return launch_t<T, BN, STAGES, KIND, 8>(am, bm, M, N, K, e, s);
+    if (cl >= 4 && nkb >= 8 && tiles <= max_clusters<T, BN, STAGES, KIND, 4>())
+      return launch_t<T, BN, STAGES, KIND, 4>(am, bm, M, N, K, e, s);
+    if (cl >= 2 && nkb >= 4 && tiles <= max_clusters<T, BN, STAGES, KIND, 2>())
+      return launch_t<T, BN, STAGES, KIND, 2>(am, bm, M, N, K, e, s);
+    return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
+  }
+}
+
+// Ring depth per tile width: about 192 KB of loads in flight for the one CTA on the SM.
+template <typename T, int KIND>
+static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
+                       int K, const EpiArgs& e, cudaStream_t s) {
+  switch (bn) {
+    case 64: return dispatch_cl<T, 64, 8, KIND>(cl, am, bm, M, N, K, e, s);
+    case 128: return dispatch_cl<T, 128, 6, KIND>(cl, am, bm, M, N, K, e, s);
+    case 256: return launch_t<T, 256, 4, KIND, 1>(am, bm, M, N, K, e, s);   // never split
+    default: return set_error(TI_ERR_UNSUPPORTED, "gemm: block_n must be 64, 128 or 256");
+  }
+}
+
+// QKV: as much split-K as keeps one wave.
 template <typename T>
 static int launch_qkv(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                       const EpiArgs& e, cudaStream_t s) {
-  return launch_t<T, 64, 4, TI_EPI_QKV_ROPE>(am, bm, M, N, K, 1, e, s);
-}
-
-template <typename T, int KIND>
-static int dispatch_bn(int bn, const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
-                       int splits, const EpiArgs& e, cudaStream_t s) {
-  switch (bn) {
-    case 64: return launch_t<T, 64, 4, KIND>(am, bm, M, N, K, splits, e, s);
-    case 128: return launch_t<T, 128, 3, KIND>(am, bm, M, N, K, splits, e, s);
-    case 256: return launch_t<T, 256, 3, KIND>(am, bm, M, N, K, splits, e, s);
-    default: return set_error(TI_ERR_UNSUPPORTED, "gemm: block_n must be 64, 128 or 256");
-  }
+  return dispatch_cl<T, 64, 8, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
 }
 
 }  // namespace gemm
@@ -457,9 +810,10 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
     return set_error(TI_ERR_UNSUPPORTED, "gemm: N must be a multiple of block_n and K of 64");
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15 || (lda % 8) || (ldb % 8))
     return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: operands must be 16-byte aligned with ld % 8 == 0");
-  if (split_k <= 0) split_k = 1;
-  if (split_k > 1 && epilogue != TI_EPI_RESIDUAL)
-    return set_error(TI_ERR_UNSUPPORTED, "gemm: split-K only with the residual epilogue");
+  const int cl = epilogue == TI_EPI_RESIDUAL ? std::max(1, std::min(split_k, gemm::kMaxResidualSplit))
+                                             : gemm::cluster_for(split_k);
+  if (cl > 1 && epilogue == TI_EPI_ARGMAX)
+    return set_error(TI_ERR_UNSUPPORTED, "gemm: no split-K with the argmax epilogue");
   if (epilogue == TI_EPI_ARGMAX && (!aux_val || !aux_idx))
     return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: argmax epilogue needs aux_val / aux_idx");
   if (epilogue != TI_EPI_ARGMAX && !out)
@@ -478,14 +832,14 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
   if (rc) return rc;
   gemm::EpiArgs e{};
   e.out = out; e.ldo = ldo; e.bias = bias; e.aux_val = aux_val; e.aux_idx = aux_idx;
-  e.M = M; e.N = N; e.ntiles = N / block_n; e.atomic = split_k > 1 ? 1 : 0;
+  e.M = M; e.N = N; e.ntiles = N / block_n;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 #define TI_GEMM_KIND(T)                                                                       \
   switch (epilogue) {                                                                         \
-    case TI_EPI_STORE: return gemm::dispatch_bn<T, TI_EPI_STORE>(block_n, am, bm, M, N, K, split_k, e, s); \
-    case TI_EPI_SWIGLU: return gemm::dispatch_bn<T, TI_EPI_SWIGLU>(block_n, am, bm, M, N, K, split_k, e, s); \
-    case TI_EPI_RESIDUAL: return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, am, bm, M, N, K, split_k, e, s); \
-    case TI_EPI_ARGMAX: return gemm::dispatch_bn<T, TI_EPI_ARGMAX>(block_n, am, bm, M, N, K, split_k, e, s); \
+    case TI_EPI_STORE: return gemm::dispatch_bn<T, TI_EPI_STORE>(block_n, cl, am, bm, M, N, K, e, s); \
+    case TI_EPI_SWIGLU: return gemm::dispatch_bn<T, TI_EPI_SWIGLU>(block_n, cl, am, bm, M, N, K, e, s); \
+    case TI_EPI_RESIDUAL: return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, cl, am, bm, M, N, K, e, s); \
+    case TI_EPI_ARGMAX: return gemm::dispatch_bn<T, TI_EPI_ARGMAX>(block_n, 1, am, bm, M, N, K, e, s); \
     default: return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue");             \
   }
   if (dtype == TI_DTYPE_BF16) { TI_GEMM_KIND(__nv_bfloat16) }

@@ -78,6 +78,8 @@ template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads)
 decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
               Params p) {
+  pdl_wait();
+  pdl_launch_dependents();
   using S = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -406,11 +408,8 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
     attr_dev = dev;
   }
   dim3 grid(p.max_parts, p.num_kv_heads, batch);
-  decode_kernel<T, HD><<<grid, kThreads, S::kTotal, stream>>>(km, vm, p);
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error(e, "paged attention launch");
-  return TI_OK;
+  return launch_kernel("paged attention launch", decode_kernel<T, HD>, grid, dim3(kThreads),
+                       S::kTotal, stream, 1, km, vm, p);
 }
 
 
@@ -681,6 +680,8 @@ template <typename T, int HP>
 __global__ void __launch_bounds__(CfgV2<HP>::kWarps * 32, 1)
 decode_kernel_v2(const __grid_constant__ CUtensorMap kmap,
                  const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  pdl_wait();
+  pdl_launch_dependents();
   using C = CfgV2<HP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -912,51 +913,6 @@ decode_kernel_v2(const __grid_constant__ CUtensorMap kmap,
   }
 }
 
-// ==========================================================================================
-// v3: persistent, load-balanced, warp-specialised kernel (head_dim 64)
-//
-// Same work split as v2 (the whole batch's KV blocks as one stream, an equal chunk per compute
-// warp, split-K only where a unit is cut), but each CTA has one producer warp and kV3Consumers
-// compute warps.  In the prologue the CTA resolves every position of its range of the stream
-// to a pool block id and a valid-token count (shared memory, no global metadata loads after
-// that); the producer then keeps every consumer's 2-stage ring full with TMA loads, and the
-// consumers only wait, compute and finish pieces.  Both walk the same position sequence
-// (skipping the rest of a unit after a negative block-table entry), so no per-block
-// descriptors are exchanged.
-// ==========================================================================================
-constexpr int kV3Consumers = 8;
-constexpr int kV3Stages = 3;
-constexpr int kV3IdCap = 2048;                             // stream positions per CTA
-
-template <int HP>
-struct CfgV3 {
-  static constexpr int kTile = HP * kBlock * 64 * 2;
-  static constexpr int kStage = 2 * kTile;
-  static constexpr int kRing = kV3Consumers * kV3Stages * kStage;        // 128 KB with HP = 2
-  static constexpr int kBars = 2 * kV3Consumers * kV3Stages * 8;
-  static constexpr int kIds = kV3IdCap * 4;
-  static constexpr int kVtok = kV3IdCap;
-  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
-  static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
-  static_assert(kTotal <= 227 * 1024, "v3 shared memory");
-};
-
-// Sequence of stream positions a consumer handles: [pos, end), skipping the remainder of a unit
-// once a position's block id is negative.  Shared by producer and consumer.
-struct V3Walk {
-  int pos, end;
-  __device__ __forceinline__ int unit_end(const int* s_off, int batch, int kvu, int p) const {
-    int lo = 0, hi = batch;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (s_off[mid] <= p) lo = mid; else hi = mid;
-    }
-    const int nb = (s_off[lo + 1] - s_off[lo]) / kvu;
-    const int unit = (p - s_off[lo]) / nb;
-    return s_off[lo] + (unit + 1) * nb;
-  }
-};
-
 // One KV block of ONE kv head with the tokens as the MMA M dimension and the (<= 8) query heads
 // of its GQA group as N: S^T[16 tokens x 8 heads] = K . Q^T (4 MMAs over head_dim 64), online
 // softmax per head (column), O^T[64 dims x 8 heads] += V^T . P^T (4 MMAs; with bf16 P split into
@@ -1051,261 +1007,6 @@ __device__ __forceinline__ void swapped_block(uint32_t kb, uint32_t vb, uint8_t*
   }
 }
 
-template <typename T, int HP>
-__global__ void __launch_bounds__((kV3Consumers + 1) * 32, 1)
-decode_kernel_v3(const __grid_constant__ CUtensorMap kmap,
-                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
-  using C = CfgV3<HP>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  const uint32_t full_all = smem_u32(smem + C::kRing);
-  const uint32_t empty_all = full_all + kV3Consumers * kV3Stages * 8;
-  int* ids = reinterpret_cast<int*>(smem + C::kRing + C::kBars);
-  uint8_t* vtok = smem + C::kRing + C::kBars + C::kIds;
-  int* s_off = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kIds + C::kVtok);
-  constexpr int kThreads = (kV3Consumers + 1) * 32;
-  __shared__ int s_wsum[kV3Consumers + 1];
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int KVH = p.num_kv_heads;
-  const int KVU = KVH / HP;
-  auto nblk_of = [&](int r) {
-    const int ctx = p.context_lens[r];
-    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
-  };
-
-  // ---- prefix sum of KVU * blocks per sequence
-  const int per = (batch + kThreads - 1) / kThreads;
-  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
-  int local = 0;
-  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) s_wsum[warp] = incl;
-  if (tid < 2 * kV3Consumers * kV3Stages) {
-    mbar_init(full_all + 8 * tid, 1);          // full and empty barriers are contiguous
-    fence_mbar_init();
-  }
-  __syncthreads();
-  int run = incl - local;
-  for (int w = 0; w < warp; ++w) run += s_wsum[w];
-  for (int r = r0; r < r1; ++r) {
-    s_off[r] = run;
-    run += KVU * nblk_of(r);
-  }
-  if (tid == 0) {
-    int tot = 0;
-    for (int w = 0; w <= kV3Consumers; ++w) tot += s_wsum[w];
-    s_off[batch] = tot;
-  }
-  __syncthreads();
-  const int total = s_off[batch];
-  const int W = gridDim.x * kV3Consumers;
-  const int chunk = v2_chunk(total, W, p.max_blocks);
-  const int cb = blockIdx.x * kV3Consumers * chunk;
-  if (cb >= total) return;
-  const int ce = min(total, cb + kV3Consumers * chunk);
-
-  // ---- resolve the CTA's positions: block id (-1 = stop) and valid tokens
-  for (int q = tid; q < ce - cb; q += kThreads) {
-    const int pos = cb + q;
-    int lo = 0, hi = batch;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (s_off[mid] <= pos) lo = mid; else hi = mid;
-    }
-    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
-    const int rel = pos - s_off[lo];
-    const int unit = rel / nb, j = rel - unit * nb;
-    const int brow = p.row_index ? p.row_index[lo] : lo;
-    const int phys = p.block_tables[(int64_t)brow * p.bt_stride + j];
-    const bool bad = phys < 0 || (int64_t)phys >= p.num_blocks;
-    // the TMA row coordinate of the unit's first kv head in this block, or -1 (stop)
-    ids[q] = bad ? -1 : (phys * KVH + unit * HP) * kBlock;
-    vtok[q] = (uint8_t)min(kBlock, p.context_lens[lo] - j * kBlock);
-  }
-  __syncthreads();
-
-  if (warp == kV3Consumers) {
-    // ================= producer =================
-    if (lane != 0) return;
-    const uint64_t pol = l2_policy_evict_first();
-    int pos[kV3Consumers], endp[kV3Consumers], cnt[kV3Consumers];
-    uint32_t ephase = 0;
-#pragma unroll
-    for (int c = 0; c < kV3Consumers; ++c) {
-      pos[c] = min(ce, cb + c * chunk);
-      endp[c] = min(ce, pos[c] + chunk);
-      cnt[c] = 0;
-    }
-    V3Walk wk{0, 0};
-    const long long t0 = clock64();
-    while (true) {
-      bool any = false, progress = false;
-#pragma unroll
-      for (int c = 0; c < kV3Consumers; ++c) {
-        // skip positions after a stop, then issue while the ring has room
-        while (pos[c] < endp[c] && ids[pos[c] - cb] < 0) {
-          // the stop position itself is not read; neither is the rest of its unit
-          pos[c] = min(endp[c], wk.unit_end(s_off, batch, KVU, pos[c]));
-        }
-        if (pos[c] >= endp[c]) continue;
-        any = true;
-        // fill every free stage of this consumer
-        while (pos[c] < endp[c]) {
-          const int y = ids[pos[c] - cb];
-          if (y < 0) break;                       // a stop: skipped on the next pass
-          const int st = cnt[c] % kV3Stages;
-          const int slot = c * kV3Stages + st;
-          if (cnt[c] >= kV3Stages) {
-            if (!mbar_test_wait(empty_all + 8 * slot, (ephase >> slot) & 1u)) break;
-            ephase ^= 1u << slot;
-          }
-          const uint32_t dst = smem_u32(smem + slot * C::kStage);
-          // the consumer's generic-proxy reads / zero-fill of this stage precede the TMA write
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mbar_arrive_expect_tx(full_all + 8 * slot, C::kStage);
-          tma_load_2d_hint(dst, &kmap, full_all + 8 * slot, 0, y, pol);
-          tma_load_2d_hint(dst + C::kTile, &vmap, full_all + 8 * slot, 0, y, pol);
-          ++cnt[c];
-          ++pos[c];
-          progress = true;
-        }
-      }
-      if (!any) break;
-      if (!progress) {
-        if (clock64() - t0 > kWaitCycles) { raise_device_error(TI_DEVERR_ATTN_WAIT); break; }
-        __nanosleep(64);
-      }
-    }
-    return;
-  }
-
-  // ================= consumers =================
-  const int c = warp;
-  int pos = min(ce, cb + c * chunk);
-  const int end = min(ce, pos + chunk);
-  if (pos >= end) return;
-  const int G = p.group;                       // <= 8: the MMA N dimension
-  const int NHU = HP * G;
-  const int g = lane >> 2, t4 = lane & 3;
-  uint32_t fphase = 0;
-  int cnt = 0;
-  uint32_t qb[HP][4][2];
-  float m[HP][2], l[HP][2], o[HP][4][4];
-
-  while (pos < end) {
-    // ---- a piece: positions of one unit inside [pos, end)
-    int lo = 0, hi = batch;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (s_off[mid] <= pos) lo = mid; else hi = mid;
-    }
-    const int row = lo;
-    const int nb = (s_off[row + 1] - s_off[row]) / KVU;
-    const int unit = (pos - s_off[row]) / nb;
-    const int pstart = s_off[row] + unit * nb;
-    const int pend = min(end, pstart + nb);
-    const int piece = pos / chunk - pstart / chunk;
-    const int pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
-    {
-      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride;
-#pragma unroll
-      for (int sub = 0; sub < HP; ++sub) {
-        const T* qh = qrow + (int64_t)((unit * HP + sub) * G + g) * 64;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          qb[sub][ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t4) : 0u;
-          qb[sub][ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t4) : 0u;
-        }
-        m[sub][0] = m[sub][1] = -INFINITY;
-        l[sub][0] = l[sub][1] = 0.f;
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) o[sub][mt][0] = o[sub][mt][1] = o[sub][mt][2] = o[sub][mt][3] = 0.f;
-      }
-    }
-    int stop = 0;
-    for (; pos < pend; ++pos) {
-      if (ids[pos - cb] < 0) { stop = 1; pos = pend; break; }
-      const int st = cnt % kV3Stages;
-      const int slot = c * kV3Stages + st;
-      if (!mbar_wait(full_all + 8 * slot, (fphase >> slot) & 1u, TI_DEVERR_ATTN_WAIT)) return;
-      fphase ^= 1u << slot;
-      uint8_t* kt = smem + slot * C::kStage;
-      const int valid = vtok[pos - cb];
-#pragma unroll
-      for (int sub = 0; sub < HP; ++sub) {
-        uint8_t* ks_ = kt + sub * kBlock * 128;
-        uint8_t* vs_ = kt + C::kTile + sub * kBlock * 128;
-        swapped_block<T>(smem_u32(ks_), smem_u32(vs_), vs_, valid, lane, qb[sub], p.scale_log2,
-                         m[sub], l[sub], o[sub]);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_all + 8 * slot);
-      ++cnt;
-    }
-    // ---- finish the piece: lane holds heads (2t4, 2t4+1) x dims (16mt+g, 16mt+g+8)
-    T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
-    const int64_t pair = (int64_t)row * KVU + unit;
-#pragma unroll
-    for (int sub = 0; sub < HP; ++sub) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1)
-          l[sub][j] += __shfl_xor_sync(0xffffffffu, l[sub][j], off);
-    }
-    if (pieces == 1) {
-#pragma unroll
-      for (int sub = 0; sub < HP; ++sub)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int hl = 2 * t4 + j;
-          if (hl >= G) continue;
-          const float inv = 1.f / l[sub][j];           // l == 0 -> NaN (attention.cu:150)
-          T* oh = outp + (int64_t)((unit * HP + sub) * G + hl) * 64;
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            oh[mt * 16 + g] = Elem<T>::from_f(o[sub][mt][j] * inv);
-            oh[mt * 16 + g + 8] = Elem<T>::from_f(o[sub][mt][2 + j] * inv);
-          }
-        }
-    } else {
-#pragma unroll
-      for (int sub = 0; sub < HP; ++sub)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int hl = 2 * t4 + j;
-          if (hl >= G) continue;
-          const int64_t sl = ((int64_t)row * p.num_heads + (unit * HP + sub) * G + hl) * p.max_parts + piece;
-          float* wo = p.ws_o + sl * 64;
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            wo[mt * 16 + g] = o[sub][mt][j];
-            wo[mt * 16 + g + 8] = o[sub][mt][2 + j];
-          }
-          if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[sub][j], l[sub][j]);
-        }
-      if (lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = atomicAdd(&p.ws_count[pair], 1) == pieces - 1;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        v2_merge<T>(p, row, unit, NHU, pieces, lane, outp);
-        if (lane == 0) p.ws_count[pair] = 0;     // ready for the next launch
-      }
-    }
-  }
-}
-
 // ==========================================================================================
 // v4: persistent, load-balanced, self-issuing kernel (head_dim 64, GQA groups <= 8)
 //
@@ -1339,6 +1040,8 @@ template <typename T, int HP>
 __global__ void __launch_bounds__(kV4Warps * 32, 1)
 decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
                  const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  pdl_wait();
+  pdl_launch_dependents();
   using C = CfgV4<HP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1574,34 +1277,8 @@ static int launch_v4(const Params& p, const CUtensorMap& km, const CUtensorMap& 
     if (sms <= 0) sms = 148;
     set_dev = dev;
   }
-  decode_kernel_v4<T, HP><<<sms, kV4Warps * 32, C::kTotal, stream>>>(km, vm, p, batch);
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v4 launch");
-  return TI_OK;
-}
-
-template <typename T, int HP>
-static int launch_v3(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
-                     cudaStream_t stream) {
-  using C = CfgV3<HP>;
-  static int set_dev = -1;
-  static int sms = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (set_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v3<T, HP>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v3)");
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-    set_dev = dev;
-  }
-  decode_kernel_v3<T, HP><<<sms, (kV3Consumers + 1) * 32, C::kTotal, stream>>>(km, vm, p, batch);
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v3 launch");
-  return TI_OK;
+  return launch_kernel("paged attention v4 launch", decode_kernel_v4<T, HP>, dim3(sms),
+                       dim3(kV4Warps * 32), C::kTotal, stream, 1, km, vm, p, batch);
 }
 
 template <typename T, int HP>
@@ -1620,11 +1297,8 @@ static int launch_v2(const Params& p, const CUtensorMap& km, const CUtensorMap& 
     if (sms <= 0) sms = 148;
     set_dev = dev;
   }
-  decode_kernel_v2<T, HP><<<sms, C::kWarps * 32, C::kTotal, stream>>>(km, vm, p, batch);
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error(e, "paged attention v2 launch");
-  return TI_OK;
+  return launch_kernel("paged attention v2 launch", decode_kernel_v2<T, HP>, dim3(sms),
+                       dim3(C::kWarps * 32), C::kTotal, stream, 1, km, vm, p, batch);
 }
 
 // Partition size (KV blocks per split-K CTA of the v1 kernel) used when the caller passes 0.
@@ -1724,7 +1398,7 @@ extern "C" int ti_paged_attention_decode(
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (v2) {
-    // v3 needs its CTA's whole stream range in shared memory: check the worst case here
+    // v4 needs its CTA's whole stream range in shared memory: check the worst case here
     static int sms = 0;
     if (!sms) {
       int dev = 0;

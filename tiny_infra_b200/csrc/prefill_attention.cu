@@ -49,6 +49,8 @@ struct Smem {
 template <typename T, int HD>
 __global__ void prefill_kernel(const __grid_constant__ CUtensorMap kmap,
                                const __grid_constant__ CUtensorMap vmap, Params p) {
+  pdl_wait();
+  pdl_launch_dependents();
   using S = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -226,10 +228,8 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
     set_dev = dev;
   }
   dim3 grid(num_tiles, p.num_kv_heads);
-  prefill_kernel<T, HD><<<grid, (p.group + 1) * 32, Smem<HD>::kTotal, s>>>(km, vm, p);
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TI_OK : set_cuda_error(e, "prefill attention launch");
+  return launch_kernel("prefill attention launch", prefill_kernel<T, HD>, grid,
+                       dim3((p.group + 1) * 32), Smem<HD>::kTotal, s, 1, km, vm, p);
 }
 
 }  // namespace prefill

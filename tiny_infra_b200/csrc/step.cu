@@ -26,6 +26,8 @@ __global__ void decode_prepare_kernel(const int32_t* __restrict__ tokens,
                                       int64_t* __restrict__ slot_mapping,
                                       int32_t* __restrict__ ctx_lens, float* __restrict__ hidden,
                                       const T* __restrict__ embed, int H, int64_t V, int rows) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int r = blockIdx.x;
   if (r >= rows) return;
   const int slot = slots[r];
@@ -75,6 +77,8 @@ __global__ void decode_prepare_kernel(const int32_t* __restrict__ tokens,
 __global__ void argmax_finish_kernel(const float* __restrict__ val, const int32_t* __restrict__ idx,
                                      int ntiles, int rows, int32_t* __restrict__ out_tokens,
                                      const int32_t* __restrict__ slots, int32_t* seq_len, int inc) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -106,6 +110,8 @@ __global__ void kv_scatter_kernel(T* k_cache, T* v_cache, const T* __restrict__ 
                                   const T* __restrict__ v, int64_t v_tok_stride,
                                   int64_t v_head_stride, const int64_t* __restrict__ slots,
                                   int tokens, int KVH, int HD, int bs) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int per = KVH * (HD / 8);
   const int64_t total = (int64_t)tokens * per;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -121,12 +127,6 @@ __global__ void kv_scatter_kernel(T* k_cache, T* v_cache, const T* __restrict__ 
     *reinterpret_cast<uint4*>(v_cache + dst) =
         *reinterpret_cast<const uint4*>(v + t * v_tok_stride + h * v_head_stride + d);
   }
-}
-
-static int finish(const char* what) {
-  count_launch();
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TI_OK : set_cuda_error(e, what);
 }
 
 }  // namespace step
@@ -148,16 +148,17 @@ extern "C" int ti_decode_prepare(const int32_t* tokens, const int32_t* slots,
   if (hidden_size % 8) return set_error(TI_ERR_UNSUPPORTED, "decode_prepare: hidden % 8 != 0");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    step::decode_prepare_kernel<__nv_bfloat16><<<rows, 128, 0, s>>>(
+    return launch_kernel("decode_prepare launch", step::decode_prepare_kernel<__nv_bfloat16>,
+                         dim3(rows), dim3(128), 0, s, 1,
         tokens, slots, new_block, seq_len, block_tables, bt_stride, block_size, positions,
         slot_mapping, ctx_lens, hidden, (const __nv_bfloat16*)embed, hidden_size, vocab, rows);
   else if (dtype == TI_DTYPE_FP16)
-    step::decode_prepare_kernel<__half><<<rows, 128, 0, s>>>(
+    return launch_kernel("decode_prepare launch", step::decode_prepare_kernel<__half>,
+                         dim3(rows), dim3(128), 0, s, 1,
         tokens, slots, new_block, seq_len, block_tables, bt_stride, block_size, positions,
         slot_mapping, ctx_lens, hidden, (const __half*)embed, hidden_size, vocab, rows);
   else
     return set_error(TI_ERR_UNSUPPORTED, "decode_prepare: dtype must be bf16 or fp16");
-  return step::finish("decode_prepare launch");
 }
 
 extern "C" int ti_argmax_finish(const float* part_val, const int32_t* part_idx, int ntiles,
@@ -169,9 +170,9 @@ extern "C" int ti_argmax_finish(const float* part_val, const int32_t* part_idx, 
     return set_error(TI_ERR_INVALID_ARGUMENT, "argmax_finish: bad arguments");
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
-  step::argmax_finish_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  return launch_kernel("argmax_finish launch", step::argmax_finish_kernel,
+                       dim3(blocks), dim3(threads), 0, reinterpret_cast<cudaStream_t>(stream), 1,
       part_val, part_idx, ntiles, rows, out_tokens, slots, seq_len, seq_inc);
-  return step::finish("argmax_finish launch");
 }
 
 extern "C" int ti_kv_scatter(void* k_cache, void* v_cache, const void* k, int64_t k_tok_stride,
@@ -190,16 +191,17 @@ extern "C" int ti_kv_scatter(void* k_cache, void* v_cache, const void* k, int64_
   const int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 16);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
-    step::kv_scatter_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+    return launch_kernel("kv_scatter launch", step::kv_scatter_kernel<__nv_bfloat16>,
+                         dim3(blocks), dim3(256), 0, s, 1,
         (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (const __nv_bfloat16*)k, k_tok_stride,
         k_head_stride, (const __nv_bfloat16*)v, v_tok_stride, v_head_stride, slot_mapping,
         num_tokens, num_kv_heads, head_dim, block_size);
   else if (dtype == TI_DTYPE_FP16)
-    step::kv_scatter_kernel<__half><<<blocks, 256, 0, s>>>(
+    return launch_kernel("kv_scatter launch", step::kv_scatter_kernel<__half>,
+                         dim3(blocks), dim3(256), 0, s, 1,
         (__half*)k_cache, (__half*)v_cache, (const __half*)k, k_tok_stride, k_head_stride,
         (const __half*)v, v_tok_stride, v_head_stride, slot_mapping, num_tokens, num_kv_heads,
         head_dim, block_size);
   else
     return set_error(TI_ERR_UNSUPPORTED, "kv_scatter: dtype must be bf16 or fp16");
-  return step::finish("kv_scatter launch");
 }

@@ -24,8 +24,10 @@ import torch
 from . import _native as N
 from .config import QwenConfig
 
-GATE_UP_TILE = 128          # block_n of the gate/up GEMM: 64 gate rows then 64 up rows
+GATE_UP_TILE = 256          # block_n of the gate/up GEMM: 128 gate rows then 128 up rows
 LM_TILE = 128               # block_n of the lm_head GEMM (argmax partials per 128 columns)
+O_TILE = 64                 # block_n of the o_proj GEMM (+residual, split-K)
+DOWN_TILE = 128             # block_n of the down_proj GEMM (+residual, split-K)
 
 
 def _ptr(t: torch.Tensor | None):
@@ -209,10 +211,10 @@ class Qwen2ForCausalLM:
         return owner
 
     @staticmethod
-    def _splits(rows: int, n: int, k: int) -> int:
-        """split-K factor for the residual GEMMs: enough CTAs to cover the SMs once."""
-        tiles = ((rows + 127) // 128) * (n // 64)
-        return int(max(1, min(8, k // 64 // 2, (2 * 148 + tiles - 1) // tiles)))
+    def _splits(k: int) -> int:
+        """Requested split-K factor of a residual projection with reduction length k: up to 16
+        slices of at least two 64-wide K blocks (the library lowers it to fit one wave)."""
+        return int(max(1, min(16, k // 128)))
 
     def _layers(self, pb: PackedBatch, kv_cache, cos: torch.Tensor, sin: torch.Tensor,
                 hidden: torch.Tensor, stream: int, num_layers: int | None = None,
@@ -230,8 +232,8 @@ class Qwen2ForCausalLM:
         if pb.decode and ws is None:
             need = lib.ti_paged_attention_workspace_bytes(pb.num_seqs, NH, KVH, D, maxb, 0)
             ws = self._ws.get(self.device, need)
-        split_o = self._splits(T, H, NH * D)
-        split_d = self._splits(T, H, I)
+        split_o = self._splits(NH * D)
+        split_d = self._splits(I)
         for li in range(c.num_layers if num_layers is None else num_layers):
             kc, vc = kv_cache.key_cache[li], kv_cache.value_cache[li]
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
@@ -255,15 +257,15 @@ class Qwen2ForCausalLM:
                     pb.tile_seq.numel(), NH, KVH, D, kv_cache.block_size, dt, stream))
             N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
                                 NH * D, T, H, NH * D, hidden.data_ptr(), H, None, None, None, dt,
-                                64, split_o, stream))
+                                O_TILE, split_o, stream))
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
                                    W[f"{li}.ln2"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
             N.check(lib.ti_gemm(N.TI_EPI_SWIGLU, xn.data_ptr(), H, W[f"{li}.gate_up"].data_ptr(),
                                 H, T, 2 * I, H, act.data_ptr(), I, None, None, None, dt,
                                 GATE_UP_TILE, 1, stream))
             N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
-                                I, T, H, I, hidden.data_ptr(), H, None, None, None, dt, 64,
-                                split_d, stream))
+                                I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
+                                DOWN_TILE, split_d, stream))
 
     def _final_norm(self, hidden_rows: torch.Tensor, stream: int) -> torch.Tensor:
         c = self.config
