@@ -72,6 +72,7 @@ struct Params {
   float* ws_ml;             // [B, NH, max_parts, 2]
   int32_t* ws_stop;         // [B, KVH, max_parts]
   int32_t* ws_count;        // [B, KVH]
+  int32_t* ws_pieces;       // [B, KVH] v4: pieces of each unit (written by its first piece)
 };
 
 template <typename T, int HD>
@@ -631,17 +632,33 @@ __device__ __forceinline__ void v2_merge(const Params& p, int row, int unit, int
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0.f;
     float L = 0.f;
+    float f[kV2MaxPieces];
 #pragma unroll
     for (int q = 0; q < kV2MaxPieces; ++q) {
-      if (q < use && live) {
-        const float f = (mq[q] == -INFINITY) ? 0.f : fast_exp2(mq[q] - M);
-        L += lq[q] * f;
-        const float4* src = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64 + half * 32);
+      f[q] = (q < use && live && mq[q] != -INFINITY) ? fast_exp2(mq[q] - M) : 0.f;
+      L += lq[q] * f[q];
+    }
+    // two pieces per round: their 16 loads are in flight together (the merge sits on the
+    // kernel's critical tail, so its L2 round trips are what it costs)
+#pragma unroll
+    for (int q = 0; q < kV2MaxPieces; q += 2) {
+      if (q < use) {
+        const bool two = q + 1 < use && q + 1 < kV2MaxPieces;
+        float4 va[8], vb[8];
+        const float4* s0 = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64 + half * 32);
+        const float4* s1 = s0 + 16;   // the next piece's slot of this head (64 floats later)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 v = __ldcg(src + i);
-          acc[4 * i] += f * v.x; acc[4 * i + 1] += f * v.y;
-          acc[4 * i + 2] += f * v.z; acc[4 * i + 3] += f * v.w;
+          va[i] = live ? __ldcg(s0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          vb[i] = (live && two) ? __ldcg(s1 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float f0 = f[q], f1 = two ? f[q + 1 < kV2MaxPieces ? q + 1 : q] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          acc[4 * i] += f0 * va[i].x + f1 * vb[i].x;
+          acc[4 * i + 1] += f0 * va[i].y + f1 * vb[i].y;
+          acc[4 * i + 2] += f0 * va[i].z + f1 * vb[i].z;
+          acc[4 * i + 3] += f0 * va[i].w + f1 * vb[i].w;
         }
       }
     }
@@ -1019,8 +1036,8 @@ __device__ __forceinline__ void swapped_block(uint32_t kb, uint32_t vb, uint8_t*
 // and computes each KV block with tokens as the MMA M dimension and the group's query heads as
 // N (swapped_block).
 // ==========================================================================================
-constexpr int kV4Warps = 8;
-constexpr int kV4Stages = 3;
+constexpr int kV4Warps = 12;
+constexpr int kV4Stages = 2;
 constexpr int kV4IdCap = 2048;
 
 template <int HP>
@@ -1221,6 +1238,7 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1)
           l[sub][j] += __shfl_xor_sync(0xffffffffu, l[sub][j], off);
+    if (piece == 0 && lane == 0) p.ws_pieces[pair] = pieces;   // read by merge_pieces_kernel
     if (pieces == 1) {
 #pragma unroll
       for (int sub = 0; sub < HP; ++sub)
@@ -1253,12 +1271,68 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
           if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[sub][j], l[sub][j]);
         }
       if (lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
-      if (arrive_last(&p.ws_count[pair], pieces, lane)) {
-        v2_merge<T>(p, row, unit, NHU, pieces, lane, outp);
-        if (lane == 0) p.ws_count[pair] = 0;     // ready for the next launch
-      }
     }
   }
+}
+
+// v4 split-K merge: one CTA per (sequence, unit of HP kv heads), one thread per (query head of
+// the unit, 4 dims).  Units that v4 did not split (pieces == 1) or that have no blocks are left
+// as they are.  All of a thread's partials are loaded in one round: this runs right after the
+// attention kernel (programmatic dependent launch) and costs about two L2 round trips.
+template <typename T>
+__global__ void __launch_bounds__(256)
+merge_pieces_kernel(Params p, int units, int nheads) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pair = blockIdx.x;
+  const int row = pair / units, unit = pair % units;
+  if (p.context_lens[row] <= 0) return;   // no blocks: the row is left untouched
+  const int pieces = p.ws_pieces[pair];
+  if (pieces <= 1) return;
+  const int h = threadIdx.x >> 4, d4 = threadIdx.x & 15;
+  if (h >= nheads) return;
+  const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
+  const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
+  int st[kV2MaxPieces];
+  float2 ml[kV2MaxPieces];
+  float4 v[kV2MaxPieces];
+#pragma unroll
+  for (int q = 0; q < kV2MaxPieces; ++q) {
+    if (q < pieces) {
+      st[q] = stops[q];
+      ml[q] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
+      v[q] = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64)[d4];
+    } else {
+      st[q] = 0;
+      ml[q] = make_float2(-INFINITY, 0.f);
+      v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  int use = pieces;                       // up to and including the first piece that stopped
+#pragma unroll
+  for (int q = kV2MaxPieces - 1; q >= 0; --q)
+    if (q < pieces && st[q]) use = q + 1;
+  float M = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kV2MaxPieces; ++q)
+    if (q < use) M = fmaxf(M, ml[q].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < kV2MaxPieces; ++q) {
+    if (q < use) {
+      const float f = ml[q].x == -INFINITY ? 0.f : fast_exp2(ml[q].x - M);
+      L += ml[q].y * f;
+      acc.x += f * v[q].x; acc.y += f * v[q].y; acc.z += f * v[q].z; acc.w += f * v[q].w;
+    }
+  }
+  const float inv = 1.f / L;               // L == 0 -> NaN (attention.cu:150)
+  T* dst = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride +
+           (int64_t)(unit * nheads + h) * 64 + d4 * 4;
+  uint2 u;
+  u.x = Elem<T>::pack2(acc.x * inv, acc.y * inv);
+  u.y = Elem<T>::pack2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(dst) = u;
 }
 
 template <typename T, int HP>
@@ -1277,8 +1351,12 @@ static int launch_v4(const Params& p, const CUtensorMap& km, const CUtensorMap& 
     if (sms <= 0) sms = 148;
     set_dev = dev;
   }
-  return launch_kernel("paged attention v4 launch", decode_kernel_v4<T, HP>, dim3(sms),
-                       dim3(kV4Warps * 32), C::kTotal, stream, 1, km, vm, p, batch);
+  int rc = launch_kernel("paged attention v4 launch", decode_kernel_v4<T, HP>, dim3(sms),
+                         dim3(kV4Warps * 32), C::kTotal, stream, 1, km, vm, p, batch);
+  if (rc) return rc;
+  const int units = p.num_kv_heads / HP;
+  return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
+                       dim3(batch * units), dim3(256), 0, stream, 1, p, units, HP * p.group);
 }
 
 template <typename T, int HP>
@@ -1328,6 +1406,7 @@ extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, i
   bytes += (size_t)slots * head_dim * 4;                        // ws_o
   bytes += (size_t)slots * 2 * 4;                               // ws_ml
   bytes += (size_t)batch * num_kv_heads * parts * 4;            // ws_stop
+  bytes += (size_t)batch * num_kv_heads * 4;                    // ws_pieces
   return bytes + 256;
 }
 
@@ -1387,6 +1466,7 @@ extern "C" int ti_paged_attention_decode(
     p.ws_o = reinterpret_cast<float*>(w); w += slots * head_dim * 4;
     p.ws_ml = reinterpret_cast<float*>(w); w += slots * 2 * 4;
     p.ws_stop = reinterpret_cast<int32_t*>(w);
+    p.ws_pieces = p.ws_stop + (int64_t)batch * num_kv_heads * max_parts;
   }
   const int64_t rows = num_blocks * num_kv_heads * attn::kBlock;
   // two kv heads per MMA tile when both GQA groups fit the 16 rows
