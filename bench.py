@@ -43,7 +43,7 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--kernel", choices=["attention"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "gate_up"], default=None,
                     help="time one kernel alone instead of the decode step")
     ap.add_argument("--case", choices=["256", "config1"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
@@ -213,7 +213,7 @@ def attention_roofline(engine, kv, cfg, ctx, reps, peak_gbs):
     tot = int(lens.sum().item())
     algo = tot * KVH * D * 2 * 2 + 2 * n * NH * D * 2      # K+V of every context token, q, out
     achieved = algo / t / 1e9
-    return {"bound": "hbm", "kernel": "ti::attn::decode_kernel (paged decode attention)",
+    return {"bound": "hbm", "kernel": "attn::decode_kernel_v4 + merge_pieces_kernel (paged decode attention)",
             "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": _traffic_from_profiles(),
             "algorithmic_bytes_per_launch": algo, "us_per_launch": round(t * 1e6, 2)}
@@ -448,9 +448,40 @@ def run_ours(a, rank, world, local):
     return 0
 
 
+def _kernel_line(a, metric_value, t, algo, workload, data, extra_cfg=None):
+    peak, kind = _peaks()
+    gbs = algo / t / 1e9
+    cfg = {"workload": workload, "l2": "inputs larger than L2 (distinct buffers per launch), no flush"}
+    cfg.update(extra_cfg or {})
+    print(json.dumps({
+        "metric": metric_value, "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": data, "config": cfg,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": kind,
+                     "algorithmic_bytes_per_launch": int(algo)}}), flush=True)
+
+
+def _time_launches(fn, n_buffers, steps, warmup):
+    """Average device time of `steps` back-to-back launches cycling over n_buffers inputs."""
+    import torch
+    for i in range(max(warmup, n_buffers)):
+        fn(i % n_buffers)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i % n_buffers)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / steps
+
+
 def run_attention_kernel(a):
-    """Paged decode attention alone: one layer of the 256-sequence workload (ctx U[128,2048])
-    or the 8-sequence op of ctx U[1,512] over a 512-block pool; HBM GB/s of the kernel."""
+    """Paged decode attention alone: the 256-sequence workload (ctx U[128,2048]) or the
+    8-sequence op of ctx U[1,512] over a 512-block pool; HBM GB/s of one layer's launch (the
+    attention kernel and its split-K merge), cycling over 8 layers' pools."""
     import torch
     from tiny_infra_b200 import custom_paged_attn
     dev = torch.device("cuda:0")
@@ -468,39 +499,52 @@ def run_attention_kernel(a):
         n = (int(ctx[b]) + bs - 1) // bs
         bt[b, :n] = perm[off:off + n]
         off += n
+    layers = 8 if a.case == "256" else 64   # > 126 MB of KV either way
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed)
     q = torch.randn(B, NH, D, device=dev, generator=g).to(torch.bfloat16)
-    k = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
-    v = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+    ks = [torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+          for _ in range(layers)]
+    vs = [torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+          for _ in range(layers)]
     out = torch.empty_like(q)
     btt, ct = torch.from_numpy(bt).to(dev), torch.from_numpy(ctx).to(dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > L2 (126 MB)
-    for _ in range(a.warmup):
-        custom_paged_attn.launch_paged_attention(out, q, k, v, btt, ct, bs)
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(a.steps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        custom_paged_attn.launch_paged_attention(out, q, k, v, btt, ct, bs)
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) / 1e3)
-    t = float(np.mean(ts))
+    t = _time_launches(lambda i: custom_paged_attn.launch_paged_attention(
+        out, q, ks[i], vs[i], btt, ct, bs), layers, a.steps, a.warmup)
     algo = int(ctx.sum()) * KVH * D * 2 * 2 + 2 * B * NH * D * 2
-    peak, kind = _peaks()
-    print(json.dumps({
-        "metric": "paged-attn HBM GB/s", "value": round(algo / t / 1e9, 1), "unit": "GB/s",
-        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (N(0,1) q/k/v, random block permutation)",
-        "config": {"workload": f"paged decode attention, {B} seqs, ctx U[{lo},{hi}], 14/2 heads, "
-                               f"D=64, pool {NB} blocks x 16", "l2": "flushed between launches"},
-        "roofline": {"bound": "hbm", "achieved": round(algo / t / 1e9, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(algo / t / 1e9 / peak, 4),
-                     "peak_kind": kind, "algorithmic_bytes_per_launch": algo}}), flush=True)
+    _kernel_line(a, "paged-attn HBM GB/s", t, algo,
+                 f"paged decode attention, {B} seqs, ctx U[{lo},{hi}], 14/2 heads, D=64, "
+                 f"pool {NB} blocks x 16, {layers} layers cycled",
+                 "synthetic (N(0,1) q/k/v, random block permutation)")
+    return 0
+
+
+def run_gate_up_kernel(a):
+    """The decode step's gate/up projection alone (256 tokens x 896 -> 2 x 4864, SwiGLU fused),
+    cycling over 24 layers' weights; GB/s of its algorithmic bytes (weights + activations in,
+    SwiGLU output)."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    from tiny_infra_b200.qwen2 import GATE_UP_TILE
+    dev = torch.device("cuda:0")
+    M, H, I, L = SEQS, 896, 4864, 24
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    x = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    ws = [(torch.randn(2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+          for _ in range(L)]
+    act = torch.empty(M, I, device=dev, dtype=torch.bfloat16)
+    lib = N.lib()
+
+    def launch(i):
+        N.check(lib.ti_gemm(N.TI_EPI_SWIGLU, x.data_ptr(), H, ws[i].data_ptr(), H, M, 2 * I, H,
+                            act.data_ptr(), I, None, None, None, N.TI_DTYPE_BF16, GATE_UP_TILE, 1,
+                            torch.cuda.current_stream().cuda_stream))
+    t = _time_launches(launch, L, a.steps, a.warmup)
+    algo = 2 * I * H * 2 + M * H * 2 + M * I * 2
+    _kernel_line(a, "gate_up GEMM HBM GB/s", t, algo,
+                 f"gate/up projection + SwiGLU, M={M}, N={2 * I}, K={H}, block_n {GATE_UP_TILE}, "
+                 f"{L} layers' weights cycled", "synthetic (N(0,1) activations, N(0,0.02) weights)")
     return 0
 
 
@@ -509,6 +553,8 @@ def main():
     rank, world, local = _dist()
     if a.kernel == "attention":
         return run_attention_kernel(a) if rank == 0 else 0
+    if a.kernel == "gate_up":
+        return run_gate_up_kernel(a) if rank == 0 else 0
     if a.impl == "reference":
         return run_reference(a, rank, world)
     return run_ours(a, rank, world, local)
