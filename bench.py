@@ -381,7 +381,7 @@ def run_ours(a, rank, world, local):
         t = torch.tensor([secs], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         secs = float(t.item())
-    launches = engine.launches_per_step.get(rows, 0) * a.steps
+    launches = engine.launches_per_step.get((rows, False), 0) * a.steps
     value = world * SEQS * a.steps / secs
 
     # ---- e2e through the public per-step API (host tokens in/out) ----

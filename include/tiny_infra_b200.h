@@ -199,6 +199,23 @@ int ti_paged_prefill_attention(void* out, int64_t out_tok_stride, const void* q,
                                int num_kv_heads, int head_dim, int block_size, int dtype,
                                void* stream);
 
+/* ---- sampler: temperature / top-k / top-p / draw ----------------------------------------------
+ * Replaces ContinuousBatcher._sample_next_token (engine/scheduler.py:104-156) for `rows` rows of
+ * logits [rows, vocab] (leading dimension ld elements, dtype bf16 / fp16 / fp32).  Per row r:
+ * x = logits[r] / temperatures[r] (temperature 0: the result is the first argmax);
+ * cut_ks[r] > 0 keeps x >= the cut_ks[r]-th largest value (0: no cut); top_ps[r] < 1 keeps the
+ * descending order up to and including the first token whose cumulative softmax probability
+ * exceeds top_ps[r] (>= 1: no cut); the token is the first kept one in descending order (ties:
+ * lower index first) whose cumulative probability exceeds uniforms[r] in [0, 1).
+ * The reference's batch-level rules (top-k only in rows whose top_k equals the batch's largest
+ * one, :119-130; top-p in every row once any row has p < 1, :133-134) are applied by the caller
+ * when it fills cut_ks / top_ps.  out_tokens[r] receives the token; when slots / seq_len are not
+ * NULL, seq_len[slots[r]] += seq_inc for slots[r] >= 0. */
+int ti_sample(const void* logits, int64_t ld, int dtype, int rows, int vocab,
+              const float* temperatures, const int32_t* cut_ks, const float* top_ps,
+              const float* uniforms, int32_t* out_tokens, const int32_t* slots, int32_t* seq_len,
+              int seq_inc, void* stream);
+
 /* ---- decode-step packing on the device ---------------------------------------------
  * For rows r < rows: slot = slots[r] (-1 = padding row).  First writes this step's new block,
  * block_tables[slot][seq_len[slot] / block_size] = new_block[r] when new_block[r] >= 0 (the

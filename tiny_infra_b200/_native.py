@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple] = {
     "ti_kv_scatter": (I32, [P, P, P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P]),
     "ti_gemm_qkv_rope": (I32, [P, I64, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P,
                                P, I32, I32, P]),
+    "ti_sample": (I32, [P, I64, I32, I32, I32, P, P, P, P, P, P, P, I32, P]),
 }
 
 TI_EPI_STORE, TI_EPI_SWIGLU, TI_EPI_RESIDUAL, TI_EPI_ARGMAX = 0, 1, 2, 3

@@ -42,6 +42,95 @@ class FreeBlockList(collections.deque):
         return list(self) == list(other)
 
 
+class BlockAllocator:
+    """Host side of the paged pool: the FIFO free list, per-slot lengths and block tables, and
+    the reference's allocation order (engine/cache_manager.py:51-120) -- no device state, so
+    schedulers and tests can plan on it anywhere.  ``KVCacheManager`` owns one and mirrors its
+    tables to the device."""
+
+    def __init__(self, max_batch_size: int, max_seq_len: int, block_size: int = 16,
+                 num_blocks: int | None = None) -> None:
+        self.max_batch_size = max_batch_size
+        self.max_seq_len = max_seq_len
+        self.block_size = block_size
+        self.max_blocks_per_seq = (max_seq_len + block_size - 1) // block_size      # :25
+        self.total_physical_blocks = (max_batch_size * self.max_blocks_per_seq        # :26
+                                      if num_blocks is None else int(num_blocks))
+        self.free_blocks = FreeBlockList(range(self.total_physical_blocks))
+        self.seq_len = np.zeros(max_batch_size, np.int32)
+        self.block_tables = np.full((max_batch_size, self.max_blocks_per_seq), -1, np.int32)
+
+    def plan_tokens(self, slots, counts, *, strict_len: bool = True):
+        """Allocate blocks for ``counts[i]`` new tokens of each slot, in the reference's order
+        (slot by slot, token by token, cache_manager.py:73-92).
+
+        Returns (slot_mapping int64 [sum(counts)], updates list of (slot, logical, phys)).
+        Raises ValueError / RuntimeError like the reference; on error the blocks allocated
+        before the failing token stay assigned (``updates`` then lists them in the exception's
+        ``updates`` attribute), as in the reference.
+        """
+        bs = self.block_size
+        out = np.empty(int(sum(counts)), np.int64)
+        updates = []
+        k = 0
+        try:
+            for b, n in zip(slots, counts):
+                start = int(self.seq_len[b])
+                if strict_len and start > self.max_seq_len:                        # :60-61
+                    raise ValueError("Sequence length exceeds maximum allowed length.")
+                for t in range(n):
+                    pos = start + t
+                    if pos >= self.max_seq_len:                                     # :79-80
+                        raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
+                    lb = pos // bs
+                    if self.block_tables[b, lb] == -1:
+                        if not self.free_blocks:                                    # :87-88
+                            raise RuntimeError("OOM : No free physical blocks available for allocation.")
+                        phys = self.free_blocks.popleft()
+                        self.block_tables[b, lb] = phys
+                        updates.append((b, lb, phys))
+                    out[k] = int(self.block_tables[b, lb]) * bs + pos % bs
+                    k += 1
+        except (ValueError, RuntimeError) as e:
+            e.updates = updates
+            raise
+        return out, updates
+
+    def plan_decode(self, slots) -> np.ndarray:
+        """One new token per slot: the block each slot takes from the free list, or -1."""
+        bs = self.block_size
+        new_block = np.full(len(slots), -1, np.int32)
+        for i, b in enumerate(slots):
+            pos = int(self.seq_len[b])
+            if pos >= self.max_seq_len:
+                raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
+            lb = pos // bs
+            if self.block_tables[b, lb] == -1:
+                if not self.free_blocks:
+                    raise RuntimeError("OOM : No free physical blocks available for allocation.")
+                phys = self.free_blocks.popleft()
+                self.block_tables[b, lb] = phys
+                new_block[i] = phys
+        return new_block
+
+    def advance(self, slots, n) -> None:
+        """seq_len[slots] += n."""
+        self.seq_len[np.asarray(slots, np.int64)] += np.asarray(n, np.int32)
+
+    def free_slot(self, batch_idx: int) -> None:
+        """engine/cache_manager.py:104-120: return the slot's blocks to the back of the free
+        list in logical order, reset its table row and its length."""
+        if batch_idx < 0 or batch_idx >= self.max_batch_size:
+            raise IndexError(f"batch_idx {batch_idx} is out of range.")
+        row = self.block_tables[batch_idx]
+        for lb in range(self.max_blocks_per_seq):
+            phys = int(row[lb])
+            if phys != -1:
+                self.free_blocks.append(phys)
+                row[lb] = -1
+        self.seq_len[batch_idx] = 0
+
+
 class KVCacheManager:
     def __init__(self, max_batch_size: int, max_seq_len: int, num_layers: int, num_kv_heads: int,
                  head_dim: int, block_size: int = 16,
@@ -60,19 +149,22 @@ class KVCacheManager:
         self.block_size = block_size
         self.device = device
         self.dtype = dtype
-        self.max_blocks_per_seq = (max_seq_len + block_size - 1) // block_size      # :25
-        self.total_physical_blocks = (max_batch_size * self.max_blocks_per_seq        # :26
-                                      if num_blocks is None else int(num_blocks))
+        self.alloc = BlockAllocator(max_batch_size, max_seq_len, block_size, num_blocks)
+        self.max_blocks_per_seq = self.alloc.max_blocks_per_seq
+        self.total_physical_blocks = self.alloc.total_physical_blocks
         shape = (num_layers, self.total_physical_blocks, num_kv_heads, block_size, head_dim)
         self.key_cache = torch.zeros(shape, device=device, dtype=dtype)
         self.value_cache = torch.zeros(shape, device=device, dtype=dtype)
         self.seq_len = torch.zeros(max_batch_size, device=device, dtype=torch.int32)
         self.block_tables = torch.full((max_batch_size, self.max_blocks_per_seq), -1,
                                        dtype=torch.int32, device=device)
-        self.free_blocks = FreeBlockList(range(self.total_physical_blocks))
-        # host mirrors, authoritative for the engine's step planning
-        self._seq_host = np.zeros(max_batch_size, np.int32)
-        self._bt_host = np.full((max_batch_size, self.max_blocks_per_seq), -1, np.int32)
+        # host mirrors (the allocator's arrays), authoritative for the engine's step planning
+        self._seq_host = self.alloc.seq_len
+        self._bt_host = self.alloc.block_tables
+
+    @property
+    def free_blocks(self) -> FreeBlockList:
+        return self.alloc.free_blocks
 
     # ---- mirrors ------------------------------------------------------------------------
     def sync_from_device(self) -> None:
@@ -86,57 +178,21 @@ class KVCacheManager:
         return int(self._seq_host[slot])
 
     def plan_tokens(self, slots, counts, *, strict_len: bool = True):
-        """Allocate blocks for ``counts[i]`` new tokens of each slot, in the reference's order
-        (slot by slot, token by token, cache_manager.py:73-92), on the host mirror.
-
-        Returns (slot_mapping int64 [sum(counts)], updates list of (slot, logical, phys)).
-        Raises ValueError / RuntimeError like the reference; on error the blocks allocated
-        before the failing token stay assigned, as in the reference.
-        """
-        bs = self.block_size
-        out = np.empty(int(sum(counts)), np.int64)
-        updates = []
-        k = 0
+        """``BlockAllocator.plan_tokens`` on the host mirror; the new block-table entries are
+        pushed to the device table (also those made before an allocation error)."""
         try:
-            for b, n in zip(slots, counts):
-                start = int(self._seq_host[b])
-                if strict_len and start > self.max_seq_len:                        # :60-61
-                    raise ValueError("Sequence length exceeds maximum allowed length.")
-                for t in range(n):
-                    pos = start + t
-                    if pos >= self.max_seq_len:                                     # :79-80
-                        raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
-                    lb = pos // bs
-                    if self._bt_host[b, lb] == -1:
-                        if not self.free_blocks:                                    # :87-88
-                            raise RuntimeError("OOM : No free physical blocks available for allocation.")
-                        phys = self.free_blocks.popleft()
-                        self._bt_host[b, lb] = phys
-                        updates.append((b, lb, phys))
-                    out[k] = int(self._bt_host[b, lb]) * bs + pos % bs
-                    k += 1
-        finally:
-            self._push_updates(updates)
+            out, updates = self.alloc.plan_tokens(slots, counts, strict_len=strict_len)
+        except (ValueError, RuntimeError) as e:
+            self._push_updates(getattr(e, "updates", []))
+            raise
+        self._push_updates(updates)
         return out, updates
 
     def plan_decode(self, slots) -> np.ndarray:
         """One new token per slot: the block each slot must take from the free list this step,
         or -1.  Same order and checks as :meth:`plan_tokens`; the device block table is written
         by the step's prepare kernel (``ti_decode_prepare``), not here."""
-        bs = self.block_size
-        new_block = np.full(len(slots), -1, np.int32)
-        for i, b in enumerate(slots):
-            pos = int(self._seq_host[b])
-            if pos >= self.max_seq_len:
-                raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
-            lb = pos // bs
-            if self._bt_host[b, lb] == -1:
-                if not self.free_blocks:
-                    raise RuntimeError("OOM : No free physical blocks available for allocation.")
-                phys = self.free_blocks.popleft()
-                self._bt_host[b, lb] = phys
-                new_block[i] = phys
-        return new_block
+        return self.alloc.plan_decode(slots)
 
     def _push_updates(self, updates) -> None:
         if not updates:
@@ -148,7 +204,7 @@ class KVCacheManager:
     def advance(self, slots, n) -> None:
         """seq_len[slots] += n on the host mirror (the device copy is advanced by the step, or
         by :meth:`advance_device`)."""
-        self._seq_host[np.asarray(slots, np.int64)] += np.asarray(n, np.int32)
+        self.alloc.advance(slots, n)
 
     def advance_device(self, slots, n) -> None:
         idx = torch.as_tensor(np.asarray(slots, np.int64), device=self.device)
@@ -212,14 +268,6 @@ class KVCacheManager:
     def free_batch_slot(self, batch_idx: int) -> None:
         """engine/cache_manager.py:104-120: return the slot's blocks to the back of the free
         list in logical order, reset its table row and its length."""
-        if batch_idx < 0 or batch_idx >= self.max_batch_size:
-            raise IndexError(f"batch_idx {batch_idx} is out of range.")
-        row = self._bt_host[batch_idx]
-        for lb in range(self.max_blocks_per_seq):
-            phys = int(row[lb])
-            if phys != -1:
-                self.free_blocks.append(phys)
-                row[lb] = -1
-        self._seq_host[batch_idx] = 0
+        self.alloc.free_slot(batch_idx)
         self.block_tables[batch_idx].fill_(-1)
         self.seq_len[batch_idx] = 0

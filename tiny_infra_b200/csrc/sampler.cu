@@ -1,0 +1,302 @@
+// Device sampler: temperature, top-k, top-p and the draw of the reference's
+// ContinuousBatcher._sample_next_token (engine/scheduler.py:104-156), one CTA per row, with no
+// sort of the vocabulary.
+//
+// The reference divides the row by its temperature (0 -> 1; here: multiplies by 1/t in fp32),
+// keeps values >= a cutoff that is the max_k-th largest value for rows whose top_k equals the
+// batch's largest top_k and -inf for the others (:119-130), then -- when any row has p < 1 --
+// removes the tail of the descending order after the first token whose cumulative softmax
+// probability exceeds p (:133-146), and finally draws from the softmax of what is left, or
+// takes the argmax for temperature 0 (:149-155).  The batch-level rules are resolved on the
+// host into a per-row cut rank (0: no cut) and p (>= 1: no top-p).
+//
+// Here every "position in the descending order" question is answered by a radix select over
+// order-preserving 32-bit keys of the fp32 values (4 passes of 8-bit digits over the row):
+//   * top-k cutoff: the max_k-th largest key (counts);
+//   * top-p boundary and the draw: the first element of the descending order whose cumulative
+//     weight exceeds a target, weights exp(x - max) in 32.32 fixed point (integer sums: the
+//     result does not depend on the order of the additions); elements with equal values are
+//     ordered by ascending index (a final pass scans the tied elements in index order).
+// The draw uses a caller-provided uniform u in [0, 1): the token is the first one, in
+// descending order, whose cumulative kept weight exceeds u * (total kept weight).
+#include <algorithm>
+#include <type_traits>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ti {
+namespace smp {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kBins = 256;
+
+__device__ __forceinline__ uint32_t f2key(float x) {   // order-preserving: larger x, larger key
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+struct Shared {
+  unsigned long long hist[kBins];
+  unsigned long long scan[kWarps];
+  float red_v[kWarps];
+  int red_i[kWarps];
+  uint32_t sel_key;
+  unsigned long long sel_acc;    // weight of the elements above the selected bucket
+  int sel_found;
+  int sel_index;
+  unsigned long long sel_cum;    // cumulative weight up to and including the selected element
+};
+
+// A row of logits scaled by 1 / temperature (temperature 0 -> 1): the value every pass sees.
+template <typename T>
+struct Row {
+  const T* p;
+  float inv_t;
+  __device__ __forceinline__ float x(int j) const {
+    float v;
+    if constexpr (std::is_same<T, float>::value) v = p[j];
+    else v = Elem<T>::to_f(p[j]);
+    return v * inv_t;
+  }
+};
+
+// Weight of element with value x in 32.32 fixed point (exp(x - m), x <= m), 0 when not a
+// candidate.
+__device__ __forceinline__ unsigned long long weight(float x, float m) {
+  const float w = __expf(x - m);
+  return (unsigned long long)(w * 4294967296.0f);
+}
+
+// Find, among the elements with key >= lowkey, the first element of the descending order
+// (ties: ascending index) whose cumulative weight exceeds `target` (COUNT: every weight is 1).
+// Results in sh.sel_*: sel_found, sel_key, sel_index, sel_cum.  With SKIP_TIES only the key
+// is resolved (sel_index = -1).
+template <typename T, bool COUNT, bool SKIP_TIES>
+__device__ void select_first_exceeding(Shared& sh, const Row<T>& row, int V, uint32_t lowkey,
+                                       float m, unsigned long long target) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t prefix = 0, pmask = 0;
+  unsigned long long acc = 0;
+  bool found = true;
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < kBins; b += kThreads) sh.hist[b] = 0ull;
+    __syncthreads();
+    for (int j = tid; j < V; j += kThreads) {
+      const float x = row.x(j);
+      const uint32_t k = f2key(x);
+      if (k < lowkey || (k & pmask) != prefix) continue;
+      atomicAdd(&sh.hist[(k >> shift) & 255u], COUNT ? 1ull : weight(x, m));
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255 - 8l ... 248 - 8l (descending); suffix sums in that order
+      unsigned long long own[8], s = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { own[i] = sh.hist[255 - 8 * lane - i]; s += own[i]; }
+      unsigned long long before = s;                 // inclusive scan over lanes
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long v = __shfl_up_sync(0xffffffffu, before, o);
+        if (lane >= o) before += v;
+      }
+      before -= s;                                   // exclusive: weight of higher bins
+      const bool here = acc + before <= target && acc + before + s > target;
+      const unsigned ball = __ballot_sync(0xffffffffu, here);
+      if (ball == 0) {
+        if (lane == 0) sh.sel_found = 0;
+      } else if (lane == __ffs(ball) - 1) {
+        unsigned long long run = acc + before;
+        int bin = 255 - 8 * lane;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (run + own[i] > target) { bin = 255 - 8 * lane - i; break; }
+          run += own[i];
+        }
+        sh.sel_found = 1;
+        sh.sel_key = (uint32_t)bin;
+        sh.sel_acc = run;
+      }
+    }
+    __syncthreads();
+    if (!sh.sel_found) { found = false; break; }
+    prefix |= sh.sel_key << shift;
+    pmask |= 255u << shift;
+    acc = sh.sel_acc;
+    __syncthreads();
+  }
+  if (!found) {
+    if (tid == 0) sh.sel_found = 0;
+    __syncthreads();
+    return;
+  }
+  if (SKIP_TIES) {
+    if (tid == 0) { sh.sel_found = 1; sh.sel_key = prefix; sh.sel_index = -1; sh.sel_acc = acc; }
+    __syncthreads();
+    return;
+  }
+  // elements with key == prefix, in index order: thread t owns a contiguous index range
+  if (tid == 0) sh.sel_index = -1;
+  __syncthreads();
+  const int chunk = (V + kThreads - 1) / kThreads;
+  const int j0 = min(V, tid * chunk), j1 = min(V, j0 + chunk);
+  unsigned long long mine = 0;
+  for (int j = j0; j < j1; ++j) {
+    const float x = row.x(j);
+    if (f2key(x) == prefix) mine += COUNT ? 1ull : weight(x, m);
+  }
+  unsigned long long incl = mine;   // block-wide inclusive scan in thread order
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sh.scan[warp] = incl;
+  __syncthreads();
+  unsigned long long wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += sh.scan[w];
+  const unsigned long long excl = acc + wbase + incl - mine;
+  if (excl <= target && excl + mine > target) {
+    unsigned long long run = excl;
+    for (int j = j0; j < j1; ++j) {
+      const float x = row.x(j);
+      if (f2key(x) != prefix) continue;
+      run += COUNT ? 1ull : weight(x, m);
+      if (run > target) {
+        sh.sel_index = j;
+        sh.sel_cum = run;
+        break;
+      }
+    }
+    sh.sel_key = prefix;
+    sh.sel_found = 1;
+  }
+  __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temps,
+              const int32_t* __restrict__ cut_ks, const float* __restrict__ top_ps,
+              const float* __restrict__ uniforms, int32_t* __restrict__ out,
+              const int32_t* __restrict__ slots, int32_t* seq_len, int inc) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ Shared sh;
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float temp = temps[r];
+  Row<T> row;
+  row.p = logits + (int64_t)r * ld;
+  row.inv_t = temp == 0.f ? 1.f : 1.f / temp;
+
+  // ---- max and first argmax
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = tid; j < V; j += kThreads) {
+    const float x = row.x(j);
+    if (x > best || (x == best && j < bi)) { best = x; bi = j; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  }
+  if (lane == 0) { sh.red_v[warp] = best; sh.red_i[warp] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kWarps; ++w)
+      if (sh.red_v[w] > sh.red_v[0] || (sh.red_v[w] == sh.red_v[0] && sh.red_i[w] < sh.red_i[0])) {
+        sh.red_v[0] = sh.red_v[w];
+        sh.red_i[0] = sh.red_i[w];
+      }
+  }
+  __syncthreads();
+  const float m = sh.red_v[0];
+  int token = sh.red_i[0] == 0x7fffffff ? 0 : sh.red_i[0];   // an all-NaN row yields 0
+
+  if (temp != 0.f && m > -INFINITY) {
+    // ---- top-k cutoff: keep x >= the k-th largest value (k = 0: keep everything)
+    uint32_t lowkey = 0;
+    const int k = cut_ks[r];
+    if (k > 0 && k < V) {
+      select_first_exceeding<T, true, true>(sh, row, V, 0u, m, (unsigned long long)(k - 1));
+      if (sh.sel_found) lowkey = sh.sel_key;       // keep x >= the k-th largest value
+    }
+    // ---- total weight of the candidates
+    unsigned long long z = 0;
+    for (int j = tid; j < V; j += kThreads) {
+      const float x = row.x(j);
+      if (f2key(x) >= lowkey) z += weight(x, m);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    if (lane == 0) sh.scan[warp] = z;
+    __syncthreads();
+    unsigned long long Z = 0;
+    for (int w = 0; w < kWarps; ++w) Z += sh.scan[w];
+    __syncthreads();
+    // ---- top-p: kept = the descending prefix up to the first element whose cumulative
+    //      weight exceeds p * Z (the first element is always kept)
+    unsigned long long zk = Z;
+    const float p = top_ps[r];
+    if (p < 1.f) {
+      const double tgt = (double)p * (double)Z;
+      if (tgt < (double)Z) {
+        const unsigned long long target = tgt <= 0.0 ? 0ull : (unsigned long long)tgt;
+        select_first_exceeding<T, false, false>(sh, row, V, lowkey, m, target);
+        if (sh.sel_found) zk = sh.sel_cum;
+      }
+    }
+    // ---- the draw: first element whose cumulative weight exceeds u * zk
+    const float u = fminf(fmaxf(uniforms[r], 0.f), 0.99999994f);
+    const unsigned long long t2 = (unsigned long long)((double)u * (double)zk);
+    select_first_exceeding<T, false, false>(sh, row, V, lowkey, m, t2);
+    if (sh.sel_found && sh.sel_index >= 0) token = sh.sel_index;
+  }
+  if (tid == 0) {
+    out[r] = token;
+    if (slots && seq_len) {
+      const int s = slots[r];
+      if (s >= 0) seq_len[s] += inc;
+    }
+  }
+}
+
+}  // namespace smp
+}  // namespace ti
+
+using namespace ti;
+
+extern "C" int ti_sample(const void* logits, int64_t ld, int dtype, int rows, int vocab,
+                         const float* temperatures, const int32_t* cut_ks, const float* top_ps,
+                         const float* uniforms, int32_t* out_tokens, const int32_t* slots,
+                         int32_t* seq_len, int seq_inc, void* stream) {
+  clear_error();
+  if (rows == 0) return TI_OK;
+  if (!logits || !temperatures || !cut_ks || !top_ps || !uniforms || !out_tokens || rows < 0 ||
+      vocab <= 0 || ld < vocab)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "sample: null pointer or bad size");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == TI_DTYPE_BF16)
+    return launch_kernel("sample launch", smp::sample_kernel<__nv_bfloat16>, dim3(rows),
+                         dim3(smp::kThreads), 0, s, 1, (const __nv_bfloat16*)logits, ld, vocab,
+                         temperatures, cut_ks, top_ps, uniforms, out_tokens, slots, seq_len,
+                         seq_inc);
+  if (dtype == TI_DTYPE_FP16)
+    return launch_kernel("sample launch", smp::sample_kernel<__half>, dim3(rows),
+                         dim3(smp::kThreads), 0, s, 1, (const __half*)logits, ld, vocab,
+                         temperatures, cut_ks, top_ps, uniforms, out_tokens, slots, seq_len,
+                         seq_inc);
+  if (dtype == TI_DTYPE_FP32)
+    return launch_kernel("sample launch", smp::sample_kernel<float>, dim3(rows),
+                         dim3(smp::kThreads), 0, s, 1, (const float*)logits, ld, vocab,
+                         temperatures, cut_ks, top_ps, uniforms, out_tokens, slots, seq_len,
+                         seq_inc);
+  return set_error(TI_ERR_UNSUPPORTED, "sample: dtype must be bf16, fp16 or fp32");
+}

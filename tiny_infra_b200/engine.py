@@ -47,8 +47,13 @@ class DecodeEngine:
             R, c.num_attention_heads, c.num_key_value_heads, c.head_dim,
             kv_cache.max_blocks_per_seq, 0)
         self.ws = torch.zeros(need, dtype=torch.uint8, device=dev)
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.launches_per_step: dict[int, int] = {}
+        self.graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.launches_per_step: dict[tuple, int] = {}
+        # sampled steps (allocated on first use): logits [R, V] and the per-row sampling
+        # parameters (temperature, cut rank, top-p, uniform) copied in with the step's inputs
+        self.logits = None
+        self.d_params = torch.zeros(4, R, dtype=torch.float32, device=dev)
+        self.h_params = torch.zeros(4, R, dtype=torch.float32).pin_memory()
 
     @staticmethod
     def bucket(n: int) -> int:
@@ -65,8 +70,9 @@ class DecodeEngine:
             tile_seq=None, tile_q0=None, num_tokens=rows, num_seqs=rows, decode=True,
             last_rows=None)
 
-    def _launch(self, rows: int) -> None:
-        """All launches of one decode step for ``rows`` (bucket-padded) rows."""
+    def _launch(self, rows: int, sampled: bool = False) -> None:
+        """All launches of one decode step for ``rows`` (bucket-padded) rows: greedy (lm_head
+        with the argmax epilogue) or sampled (logits, then the device sampler)."""
         m, c, lib = self.model, self.model.config, N.lib()
         s = torch.cuda.current_stream(m.device).cuda_stream
         dt = N.dtype_code(m.dtype)
@@ -82,6 +88,17 @@ class DecodeEngine:
         N.check(lib.ti_rmsnorm(self.xf.data_ptr(), self.hidden.data_ptr(), N.TI_DTYPE_FP32,
                                m.weights["norm"].data_ptr(), c.rms_norm_eps, rows,
                                c.hidden_size, dt, s))
+        if sampled:
+            N.check(lib.ti_gemm(N.TI_EPI_STORE, self.xf.data_ptr(), c.hidden_size,
+                                m.weights["lm_head"].data_ptr(), c.hidden_size, rows,
+                                c.vocab_size, c.hidden_size, self.logits.data_ptr(),
+                                c.vocab_size, None, None, None, dt, LM_TILE, 1, s))
+            dp = self.d_params
+            N.check(lib.ti_sample(self.logits.data_ptr(), c.vocab_size, dt, rows, c.vocab_size,
+                                  dp[0].data_ptr(), dp[1].data_ptr(), dp[2].data_ptr(),
+                                  dp[3].data_ptr(), self.next_tok.data_ptr(),
+                                  self.d_in[1].data_ptr(), kv.seq_len.data_ptr(), 1, s))
+            return
         N.check(lib.ti_gemm(N.TI_EPI_ARGMAX, self.xf.data_ptr(), c.hidden_size,
                             m.weights["lm_head"].data_ptr(), c.hidden_size, rows, c.vocab_size,
                             c.hidden_size, None, 0, None, self.part_val.data_ptr(),
@@ -90,11 +107,16 @@ class DecodeEngine:
                                      self.ntiles, rows, self.next_tok.data_ptr(),
                                      self.d_in[1].data_ptr(), kv.seq_len.data_ptr(), 1, s))
 
-    def _replay(self, rows: int) -> None:
+    def _replay(self, rows: int, sampled: bool = False) -> None:
+        if sampled and self.logits is None:
+            c = self.model.config
+            self.logits = torch.empty(self.max_rows, c.vocab_size, dtype=self.model.dtype,
+                                      device=self.model.device)
         if not self.use_graphs:
-            self._launch(rows)
+            self._launch(rows, sampled)
             return
-        g = self.graphs.get(rows)
+        key = (rows, sampled)
+        g = self.graphs.get(key)
         if g is None:
             # one eager run sets kernel attributes / tensor-map caches outside the capture; it
             # must not change state, so it runs on a padding-only input
@@ -103,15 +125,15 @@ class DecodeEngine:
             self.d_in[1].fill_(-1)
             self.d_in[2].fill_(-1)
             before = N.launch_count()
-            self._launch(rows)
-            self.launches_per_step[rows] = N.launch_count() - before
+            self._launch(rows, sampled)
+            self.launches_per_step[key] = N.launch_count() - before
             torch.cuda.current_stream().synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._launch(rows)
+                self._launch(rows, sampled)
             self.d_in.copy_(saved)
             self.kv.seq_len.copy_(seq_saved)
-            self.graphs[rows] = g
+            self.graphs[key] = g
         g.replay()
 
     def stage(self, slots, tokens) -> int:
@@ -133,17 +155,28 @@ class DecodeEngine:
         self.d_in[:, :rows].copy_(self.h_in[:, :rows], non_blocking=True)
         return rows
 
-    def step(self, slots, tokens) -> np.ndarray:
-        """One greedy decode step for the given slots (public API: host ints in, host ints out).
+    def step(self, slots, tokens, params=None) -> np.ndarray:
+        """One decode step for the given slots (public API: host ints in, host ints out).
 
         ``tokens[i]`` is the last token of the sequence in ``slots[i]``; returns the next token
-        of each.  Blocks are allocated as the reference would; ``seq_len`` advances by one.
+        of each: greedy, or drawn with ``params`` (a ``sampler.SamplingParams`` of the batch;
+        rows with temperature 0 stay greedy).  Blocks are allocated as the reference would;
+        ``seq_len`` advances by one.
         """
         n = len(slots)
         if n == 0:
             return np.zeros(0, np.int32)
         rows = self.stage(slots, tokens)
-        self._replay(rows)
+        sampled = params is not None and not params.all_greedy
+        if sampled:
+            h = self.h_params.numpy()
+            h[:, :n] = params.packed()
+            h[0, n:rows] = 0.0                    # padding rows: greedy, no cut
+            h[1, n:rows] = 0.0
+            h[2, n:rows] = 1.0
+            h[3, n:rows] = 0.0
+            self.d_params[:, :rows].copy_(self.h_params[:, :rows], non_blocking=True)
+        self._replay(rows, sampled)
         self.h_out[:n].copy_(self.next_tok[:n], non_blocking=True)
         torch.cuda.current_stream().synchronize()
         self.kv.advance(slots, 1)

@@ -164,8 +164,13 @@ class Qwen2ForCausalLM:
     # ---- packed-batch planning (host) -----------------------------------------------------------
     def plan(self, kv_cache, slots, counts, token_ids) -> PackedBatch:
         """Allocate the new tokens' blocks (reference order) and build the batch metadata."""
-        dev = self.device
         mapping, _ = kv_cache.plan_tokens(slots, counts)
+        return self.packed_batch(kv_cache, slots, counts, token_ids, mapping)
+
+    def packed_batch(self, kv_cache, slots, counts, token_ids, mapping) -> PackedBatch:
+        """Batch metadata for new tokens whose blocks are allocated (``mapping``: pool slot of
+        every new token, in order); the slots' lengths have not been advanced yet."""
+        dev = self.device
         nseq = len(slots)
         start = np.array([kv_cache.seq_len_host(s) for s in slots], np.int32)
         counts = np.asarray(counts, np.int32)
