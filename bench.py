@@ -335,6 +335,7 @@ def run_ours(a, rank, world, local):
     import torch
     import torch.distributed as dist
     from tiny_infra_b200 import _native as N
+    from tiny_infra_b200 import replicas
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -376,11 +377,7 @@ def run_ours(a, rank, world, local):
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    secs = e0.elapsed_time(e1) / 1e3
-    if world > 1:
-        t = torch.tensor([secs], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
+    secs = replicas.max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
     launches = engine.launches_per_step.get((rows, False), 0) * a.steps
     value = world * SEQS * a.steps / secs
 
@@ -397,11 +394,7 @@ def run_ours(a, rank, world, local):
         toks = engine.step(slots, toks)
     e2[1].record()
     torch.cuda.synchronize()
-    esecs = e2[0].elapsed_time(e2[1]) / 1e3
-    if world > 1:
-        t = torch.tensor([esecs], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        esecs = float(t.item())
+    esecs = replicas.max_over_ranks(e2[0].elapsed_time(e2[1]) / 1e3, device)
     e2e = world * SEQS * a.steps / esecs
 
     roof = attention_roofline(engine, kv, cfg, ctx, 50, peak) if rank == 0 else None

@@ -4,8 +4,10 @@ import sys
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-if REPO not in sys.path:
-    sys.path.insert(0, REPO)
+TESTS = os.path.join(REPO, "tests")
+for _p in (REPO, TESTS):   # test modules share helpers (and spawned workers import them)
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
 GOLDEN = os.path.join(REPO, "tests", "golden")
 
