@@ -45,7 +45,7 @@ def _args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kernel", choices=["attention", "gate_up"], default=None,
                     help="time one kernel alone instead of the decode step")
-    ap.add_argument("--case", choices=["256", "config1"], default="256",
+    ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
                          "8-sequence ctx U[1,512] paged-attention op")
     return ap.parse_args()
@@ -479,7 +479,8 @@ def run_attention_kernel(a):
     from tiny_infra_b200 import custom_paged_attn
     dev = torch.device("cuda:0")
     rng = np.random.default_rng(a.seed)
-    B, lo, hi, NB = (SEQS, CTX_LO, CTX_HI, None) if a.case == "256" else (8, 1, 512, 512)
+    B, lo, hi, NB = {"256": (SEQS, CTX_LO, CTX_HI, None), "config1": (8, 1, 512, 512),
+                     "long": (SEQS, 8192, 32768, None)}[a.case]
     NH, KVH, D, bs = 14, 2, 64, 16
     ctx = rng.integers(lo, hi + 1, B).astype(np.int32)
     need = int(sum((int(c) + bs - 1) // bs for c in ctx))
@@ -492,7 +493,7 @@ def run_attention_kernel(a):
         n = (int(ctx[b]) + bs - 1) // bs
         bt[b, :n] = perm[off:off + n]
         off += n
-    layers = 8 if a.case == "256" else 64   # > 126 MB of KV either way
+    layers = {"256": 8, "config1": 64, "long": 2}[a.case]   # > 126 MB of KV in every case
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed)
     q = torch.randn(B, NH, D, device=dev, generator=g).to(torch.bfloat16)

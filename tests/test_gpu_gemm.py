@@ -159,3 +159,28 @@ def test_argmax_epilogue(cuda_device):
     _close_bf16(logits.float().cpu().numpy(), ref)
     assert got[0] == 123             # exact tie across tiles: lowest index wins
     assert (ix >= 0).all() and (ix < N).all()
+
+
+@pytest.mark.parametrize("M", [37, 130, 256])
+def test_argmax_persistent_lm_head(cuda_device, M):
+    """Greedy lm_head without logits (the persistent kernel: both 128-row halves per CTA, two
+    TMEM buffers): per-tile (max, first argmax) equal to the float32 reference; ties planted
+    across tiles resolve to the lowest index."""
+    from tiny_infra_b200 import _native as N_
+    N, K, bn = 151936, 896, 128
+    a, b = _operands(M + 3, M, N, K)
+    b[140000] = b[77]
+    a[M - 1] = bf16_round(b[77] * 64.0)
+    nt = N // bn
+    val = torch.empty((M, nt), dtype=torch.float32, device="cuda")
+    idx = torch.empty((M, nt), dtype=torch.int32, device="cuda")
+    _gemm(N_.TI_EPI_ARGMAX, _dev(a), _dev(b), M, N, K, aux_val=val, aux_idx=idx, block_n=bn)
+    ref = a @ b.T
+    v, ix = val.cpu().numpy(), idx.cpu().numpy()
+    np.testing.assert_allclose(v, ref.reshape(M, nt, bn).max(axis=2), rtol=1e-5, atol=1e-4)
+    got = ix[np.arange(M), np.argmax(v, axis=1)]
+    srt = np.sort(ref, axis=1)
+    clear = (srt[:, -1] - srt[:, -2]) > 1e-3
+    assert (got[clear] == np.argmax(ref, axis=1)[clear]).all()
+    assert got[M - 1] == 77
+    assert (ix >= 0).all() and (ix < N).all()

@@ -630,6 +630,178 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   }
 }
 
+// ---- persistent greedy lm_head: argmax of D = A . B^T per 128-column tile, M <= 256 -----------
+// One CTA per SM loops over the N tiles.  Both 128-row halves of A (up to 256 tokens) share each
+// B stage (two MMAs per K step), and the accumulators alternate between two 256-column TMEM
+// buffers, so the epilogue of one tile (per row: max and first argmax of its 128 columns)
+// overlaps the MMAs of the next while the TMA ring keeps streaming across tiles.
+//   warp 0    TMA: A 256 x 64 + B 128 x 64 per K block (48 KB stages);
+//   warp 1    MMA: 2 x tcgen05.mma M=128 N=128 per K=16 step, commits stages and buffers;
+//   warps 2-5 epilogue: tcgen05.ld both halves, write (max, first argmax) per row and tile.
+namespace lmh {
+constexpr int kBN = 128;
+constexpr int kStages = 4;
+constexpr int kABytes = 256 * BK * 2;                 // 32 KB
+constexpr int kBBytes = kBN * BK * 2;                 // 16 KB
+constexpr int kStage = kABytes + kBBytes;             // 48 KB
+constexpr int kRing = kStages * kStage;               // 192 KB
+constexpr int kBars = (2 * kStages + 4) * 8 + 8;
+constexpr int kSmem = kRing + 1024;
+constexpr int kTmemCols = 512;                        // 2 buffers x (2 halves x 128 columns)
+static_assert(2 * kBars <= 1024, "barriers fit the slack");
+}  // namespace lmh
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+lmhead_argmax_kernel(const __grid_constant__ CUtensorMap amap,
+                     const __grid_constant__ CUtensorMap bmap, int M, int K, int ntiles,
+                     float* __restrict__ aux_val, int32_t* __restrict__ aux_idx) {
+  using namespace lmh;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* bars = (smem - smem_raw >= kBars) ? smem_raw : smem + kRing;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + kStages * 8;
+  const uint32_t accf0 = empty0 + kStages * 8;          // accumulator buffer b ready
+  const uint32_t acce0 = accf0 + 2 * 8;                 // accumulator buffer b drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + (2 * kStages + 4) * 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = K / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(full0 + 8 * s, 1);
+        mbar_init(empty0 + 8 * s, 1);
+      }
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(accf0 + 8 * b, 1);
+        mbar_init(acce0 + 8 * b, 4);                    // one arrival per epilogue warp
+      }
+      fence_mbar_init();
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&bmap);
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_last();
+      const uint64_t pol_b = l2_policy_evict_first();
+      int g = 0;          // K blocks issued so far (all tiles)
+      bool waited = false, ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages &&
+              !mbar_wait(empty0 + 8 * s, ((g / kStages) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full0 + 8 * s, kStage);
+          const uint32_t sa = sbase + s * kStage;
+          tma_load_2d_hint(sa + kABytes, &bmap, full0 + 8 * s, kb * BK, tile * kBN, pol_b);
+          if (!waited) { pdl_wait(); waited = true; }   // A is the previous kernel's output
+          tma_load_2d_hint(sa, &amap, full0 + 8 * s, kb * BK, 0, pol_a);
+        }
+      }
+      if (!waited) pdl_wait();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(kBN, std::is_same<T, __nv_bfloat16>::value);
+      int g = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
+        const int b = local & 1, use = local >> 1;
+        if (use > 0 && !mbar_wait(acce0 + 8 * b, (use & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + (uint32_t)(b * 256), d1 = d0 + 128;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (!mbar_wait(full0 + 8 * s, (g / kStages) & 1, TI_DEVERR_GEMM_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = sbase + s * kStage;
+          const uint64_t da = smem_desc(sa), da1 = smem_desc(sa + 128 * 128), db = smem_desc(sa + kABytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            tc_mma(d0, da + 2 * k, db + 2 * k, idesc, acc);
+            tc_mma(d1, da1 + 2 * k, db + 2 * k, idesc, acc);
+          }
+          tc_commit(empty0 + 8 * s);
+        }
+        tc_commit(accf0 + 8 * b);
+      }
+    }
+    __syncwarp();
+  } else {
+    pdl_wait();   // aux_* may be read by an earlier kernel of the stream
+    const int quad = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+      const int b = local & 1, use = local >> 1;
+      if (!mbar_wait(accf0 + 8 * b, use & 1, TI_DEVERR_GEMM_WAIT)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * 256 + half * 128);
+        Best best{-INFINITY, 0x7fffffff};
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          float v[32];
+          tmem_ld32(trow + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) best.take(v[i], tile * kBN + c + i);
+        }
+        const int row = half * 128 + quad * 32 + lane;
+        if (row < M) {
+          aux_val[(int64_t)row * ntiles + tile] = best.v;
+          aux_idx[(int64_t)row * ntiles + tile] = best.i;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * b);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T>
+static int launch_lmhead_argmax(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
+                                float* aux_val, int32_t* aux_idx, cudaStream_t s) {
+  auto kern = lmhead_argmax_kernel<T>;
+  static int set_dev = -1, sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lmh::kSmem);
+    if (err != cudaSuccess) return set_cuda_error(err, "cudaFuncSetAttribute(lm_head gemm)");
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    set_dev = dev;
+  }
+  const int ntiles = N / lmh::kBN;
+  return launch_kernel("lm_head gemm launch", kern, dim3(std::min(sms, ntiles)), dim3(kThreads),
+                       lmh::kSmem, s, 1, am, bm, M, K, ntiles, aux_val, aux_idx);
+}
+
 // ---- host side ----------------------------------------------------------------------------
 struct MapKey {
   const void* p;
@@ -826,7 +998,19 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
     return set_error(TI_ERR_UNSUPPORTED, "gemm: M too large");
 
   CUtensorMap am, bm;
-  int rc = gemm::operand_map(&am, A, M, K, lda, gemm::BM, dtype);
+  int rc;
+  if (epilogue == TI_EPI_ARGMAX && !out && M <= 256 && block_n == gemm::lmh::kBN) {
+    // greedy lm_head: persistent kernel, both 128-row halves per CTA
+    rc = gemm::operand_map(&am, A, M, K, lda, 256, dtype);
+    if (rc) return rc;
+    rc = gemm::operand_map(&bm, B, N, K, ldb, gemm::lmh::kBN, dtype);
+    if (rc) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    return dtype == TI_DTYPE_BF16
+               ? gemm::launch_lmhead_argmax<__nv_bfloat16>(am, bm, M, N, K, aux_val, aux_idx, s)
+               : gemm::launch_lmhead_argmax<__half>(am, bm, M, N, K, aux_val, aux_idx, s);
+  }
+  rc = gemm::operand_map(&am, A, M, K, lda, gemm::BM, dtype);
   if (rc) return rc;
   rc = gemm::operand_map(&bm, B, N, K, ldb, block_n, dtype);
   if (rc) return rc;
