@@ -43,6 +43,11 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", choices=["decode", "serving"], default="decode",
+                    help="decode: the 256-sequence decode step (the headline metric); serving: "
+                         "a Poisson request stream through the continuous batcher")
+    ap.add_argument("--requests", type=int, default=1024, help="serving: number of requests")
+    ap.add_argument("--rate", type=float, default=64.0, help="serving: arrivals per second")
     ap.add_argument("--kernel", choices=["attention", "gate_up"], default=None,
                     help="time one kernel alone instead of the decode step")
     ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
@@ -542,9 +547,92 @@ def run_gate_up_kernel(a):
     return 0
 
 
+def run_serving(a):
+    """A stream of generation requests through ContinuousBatcher (one GPU): Poisson arrivals
+    (--rate per second, seeded), prompt ids U[0, 151936), prompt lengths U[32, 1024], output
+    lengths U[16, 512], temperature 0.7 / top-k 50 / top-p 0.9, 256 slots, prefill chunked to
+    2048 tokens per tick.  Reports output tokens per second over the whole run (first arrival
+    to last completion) and latency statistics."""
+    import asyncio
+    import time
+
+    import torch
+    from tiny_infra_b200.cache_manager import KVCacheManager
+    from tiny_infra_b200.config import QwenConfig
+    from tiny_infra_b200.qwen2 import Qwen2ForCausalLM
+    from tiny_infra_b200.scheduler import ContinuousBatcher
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    cfg = QwenConfig()
+    sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=a.seed, tied=True)
+    model = Qwen2ForCausalLM(cfg).load_reference_state_dict(sd)
+    kv = KVCacheManager(SEQS, 1024 + 512 + 16, cfg.num_layers, cfg.num_key_value_heads,
+                        cfg.head_dim, device=dev)
+    sched = ContinuousBatcher(model, kv, eos_token_id=None, prefill_chunk_tokens=2048)
+    rng = np.random.default_rng(a.seed)
+    n = a.requests
+    gaps = rng.exponential(1.0 / a.rate, n)
+    arrive = np.cumsum(gaps) - gaps[0]
+    plen = rng.integers(32, 1025, n)
+    olen = rng.integers(16, 513, n)
+    prompts = [rng.integers(0, cfg.vocab_size, int(k)).tolist() for k in plen]
+
+    async def warm():
+        loop = asyncio.create_task(sched.run_loop())
+        await asyncio.gather(*[sched.generate(prompts[i][:64], 4) for i in range(4)])
+        loop.cancel()
+
+    asyncio.run(warm())                   # graphs and kernels set up outside the measurement
+    ttft, done_at, ntok = [None] * n, [None] * n, [0] * n
+
+    async def one(i, t0):
+        await asyncio.sleep(max(0.0, t0 + arrive[i] - time.perf_counter()))
+        start = time.perf_counter()
+        async for _ in sched.generate_stream(prompts[i], int(olen[i]), temperature=0.7,
+                                             p_value=0.9, top_k=50):
+            if ntok[i] == 0:
+                ttft[i] = time.perf_counter() - start
+            ntok[i] += 1
+        done_at[i] = time.perf_counter() - start
+
+    async def main():
+        loop = asyncio.create_task(sched.run_loop())
+        t0 = time.perf_counter()
+        await asyncio.gather(*[one(i, t0) for i in range(n)])
+        secs = time.perf_counter() - t0
+        loop.cancel()
+        return secs
+
+    secs = asyncio.run(main())
+    torch.cuda.synchronize()
+    total = int(sum(ntok))
+    lat = np.array(done_at)
+    tt = np.array(ttft)
+    per_tok = (lat - tt) / np.maximum(np.array(ntok) - 1, 1)
+    print(json.dumps({
+        "metric": "serving output tokens/s (Poisson stream, continuous batching)",
+        "value": round(total / secs, 1), "unit": "tokens/s", "n_gpus": 1,
+        "higher_is_better": True, "dtype": "bf16", "vs_baseline": None,
+        "data": "synthetic (random-init weights, random prompt ids, seeded arrivals and lengths)",
+        "config": {"workload": f"{n} requests, Poisson {a.rate}/s, prompt U[32,1024], output "
+                               "U[16,512], temp 0.7 / top-k 50 / top-p 0.9, 256 slots, "
+                               "prefill chunks of 2048 tokens",
+                   "wall_s": round(secs, 2), "output_tokens": total,
+                   "arrival_span_s": round(float(arrive[-1]), 2)},
+        "latency": {"ttft_ms_p50": round(float(np.median(tt)) * 1e3, 1),
+                    "ttft_ms_p90": round(float(np.percentile(tt, 90)) * 1e3, 1),
+                    "per_token_ms_p50": round(float(np.median(per_tok)) * 1e3, 2),
+                    "per_token_ms_p90": round(float(np.percentile(per_tok, 90)) * 1e3, 2)}}),
+          flush=True)
+    return 0
+
+
 def main():
     a = _args()
     rank, world, local = _dist()
+    if a.workload == "serving":
+        return run_serving(a) if rank == 0 else 0
     if a.kernel == "attention":
         return run_attention_kernel(a) if rank == 0 else 0
     if a.kernel == "gate_up":

@@ -33,11 +33,11 @@ def _model():
     return cfg, sd, Qwen2ForCausalLM(cfg).load_reference_state_dict(sd)
 
 
-def _run(model, cfg, prompts, **kw):
+def _run(model, cfg, prompts, chunk=None, **kw):
     from tiny_infra_b200.cache_manager import KVCacheManager
     from tiny_infra_b200.scheduler import ContinuousBatcher
     kv = KVCacheManager(4, MAX_SEQ, LAYERS, cfg.num_key_value_heads, cfg.head_dim)
-    sched = ContinuousBatcher(model, kv)
+    sched = ContinuousBatcher(model, kv, prefill_chunk_tokens=chunk)
 
     async def main():
         loop = asyncio.create_task(sched.run_loop())
@@ -56,10 +56,12 @@ def _prompts():
     return [(rng.integers(0, VOCAB, n).astype(np.int64), m) for n, m in PROMPTS]
 
 
-def test_batcher_greedy_matches_oracle(cuda_device):
+@pytest.mark.parametrize("chunk", [None, 16])
+def test_batcher_greedy_matches_oracle(cuda_device, chunk):
+    """Whole-prompt prefill, and prefill in chunks of 16 tokens interleaved with decode."""
     cfg, sd, model = _model()
     prompts = _prompts()
-    outs = _run(model, cfg, prompts, temperature=0.0)
+    outs = _run(model, cfg, prompts, chunk=chunk, temperature=0.0)
     W = {k: v.float().cpu().numpy() for k, v in sd.items()}
     W["lm_head.weight"] = W["model.embed_tokens.weight"]
     ocfg = OM.OracleConfig(num_layers=LAYERS, vocab_size=VOCAB)

@@ -45,10 +45,9 @@ class _StandInBackend:
     def _next(self, last, pos):
         return (last * 7 + pos * 3 + 1) % self.vocab
 
-    def prefill(self, slots, reqs):
+    def prefill(self, slots, reqs, counts):
         out = []
-        for slot, req in zip(slots, reqs):
-            S = len(req.prompt_tokens)
+        for slot, req, S in zip(slots, reqs, counts):
             start = int(self.kv.alloc.seq_len[slot])
             try:
                 self.kv.alloc.plan_tokens([slot], [S])
@@ -56,7 +55,8 @@ class _StandInBackend:
                 out.append(e)
                 continue
             self.kv.alloc.advance([slot], S)
-            out.append(self._next(req.prompt_tokens[-1], start + S - 1))
+            last = req.prompt_tokens[req.prefill_pos + S - 1]
+            out.append(self._next(last, start + S - 1))
         return out
 
     def decode(self, slots, reqs):
@@ -144,3 +144,29 @@ def test_generate_stream_end_to_end():
     assert refused
     assert all(s is None for s in sched.active_slots)
     assert len(kv.alloc.free_blocks) == kv.alloc.total_physical_blocks
+
+
+def test_chunked_prefill_same_tokens():
+    """With prefill_chunk_tokens the prompts are prefilled over several ticks interleaved with
+    decode; every request's tokens are the same as with whole-prompt prefill."""
+    cfg = {"max_batch_size": 3, "max_seq_len": 96, "block_size": 16, "head_dim": 8}
+    job = [([(7 * i + 3 * j) % 97 for j in range(5 + 13 * i)], 4 + i) for i in range(5)]
+
+    def run(chunk):
+        kv = _HostKV(cfg)
+        sched = ContinuousBatcher(None, kv, eos_token_id=None, backend=_StandInBackend(kv, 97),
+                                  prefill_chunk_tokens=chunk)
+
+        async def main():
+            loop = asyncio.create_task(sched.run_loop())
+            outs = await asyncio.gather(*[sched.generate(p, n, temperature=0.0) for p, n in job])
+            loop.cancel()
+            return outs
+
+        outs = asyncio.run(main())
+        assert len(kv.alloc.free_blocks) == kv.alloc.total_physical_blocks
+        return outs
+
+    whole = run(None)
+    assert run(16) == whole
+    assert run(7) == whole

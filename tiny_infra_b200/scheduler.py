@@ -49,6 +49,7 @@ class GenerationRequest:
         self.completion_event = asyncio.Event()
         self.error: Optional[BaseException] = None
         self.is_prefilled = False
+        self.prefill_pos = 0      # prompt tokens already in the KV cache (chunked prefill)
         self.request_id = GenerationRequest._next_id
         GenerationRequest._next_id += 1
         s = self.request_id if seed is None else seed
@@ -56,8 +57,15 @@ class GenerationRequest:
 
 
 class ContinuousBatcher:
-    def __init__(self, model, kv_cache, eos_token_id: Optional[int] = None, *, backend=None):
+    def __init__(self, model, kv_cache, eos_token_id: Optional[int] = None, *, backend=None,
+                 prefill_chunk_tokens: Optional[int] = None):
+        """``prefill_chunk_tokens``: at most this many prompt tokens are prefilled per tick
+        (chunked prefill interleaved with decode; a request's first token is emitted after its
+        last chunk).  None: whole prompts every tick, as the reference (block tables then match
+        the reference's bit for bit; with chunking the allocation order interleaves with decode).
+        """
         self.model = model
+        self.prefill_chunk_tokens = prefill_chunk_tokens
         self.kv_cache = kv_cache
         self.requests_queue: asyncio.Queue = asyncio.Queue()
         self.max_batch_size = kv_cache.max_batch_size
@@ -173,13 +181,32 @@ class ContinuousBatcher:
 
     def _execute_prefill_batch(self, slots: List[int]):
         """Prefill each new request (engine/scheduler.py:224-248); a request whose prefill fails
-        finishes with its error, the others go on."""
-        reqs = [self.active_slots[s] for s in slots]
-        results = self.backend.prefill(slots, reqs)
-        for slot_idx, res in zip(slots, results):
+        finishes with its error, the others go on.  With ``prefill_chunk_tokens`` the tick's
+        prompt tokens are capped and a request may take several ticks."""
+        budget = self.prefill_chunk_tokens
+        run, counts = [], []
+        for s in slots:
+            req = self.active_slots[s]
+            left = len(req.prompt_tokens) - req.prefill_pos
+            n = left if budget is None else min(left, budget)
+            if n <= 0:
+                break
+            run.append(s)
+            counts.append(n)
+            if budget is not None:
+                budget -= n
+                if budget == 0:
+                    break
+        if not run:
+            return
+        reqs = [self.active_slots[s] for s in run]
+        results = self.backend.prefill(run, reqs, counts)
+        for slot_idx, req, n, res in zip(run, reqs, counts, results):
             if isinstance(res, BaseException):
                 self._finish_request(slot_idx, reason="Error during prefill", error=res)
-            else:
+                continue
+            req.prefill_pos += n
+            if req.prefill_pos >= len(req.prompt_tokens):
                 self._emit(slot_idx, int(res), "prefill")
 
     def _execute_decode(self, decode_indices: List[int]):
@@ -207,18 +234,21 @@ class EngineBackend:
         return SamplingParams([r.temperature for r in reqs], [r.top_k for r in reqs],
                               [r.p_value for r in reqs], request_uniforms(reqs), vocab)
 
-    def prefill(self, slots, reqs):
-        """Plan each request's blocks (reference order; failures stay per request), run the
-        successful ones as one packed forward, advance their lengths and sample each one as
-        its own batch (the reference samples a prefill alone)."""
+    def prefill(self, slots, reqs, counts=None):
+        """Prefill ``counts[i]`` more prompt tokens of each request (default: the whole rest).
+        Plans each request's blocks (reference order; failures stay per request), runs the
+        successful ones as one packed forward, advances their lengths and samples each request
+        whose prompt is complete as its own batch (the reference samples a prefill alone)."""
         from . import sampler
         from .sampler import SamplingParams
+        if counts is None:
+            counts = [len(r.prompt_tokens) - r.prefill_pos for r in reqs]
         out: list = [None] * len(slots)
         ok, maps = [], []
         kv, m = self.kv, self.model
-        for i, (slot, req) in enumerate(zip(slots, reqs)):
+        for i, (slot, n) in enumerate(zip(slots, counts)):
             try:
-                mapping, _ = kv.plan_tokens([slot], [len(req.prompt_tokens)])
+                mapping, _ = kv.plan_tokens([slot], [n])
                 ok.append(i)
                 maps.append(mapping)
             except (ValueError, RuntimeError) as e:
@@ -226,11 +256,18 @@ class EngineBackend:
         if not ok:
             return out
         try:
-            pb = m.packed_batch(kv, [slots[i] for i in ok], [len(reqs[i].prompt_tokens) for i in ok],
-                                np.concatenate([np.asarray(reqs[i].prompt_tokens, np.int32)
-                                                for i in ok]), np.concatenate(maps))
+            chunk = [np.asarray(reqs[i].prompt_tokens[reqs[i].prefill_pos:reqs[i].prefill_pos +
+                                                      counts[i]], np.int32) for i in ok]
+            pb = m.packed_batch(kv, [slots[i] for i in ok], [counts[i] for i in ok],
+                                np.concatenate(chunk), np.concatenate(maps))
             logits = m.forward_packed(pb, kv, self.cos, self.sin, rows="last")
-            kv.advance_device([slots[i] for i in ok], [len(reqs[i].prompt_tokens) for i in ok])
+            kv.advance_device([slots[i] for i in ok], [counts[i] for i in ok])
+            done = [j for j, i in enumerate(ok)
+                    if reqs[i].prefill_pos + counts[i] >= len(reqs[i].prompt_tokens)]
+            if not done:
+                return out
+            logits = logits[done] if len(done) < len(ok) else logits
+            ok = [ok[j] for j in done]
             V = logits.shape[-1]
             sp = SamplingParams.concat([self._params([reqs[i]], V) for i in ok])
             pd = torch.from_numpy(sp.packed()).to(logits.device)
