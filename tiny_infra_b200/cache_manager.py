@@ -97,20 +97,31 @@ class BlockAllocator:
         return out, updates
 
     def plan_decode(self, slots) -> np.ndarray:
-        """One new token per slot: the block each slot takes from the free list, or -1."""
+        """One new token per slot: the block each slot takes from the free list, or -1.  Same
+        order and error points as allocating slot by slot: blocks go to the slots that need one
+        in slot order; a slot at max_seq_len raises ValueError after the slots before it got
+        theirs, an empty free list RuntimeError after the ones that could be served."""
         bs = self.block_size
-        new_block = np.full(len(slots), -1, np.int32)
-        for i, b in enumerate(slots):
-            pos = int(self.seq_len[b])
-            if pos >= self.max_seq_len:
-                raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
-            lb = pos // bs
-            if self.block_tables[b, lb] == -1:
-                if not self.free_blocks:
-                    raise RuntimeError("OOM : No free physical blocks available for allocation.")
-                phys = self.free_blocks.popleft()
-                self.block_tables[b, lb] = phys
-                new_block[i] = phys
+        sl = np.asarray(slots, np.int64)
+        new_block = np.full(len(sl), -1, np.int32)
+        if len(sl) == 0:
+            return new_block
+        pos = self.seq_len[sl].astype(np.int64)
+        over = np.nonzero(pos >= self.max_seq_len)[0]
+        stop = int(over[0]) if len(over) else len(sl)
+        lb = pos[:stop] // bs
+        need = np.nonzero(self.block_tables[sl[:stop], lb] == -1)[0]
+        take = min(len(need), len(self.free_blocks))
+        if take:
+            phys = np.fromiter((self.free_blocks.popleft() for _ in range(take)), np.int32, take)
+            idx = need[:take]
+            self.block_tables[sl[idx], lb[idx]] = phys
+            new_block[idx] = phys
+        if take < len(need):
+            raise RuntimeError("OOM : No free physical blocks available for allocation.")
+        if stop < len(sl):
+            raise ValueError(f"Sequence length exceeds maximum allowed length for batch index "
+                             f"{int(sl[stop])}.")
         return new_block
 
     def advance(self, slots, n) -> None:
