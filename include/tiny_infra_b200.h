@@ -39,6 +39,14 @@ extern "C" {
 
 /* ---- library ---------------------------------------------------------------------------- */
 
+/* Launch order.  Every kernel of this library is launched with programmatic dependent launch:
+ * it may start while the previous kernel on the stream (if it is one of this library's) is
+ * still running, and waits for it before touching its inputs -- except the weight operands
+ * (ti_gemm's B, ti_gemm_qkv_rope's W, ti_rmsnorm's weight), which are fetched before that
+ * wait.  They must therefore not be outputs of this library's kernels still in flight on the
+ * same stream (weights written by other means, e.g. a copy, are fine).  The environment
+ * variable TI_PDL=0 turns programmatic dependent launch off (plain stream order). */
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* ti_last_error(void);
 /* ABI version of this library. */
@@ -131,7 +139,8 @@ int ti_swiglu(void* out, const void* x, int64_t num_tokens, int inter, int dtype
 /* ---- RMSNorm ----------------------------------------------------------------------------
  * models/qwen_25.py:24-36.  out[t] = w * (x[t] * rsqrt(mean(x[t]^2) + eps)), x float32 or
  * the activation dtype (x_dtype), out and w in `dtype`.  The normalised row is rounded to
- * `dtype` before the weight multiply, as the reference does. */
+ * `dtype` before the weight multiply, as the reference does.  `weight` is read before the
+ * kernel waits for the previous kernel on the stream (see "Launch order" above). */
 int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* weight, float eps,
                int num_tokens, int hidden, int dtype, void* stream);
 

@@ -165,6 +165,63 @@ __global__ void swiglu_kernel(T* __restrict__ out, const T* __restrict__ x, int6
 // ---- RMSNorm: one warp per row -------------------------------------------------------------
 // y = w * round(x * rstd): the normalised row is rounded to the output dtype before the weight
 // multiply, as models/qwen_25.py:36 does (`weight * hidden.to(input_dtype)`).
+// RMSNorm with the row in registers (hidden <= NC * 256): each lane holds NC chunks of 8
+// elements, so the row is read once; the (static) weight is loaded before the wait on the
+// previous kernel.  Rounding as the reference: bf16(w * bf16(x * rstd)) (models/qwen_25.py:34-36).
+template <typename TX, typename T, int NC>
+__global__ void rmsnorm_reg_kernel(T* __restrict__ out, const TX* __restrict__ x,
+                                   const T* __restrict__ w, float eps, int rows, int H) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  float wf[NC][8];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int c = lane * 8 + k * 256;
+    if (c < H) {
+      Vec8<T> wv;
+      wv.load(w + c);
+      wv.to_float(wf[k]);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int r = warp; r < rows; r += nwarps) {
+    const TX* xr = x + (int64_t)r * H;
+    float f[NC][8];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      const int c = lane * 8 + k * 256;
+      if (c < H) {
+        if constexpr (sizeof(TX) == 4) load8f(reinterpret_cast<const float*>(xr) + c, f[k]);
+        else { Vec8<TX> v; v.load(xr + c); v.to_float(f[k]); }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      if (lane * 8 + k * 256 < H) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += f[k][j] * f[k][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      const int c = lane * 8 + k * 256;
+      if (c < H) {
+        float o8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o8[j] = wf[k][j] * Elem<T>::to_f(Elem<T>::from_f(f[k][j] * rstd));
+        Vec8<T> o;
+        o.from_float(o8);
+        o.store(out + (int64_t)r * H + c);
+      }
+    }
+  }
+}
+
 template <typename TX, typename T>
 __global__ void rmsnorm_kernel(T* __restrict__ out, const TX* __restrict__ x,
                                const T* __restrict__ w, float eps, int rows, int H) {
@@ -341,6 +398,18 @@ extern "C" int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* wei
   const int64_t work = (int64_t)num_tokens * 32;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int g = ew::grid_for(work);
+  if (hidden <= 1024) {   // the row in registers: one read of x
+#define TI_RMS_REG(TX, T)                                                                      \
+  return launch_kernel("rmsnorm launch", ew::rmsnorm_reg_kernel<TX, T, 4>, dim3(g),              \
+                       dim3(ew::kThreads), 0, s, 1, (T*)out, (const TX*)x, (const T*)weight, eps, \
+                       num_tokens, hidden)
+    if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_FP32) TI_RMS_REG(float, __nv_bfloat16);
+    if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_BF16) TI_RMS_REG(__nv_bfloat16, __nv_bfloat16);
+    if (dtype == TI_DTYPE_FP16 && x_dtype == TI_DTYPE_FP32) TI_RMS_REG(float, __half);
+    if (dtype == TI_DTYPE_FP16 && x_dtype == TI_DTYPE_FP16) TI_RMS_REG(__half, __half);
+#undef TI_RMS_REG
+    return set_error(TI_ERR_UNSUPPORTED, "rmsnorm: unsupported dtype combination");
+  }
   if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_FP32)
     return launch_kernel("rmsnorm launch", ew::rmsnorm_kernel<float, __nv_bfloat16>,
                          dim3(g), dim3(ew::kThreads), 0, s, 1,
