@@ -1277,8 +1277,8 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
 
 // v4 split-K merge: one CTA per (sequence, unit of HP kv heads), one thread per (query head of
 // the unit, 4 dims).  Units that v4 did not split (pieces == 1) or that have no blocks are left
-// as they are.  All of a thread's partials are loaded in one round: this runs right after the
-// attention kernel (programmatic dependent launch) and costs about two L2 round trips.
+// as they are.  Two rounds of loads (context length and piece count, then all of the unit's
+// partials): this runs right after the attention kernel (programmatic dependent launch).
 template <typename T>
 __global__ void __launch_bounds__(256)
 merge_pieces_kernel(Params p, int units, int nheads) {
@@ -1286,18 +1286,18 @@ merge_pieces_kernel(Params p, int units, int nheads) {
   pdl_launch_dependents();
   const int pair = blockIdx.x;
   const int row = pair / units, unit = pair % units;
-  if (p.context_lens[row] <= 0) return;   // no blocks: the row is left untouched
-  const int pieces = p.ws_pieces[pair];
-  if (pieces <= 1) return;
   const int h = threadIdx.x >> 4, d4 = threadIdx.x & 15;
   if (h >= nheads) return;
+  const int ctx = p.context_lens[row];      // both loads in one round trip
+  const int pieces = p.ws_pieces[pair];
+  if (ctx <= 0 || pieces <= 1) return;   // no blocks (row left untouched) or not split
   const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
   const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
   int st[kV2MaxPieces];
   float2 ml[kV2MaxPieces];
   float4 v[kV2MaxPieces];
 #pragma unroll
-  for (int q = 0; q < kV2MaxPieces; ++q) {
+  for (int q = 0; q < kV2MaxPieces; ++q) {   // all partials of the unit in one round
     if (q < pieces) {
       st[q] = stops[q];
       ml[q] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
