@@ -125,6 +125,33 @@ def test_attention_256_ragged(cuda_device):
     assert ok, err
 
 
+@pytest.mark.parametrize("kernel", ["v5", "v4", "v2"])
+def test_attention_each_kernel(cuda_device, monkeypatch, kernel):
+    """The equivalent head_dim-64 decode kernels selected in turn (TI_PAGED_ATTN_KERNEL): v5
+    (producer warp + warp pairs), v4 (a TMA ring per warp), v2 (persistent ring): a ragged
+    batch, long split-K contexts (units cut into up to 16 pieces), four kv heads (two units per
+    sequence) and the edge cases of test_attention_edge_cases."""
+    monkeypatch.setenv("TI_PAGED_ATTN_KERNEL", kernel)
+    cases = [(4, 256, 14, 2, 64, 256 * 128, 128, 2048), (1, 12, 14, 2, 64, 3200, 1, 4096),
+             (5, 40, 16, 4, 64, 2000, 1, 700)]
+    for c in cases:
+        q, k, v, bt, ctx = _attn_case(*c)
+        out, ref = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx)
+        ok, err = _attn_ok(out, ref)
+        assert ok, (c, err)
+    q, k, v, bt, ctx = _attn_case(2, 6, 14, 2, 64, 600, 200, 1500)
+    ctx[0] = 0
+    bt[1, 3] = -1
+    bt[2, 20] = -1
+    bt[3, 0] = -1
+    bt[4, 5] = 600 + 7
+    out, ref = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx, init=7.0)
+    assert (out[0] == 7.0).all()
+    assert np.isnan(out[3]).all() and np.isnan(ref[3]).all()
+    ok, err = _attn_ok(out[[0, 1, 2, 4, 5]], ref[[0, 1, 2, 4, 5]])
+    assert ok, err
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 def test_rope_inplace(cuda_device, dtype):
     """custom_rope.apply_inplace on a packed ragged batch: T=4096, positions in [0, 32768)."""

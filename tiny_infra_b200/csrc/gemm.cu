@@ -428,9 +428,15 @@ struct Cfg {
   static constexpr int kSmem = kRing + 1024;
   static_assert(2 * kBarBytes <= 1024, "barriers fit beside the ring in the 1 KB slack");
   static_assert(CL == 1 || kW % 4 == 0, "cluster chunks must be multiples of 4 columns");
-  static_assert(kStageOff + kRows * BN * 4 <= kRing, "partials and staged tile fit the ring");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
+
+// Whether the cluster partials and the staged output tile fit the drained stage ring.
+template <typename T, int BN, int STAGES, int KIND, int CL>
+constexpr bool ring_fits() {
+  using C = Cfg<BN, STAGES, CL>;
+  return C::kStageOff + C::kRows * Out<T, BN, KIND>::kBytes <= C::kRing;
+}
 
 // One 128 x BN output tile per cluster of CL CTAs (CL = split-K factor along grid z).
 template <typename T, int BN, int STAGES, int KIND, int CL>
@@ -438,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
             int K, int kb_per_split, EpiArgs e) {
   using C = Cfg<BN, STAGES, CL>;
+  static_assert(ring_fits<T, BN, STAGES, KIND, CL>(), "partials and staged tile fit the ring");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -505,24 +512,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     }
     __syncwarp();
   } else if (warp >= 2) {
-    // Producers: lane 0 of each epilogue warp issues the TMA loads of every 4th K block (one
-    // issuing thread's loads complete one after another, four streams overlap).
-    if (lane == 0) {
+    // Producers: lane 0 of kProd epilogue warps issues the TMA loads of every kProd-th K block
+    // (one issuing thread's loads complete one after another, the streams overlap).  The empty
+    // barrier waits are parity waits: a producer about to refill a stage for its u-th use must
+    // know that use u - 2 was consumed, which holds when its own previous K block (kProd
+    // earlier) waited for a consumption at least STAGES - kProd blocks later than that use,
+    // hence kProd <= STAGES.
+    constexpr int kProd = STAGES < 4 ? STAGES : 4;
+    if (lane == 0 && warp - 2 < kProd) {
       const int p = warp - 2;
       const uint64_t pol_a = l2_policy_evict_last();    // activations: re-read by many CTAs
       const uint64_t pol_b = l2_policy_evict_first();   // weights: streamed once
       // Weights do not depend on earlier kernels: fetch the first stages' B tiles before
       // waiting for the producer of the activations.
       const int pre_n = min(nk, STAGES);
-      for (int it = p; it < pre_n; it += 4) {
+      for (int it = p; it < pre_n; it += kProd) {
         mbar_arrive_expect_tx(full0 + 8 * it, C::kStage);
         tma_load_2d_hint(sbase + it * C::kStage + C::kABytes, &bmap, full0 + 8 * it,
                          (kb0 + it) * BK, n0, pol_b);
       }
       pdl_wait();
-      for (int it = p; it < pre_n; it += 4)
+      for (int it = p; it < pre_n; it += kProd)
         tma_load_2d_hint(sbase + it * C::kStage, &amap, full0 + 8 * it, (kb0 + it) * BK, m0, pol_a);
-      for (int it = p; it < nk; it += 4) {
+      for (int it = p; it < nk; it += kProd) {
         if (it < pre_n) continue;
         const int s = it % STAGES;
         if (!mbar_wait(empty0 + 8 * s, ((it / STAGES) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
@@ -859,54 +871,62 @@ static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols
 template <typename T, int BN, int STAGES, int KIND, int CL>
 static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                     const EpiArgs& e, cudaStream_t s, int zsplits = 1) {
-  using C = Cfg<BN, STAGES, CL>;
-  auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
-  static int set_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (set_dev != dev) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (err != cudaSuccess) return set_cuda_error(err, "cudaFuncSetAttribute(gemm)");
-    set_dev = dev;
+  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL>()) {
+    return set_error(TI_ERR_UNSUPPORTED, "gemm: this tile width and epilogue do not fit the stage ring");
+  } else {
+    using C = Cfg<BN, STAGES, CL>;
+    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
+    static int set_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (set_dev != dev) {
+      cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+      if (err != cudaSuccess) return set_cuda_error(err, "cudaFuncSetAttribute(gemm)");
+      set_dev = dev;
+    }
+    const int nkb = K / BK;
+    const int zs = CL > 1 ? CL : zsplits;
+    const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
+    dim3 grid(N / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
+    return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, K, per, e);
   }
-  const int nkb = K / BK;
-  const int zs = CL > 1 ? CL : zsplits;
-  const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
-  dim3 grid(N / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
-  return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, K, per, e);
 }
 
 // How many clusters of CL CTAs of this kernel the GPU keeps resident at once (a cluster needs
 // CL free SMs in one GPC, so this is below 148 / CL); cached per device.
 template <typename T, int BN, int STAGES, int KIND, int CL>
 static int max_clusters() {
-  static int cached_dev = -1, value = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (cached_dev != dev) {
-    using C = Cfg<BN, STAGES, CL>;
-    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1, 1, CL);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = C::kSmem;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = CL;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      (void)cudaGetLastError();
-      n = 148 / CL / 2;   // conservative when the query is unavailable
+  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL>()) {
+    return 0;
+  } else {
+    static int cached_dev = -1, value = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cached_dev != dev) {
+      using C = Cfg<BN, STAGES, CL>;
+      auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, CL);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = C::kSmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 1;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = CL;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = 148 / CL / 2;   // conservative when the query is unavailable
+      }
+      value = n;
+      cached_dev = dev;
     }
-    value = n;
-    cached_dev = dev;
+    return value;
   }
-  return value;
 }
 
 // split-K factor -> cluster size: 1, 2, 4 or 8 (the largest power of two <= split, at most 8)
@@ -943,14 +963,23 @@ static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int
   }
 }
 
+#ifndef TI_GEMM_STAGES_64
+#define TI_GEMM_STAGES_64 8
+#endif
+#ifndef TI_GEMM_STAGES_128
+#define TI_GEMM_STAGES_128 6
+#endif
+#ifndef TI_GEMM_STAGES_256
+#define TI_GEMM_STAGES_256 4
+#endif
 // Ring depth per tile width: about 192 KB of loads in flight for the one CTA on the SM.
 template <typename T, int KIND>
 static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
                        int K, const EpiArgs& e, cudaStream_t s) {
   switch (bn) {
-    case 64: return dispatch_cl<T, 64, 8, KIND>(cl, am, bm, M, N, K, e, s);
-    case 128: return dispatch_cl<T, 128, 6, KIND>(cl, am, bm, M, N, K, e, s);
-    case 256: return launch_t<T, 256, 4, KIND, 1>(am, bm, M, N, K, e, s);   // never split
+    case 64: return dispatch_cl<T, 64, TI_GEMM_STAGES_64, KIND>(cl, am, bm, M, N, K, e, s);
+    case 128: return dispatch_cl<T, 128, TI_GEMM_STAGES_128, KIND>(cl, am, bm, M, N, K, e, s);
+    case 256: return launch_t<T, 256, TI_GEMM_STAGES_256, KIND, 1>(am, bm, M, N, K, e, s);   // never split
     default: return set_error(TI_ERR_UNSUPPORTED, "gemm: block_n must be 64, 128 or 256");
   }
 }
@@ -959,7 +988,7 @@ static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap&
 template <typename T>
 static int launch_qkv(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                       const EpiArgs& e, cudaStream_t s) {
-  return dispatch_cl<T, 64, 8, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
+  return dispatch_cl<T, 64, TI_GEMM_STAGES_64, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
 }
 
 }  // namespace gemm

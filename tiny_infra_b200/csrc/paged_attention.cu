@@ -23,6 +23,8 @@
 //   * Four warps per CTA; each warp owns every fourth block of the partition and keeps its own
 //     online-softmax state; the CTA merges the four states in shared memory.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -945,9 +947,12 @@ __device__ __forceinline__ void swapped_block(uint32_t kb, uint32_t vb, uint8_t*
                                               float (&o)[4][4]) {
   const int g = lane >> 2, t4 = lane & 3;
   if (valid < kBlock) {
-    // zero the V rows past the context so that 0 * (stale value) cannot produce NaN
+    // zero the V rows past the context so that 0 * (stale value) cannot produce NaN; the
+    // proxy fence orders these generic-proxy writes before the TMA that later refills the
+    // stage (the only generic writes to the ring)
     for (int i = lane; i < (kBlock - valid) * 8; i += 32)
       *reinterpret_cast<uint4*>(vt + swz128(valid + i / 8, i & 7)) = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
   }
   // ---- S^T = K Q^T : rows = tokens g, g+8; columns = heads 2t4, 2t4+1
@@ -1040,6 +1045,74 @@ constexpr int kV4Warps = 12;
 constexpr int kV4Stages = 2;
 constexpr int kV4IdCap = 2048;
 
+// Stream prologue of the v4 / v5 kernels (all NT threads of the CTA call it).
+//  * s_off[r] = first stream position of sequence r (KVU units of its blocks, unit-major),
+//    s_off[batch] = total;
+//  * chunk = stream positions per consumer (`streams` consumers per CTA); this CTA's range is
+//    [cb, ce), resolved into ids[] (TMA row coordinate of the unit's first kv head, -1 for a
+//    negative or out-of-pool block-table entry) and vtok[] (valid tokens of the block).
+// Returns false (uniformly) when the CTA has no positions.  The leading __syncthreads also
+// publishes barrier initialisation done by the caller before the call.
+template <int HP, int NT>
+__device__ __forceinline__ bool resolve_stream(const Params& p, int batch, int streams, int* s_off,
+                                               int* ids, uint8_t* vtok, int* s_wsum, int& chunk,
+                                               int& cb, int& ce) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVH = p.num_kv_heads;
+  const int KVU = KVH / HP;
+  auto nblk_of = [&](int r) {
+    const int ctx = p.context_lens[r];
+    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
+  };
+  const int per = (batch + NT - 1) / NT;
+  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
+  int local = 0;
+  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_wsum[w];
+  for (int r = r0; r < r1; ++r) {
+    s_off[r] = run;
+    run += KVU * nblk_of(r);
+  }
+  if (tid == 0) {
+    int tot = 0;
+    for (int w = 0; w < NT / 32; ++w) tot += s_wsum[w];
+    s_off[batch] = tot;
+  }
+  __syncthreads();
+  const int total = s_off[batch];
+  chunk = v2_chunk(total, gridDim.x * streams, p.max_blocks);
+  cb = blockIdx.x * streams * chunk;
+  if (cb >= total) return false;
+  ce = min(total, cb + streams * chunk);
+  for (int q = tid; q < ce - cb; q += NT) {
+    const int pos = cb + q;
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
+    const int rel = pos - s_off[lo];
+    const int unit = rel / nb, j = rel - unit * nb;
+    const int brow = p.row_index ? p.row_index[lo] : lo;
+    const int phys = p.block_tables[(int64_t)brow * p.bt_stride + j];
+    const bool bad = phys < 0 || (int64_t)phys >= p.num_blocks;
+    ids[q] = bad ? -1 : (phys * KVH + unit * HP) * kBlock;
+    vtok[q] = (uint8_t)min(kBlock, p.context_lens[lo] - j * kBlock);
+  }
+  __syncthreads();
+  return true;
+}
+
 template <int HP>
 struct CfgV4 {
   static constexpr int kTile = HP * kBlock * 64 * 2;
@@ -1057,6 +1130,10 @@ template <typename T, int HP>
 __global__ void __launch_bounds__(kV4Warps * 32, 1)
 decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
                  const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  if (threadIdx.x == 0) {   // descriptors are kernel parameters: independent of earlier kernels
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
   pdl_wait();
   pdl_launch_dependents();
   using C = CfgV4<HP>;
@@ -1068,70 +1145,18 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
   uint8_t* vtok = smem + C::kRing + C::kBars + C::kIds;
   int* s_off = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kIds + C::kVtok);
   constexpr int kThreads = kV4Warps * 32;
-  __shared__ int s_wsum[kV4Warps];
+  __shared__ int s_wsum[kThreads / 32];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KVH = p.num_kv_heads;
   const int KVU = KVH / HP;
-  auto nblk_of = [&](int r) {
-    const int ctx = p.context_lens[r];
-    return ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
-  };
-
-  // ---- prefix sum of KVU * blocks per sequence
-  const int per = (batch + kThreads - 1) / kThreads;
-  const int r0 = min(batch, tid * per), r1 = min(batch, r0 + per);
-  int local = 0;
-  for (int r = r0; r < r1; ++r) local += KVU * nblk_of(r);
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) s_wsum[warp] = incl;
   if (tid < kV4Warps * kV4Stages) {
     mbar_init(bar_all + 8 * tid, 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  int run = incl - local;
-  for (int w = 0; w < warp; ++w) run += s_wsum[w];
-  for (int r = r0; r < r1; ++r) {
-    s_off[r] = run;
-    run += KVU * nblk_of(r);
-  }
-  if (tid == 0) {
-    int tot = 0;
-    for (int w = 0; w < kV4Warps; ++w) tot += s_wsum[w];
-    s_off[batch] = tot;
-  }
-  __syncthreads();
-  const int total = s_off[batch];
-  const int W = gridDim.x * kV4Warps;
-  const int chunk = v2_chunk(total, W, p.max_blocks);
-  const int cb = blockIdx.x * kV4Warps * chunk;
-  if (cb >= total) return;
-  const int ce = min(total, cb + kV4Warps * chunk);
-
-  // ---- resolve the CTA's positions: TMA row coordinate (-1 = stop) and valid tokens
-  for (int q = tid; q < ce - cb; q += kThreads) {
-    const int pos = cb + q;
-    int lo = 0, hi = batch;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (s_off[mid] <= pos) lo = mid; else hi = mid;
-    }
-    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
-    const int rel = pos - s_off[lo];
-    const int unit = rel / nb, j = rel - unit * nb;
-    const int brow = p.row_index ? p.row_index[lo] : lo;
-    const int phys = p.block_tables[(int64_t)brow * p.bt_stride + j];
-    const bool bad = phys < 0 || (int64_t)phys >= p.num_blocks;
-    ids[q] = bad ? -1 : (phys * KVH + unit * HP) * kBlock;
-    vtok[q] = (uint8_t)min(kBlock, p.context_lens[lo] - j * kBlock);
-  }
-  __syncthreads();
+  int chunk, cb, ce;
+  if (!resolve_stream<HP, kThreads>(p, batch, kV4Warps, s_off, ids, vtok, s_wsum, chunk, cb, ce))
+    return;
 
   int pos = min(ce, cb + warp * chunk);
   const int end = min(ce, pos + chunk);
@@ -1162,7 +1187,8 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
     if (lane == 0) {
       const int st = issued % kV4Stages;
       const uint32_t dst = smem_u32(ring + st * C::kStage);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      // Reads of the stage by ldmatrix completed before the MMAs that consume them issued;
+      // the zeroing writes fenced themselves (swapped_block).
       mbar_arrive_expect_tx(bar + 8 * st, C::kStage);
       const int y = ids[ip - cb];
       tma_load_2d_hint(dst, &kmap, bar + 8 * st, 0, y, pol);
@@ -1335,6 +1361,235 @@ merge_pieces_kernel(Params p, int units, int nheads) {
   *reinterpret_cast<uint2*>(dst) = u;
 }
 
+// ==========================================================================================
+// v5: one producer warp and pairs of consumer warps (head_dim 64, units of two kv heads,
+// GQA groups <= 8)
+//
+// Same block stream, chunking (one chunk per warp PAIR), pieces, split-K workspace and merge
+// as v4.  Warp 0 (lane 0) issues every TMA load of the CTA: per pair a kV5Stages-deep ring,
+// each stage the K and V tiles of one block for both kv heads of the unit (two 4 KB boxes).
+// The two warps of a pair read the same stage, warp 2i+1 computing the first kv head and warp
+// 2i+2 the second (swapped_block), and release it through an empty barrier of count 2.  With
+// the issue off the consumers and one head per consumer, a pair finishes a block in about the
+// time v4 spends on one of its two heads.
+// ==========================================================================================
+constexpr int kV5Pairs = 8;
+constexpr int kV5Stages = 3;
+constexpr int kV5Threads = (1 + 2 * kV5Pairs) * 32;
+
+struct CfgV5 {
+  static constexpr int kTile = 2 * kBlock * 64 * 2;          // K (or V) of one block, 2 heads
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kRing = kV5Pairs * kV5Stages * kStage;   // 192 KB
+  static constexpr int kBars = 2 * kV5Pairs * kV5Stages * 8;    // full, then empty
+  static constexpr int kIds = kV4IdCap * 4;
+  static constexpr int kVtok = kV4IdCap;
+  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
+  static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
+  static_assert(kTotal <= 227 * 1024, "v5 shared memory");
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kV5Threads, 1)
+decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
+                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+  if (threadIdx.x == 0) {   // descriptors are kernel parameters: independent of earlier kernels
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  using C = CfgV5;
+  constexpr int kSlots = kV5Pairs * kV5Stages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t full0 = smem_u32(smem + C::kRing);     // [pair][stage]
+  const uint32_t empty0 = full0 + kSlots * 8;
+  int* ids = reinterpret_cast<int*>(smem + C::kRing + C::kBars);
+  uint8_t* vtok = smem + C::kRing + C::kBars + C::kIds;
+  int* s_off = reinterpret_cast<int*>(smem + C::kRing + C::kBars + C::kIds + C::kVtok);
+  __shared__ int s_wsum[kV5Threads / 32];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVU = p.num_kv_heads / 2;
+  if (tid < kSlots) {
+    mbar_init(full0 + 8 * tid, 1);    // the producer's arrive + the two tiles' bytes
+    mbar_init(empty0 + 8 * tid, 2);   // one arrive per consumer warp of the pair
+    fence_mbar_init();
+  }
+  int chunk, cb, ce;
+  if (!resolve_stream<2, kV5Threads>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb, ce))
+    return;
+  // end of the unit that contains stream position pp
+  auto unit_end = [&](int pp) {
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pp) lo = mid; else hi = mid;
+    }
+    const int nb = (s_off[lo + 1] - s_off[lo]) / KVU;
+    return s_off[lo] + ((pp - s_off[lo]) / nb + 1) * nb;
+  };
+
+  if (warp == 0) {
+    // ---- producer: lane i issues the loads of pair i, a load whenever the pair's next stage
+    // is free (one SIMT test of all pairs' barriers per round).  The issue cursor skips the rest
+    // of a unit after a negative entry, as the consumers do.
+    if (lane >= kV5Pairs) return;
+    const uint64_t pol = l2_policy_evict_first();
+    int ip = min(ce, cb + lane * chunk);
+    const int iend = min(ce, ip + chunk);
+    while (ip < iend && ids[ip - cb] < 0) ip = min(iend, unit_end(ip));
+    int issued = 0, idle = 0;
+    long long t0 = clock64();
+    while (ip < iend) {
+      const int st = issued % kV5Stages;
+      const int use = issued / kV5Stages;
+      const int slot = lane * kV5Stages + st;
+      // stage reuse: wait for the consumption of its previous use (phase use - 1)
+      if (use == 0 || mbar_test_wait(empty0 + 8 * slot, (use - 1) & 1)) {
+        const uint32_t fb = full0 + 8 * slot;
+        const uint32_t dst = smem_u32(smem + slot * C::kStage);
+        mbar_arrive_expect_tx(fb, C::kStage);
+        const int y = ids[ip - cb];
+        tma_load_2d_hint(dst, &kmap, fb, 0, y, pol);
+        tma_load_2d_hint(dst + C::kTile, &vmap, fb, 0, y, pol);
+        ++issued;
+        ++ip;
+        while (ip < iend && ids[ip - cb] < 0) ip = min(iend, unit_end(ip));
+        t0 = clock64();
+        idle = 0;
+      } else if (clock64() - t0 > kWaitCycles) {
+        raise_device_error(TI_DEVERR_ATTN_WAIT);   // the pair's consumers time out as well
+        break;
+      } else if (++idle > 64) {
+        __nanosleep(32);   // long waits only: a sleeping lane would miss the free stage
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  const int cw = warp - 1, pr = cw >> 1, sub = cw & 1;
+  int pos = min(ce, cb + pr * chunk);
+  const int end = min(ce, pos + chunk);
+  if (pos >= end) return;
+  uint8_t* ring = smem + pr * kV5Stages * C::kStage;
+  const uint32_t fullp = full0 + pr * kV5Stages * 8, emptyp = empty0 + pr * kV5Stages * 8;
+  const int G = p.group;
+  const int g = lane >> 2, t4 = lane & 3;
+  int consumed = 0;
+  uint32_t phase = 0;
+  uint32_t qb[4][2];
+  float m[2], l[2], o[4][4];
+
+  while (pos < end) {
+    // ---- a piece: positions of one unit inside [pos, end)
+    int lo = 0, hi = batch;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_off[mid] <= pos) lo = mid; else hi = mid;
+    }
+    const int row = lo;
+    const int nb = (s_off[row + 1] - s_off[row]) / KVU;
+    const int unit = (pos - s_off[row]) / nb;
+    const int pstart = s_off[row] + unit * nb;
+    const int pend = min(end, pstart + nb);
+    const int piece = pos / chunk - pstart / chunk;
+    const int pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
+    const int head0 = (unit * 2 + sub) * G;   // first query head of this warp's kv head
+    {
+      const T* qh = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride +
+                    (int64_t)(head0 + g) * 64;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qb[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t4) : 0u;
+        qb[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t4) : 0u;
+      }
+      m[0] = m[1] = -INFINITY;
+      l[0] = l[1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    }
+    int stop = 0;
+    for (; pos < pend; ++pos) {
+      if (ids[pos - cb] < 0) { stop = 1; pos = pend; break; }
+      const int st = consumed % kV5Stages;
+      if (!mbar_wait(fullp + 8 * st, (phase >> st) & 1u, TI_DEVERR_ATTN_WAIT)) return;
+      phase ^= 1u << st;
+      uint8_t* kt = ring + st * C::kStage + sub * kBlock * 128;
+      uint8_t* vt = ring + st * C::kStage + C::kTile + sub * kBlock * 128;
+      swapped_block<T>(smem_u32(kt), smem_u32(vt), vt, vtok[pos - cb], lane, qb, p.scale_log2, m, l,
+                       o);
+      __syncwarp();                    // every lane is done with the stage before it is released
+      if (lane == 0) mbar_arrive(emptyp + 8 * st);
+      ++consumed;
+    }
+    // ---- finish the piece: lane holds heads (2t4, 2t4+1) x dims (16mt+g, 16mt+g+8)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) l[j] += __shfl_xor_sync(0xffffffffu, l[j], off);
+    const int64_t pair = (int64_t)row * KVU + unit;
+    if (piece == 0 && sub == 0 && lane == 0) p.ws_pieces[pair] = pieces;   // merge_pieces_kernel
+    if (pieces == 1) {
+      T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hl = 2 * t4 + j;
+        if (hl >= G) continue;
+        const float inv = 1.f / l[j];                 // l == 0 -> NaN (attention.cu:150)
+        T* oh = outp + (int64_t)(head0 + hl) * 64;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          oh[mt * 16 + g] = Elem<T>::from_f(o[mt][j] * inv);
+          oh[mt * 16 + g + 8] = Elem<T>::from_f(o[mt][2 + j] * inv);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hl = 2 * t4 + j;
+        if (hl >= G) continue;
+        const int64_t sl = ((int64_t)row * p.num_heads + head0 + hl) * p.max_parts + piece;
+        float* wo = p.ws_o + sl * 64;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          wo[mt * 16 + g] = o[mt][j];
+          wo[mt * 16 + g + 8] = o[mt][2 + j];
+        }
+        if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[j], l[j]);
+      }
+      if (sub == 0 && lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
+    }
+  }
+}
+
+template <typename T>
+static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
+                     cudaStream_t stream) {
+  using C = CfgV5;
+  static int set_dev = -1;
+  static int sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v5<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v5)");
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    set_dev = dev;
+  }
+  int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T>, dim3(sms),
+                         dim3(kV5Threads), C::kTotal, stream, 1, km, vm, p, batch);
+  if (rc) return rc;
+  const int units = p.num_kv_heads / 2;
+  return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
+                       dim3(batch * units), dim3(256), 0, stream, 1, p, units, 2 * p.group);
+}
+
 template <typename T, int HP>
 static int launch_v4(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
                      cudaStream_t stream) {
@@ -1377,6 +1632,13 @@ static int launch_v2(const Params& p, const CUtensorMap& km, const CUtensorMap& 
   }
   return launch_kernel("paged attention v2 launch", decode_kernel_v2<T, HP>, dim3(sms),
                        dim3(C::kWarps * 32), C::kTotal, stream, 1, km, vm, p, batch);
+}
+
+// TI_PAGED_ATTN_KERNEL=v2|v4|v5 restricts the choice among the equivalent head_dim-64 kernels
+// (for comparisons and tests; a kernel that cannot serve the call is still skipped).
+static int forced_kernel() {
+  const char* e = getenv("TI_PAGED_ATTN_KERNEL");
+  return !e ? 0 : !strcmp(e, "v2") ? 2 : !strcmp(e, "v4") ? 4 : !strcmp(e, "v5") ? 5 : 0;
 }
 
 // Partition size (KV blocks per split-K CTA of the v1 kernel) used when the caller passes 0.
@@ -1487,8 +1749,14 @@ extern "C" int ti_paged_attention_decode(
       if (sms <= 0) sms = 148;
     }
     const int64_t worst = (int64_t)batch * (num_kv_heads / hp) * max_blocks_per_seq;
+    const int forced = attn::forced_kernel();
+    if (hp == 2 && p.group <= 8 && (forced == 0 || forced == 5) &&
+        attn::v2_chunk(worst, sms * attn::kV5Pairs, max_blocks_per_seq) * attn::kV5Pairs <=
+            attn::kV4IdCap)
+      return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16>(p, km, vm, batch, s)
+                                    : attn::launch_v5<__half>(p, km, vm, batch, s);
     const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq);
-    if (p.group <= 8 && chunk_ub * attn::kV4Warps <= attn::kV4IdCap) {
+    if (p.group <= 8 && forced != 2 && chunk_ub * attn::kV4Warps <= attn::kV4IdCap) {
       if (hp == 2)
         return dtype == TI_DTYPE_BF16 ? attn::launch_v4<__nv_bfloat16, 2>(p, km, vm, batch, s)
                                       : attn::launch_v4<__half, 2>(p, km, vm, batch, s);
