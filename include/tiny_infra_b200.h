@@ -32,10 +32,12 @@ extern "C" {
 #define TI_ERR_CUDA 3
 #define TI_ERR_WORKSPACE 4
 
-/* Bits of the device status word (ti_device_status): a bounded wait inside a kernel gave up. */
+/* Bits of the device status word (ti_device_status): a bounded wait inside a kernel gave up,
+ * or a kernel rejected an input it cannot check on the host. */
 #define TI_DEVERR_ATTN_WAIT 0x1u
 #define TI_DEVERR_GEMM_WAIT 0x2u
 #define TI_DEVERR_PREFILL_WAIT 0x4u
+#define TI_DEVERR_ATTN_PLAN 0x8u   /* a planned attention call got a plan of another batch */
 
 /* ---- library ---------------------------------------------------------------------------- */
 
@@ -86,6 +88,33 @@ int ti_paged_attention_decode(void* out, int64_t out_seq_stride, const void* q,
                               int num_heads, int num_kv_heads, int head_dim, int block_size,
                               int max_blocks_per_seq, int dtype, int partition_blocks,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- decode attention plan ------------------------------------------------------------------
+ * No counterpart in the reference.  A decode step calls the attention once per layer with the
+ * same batch (context_lens, block tables).  ti_paged_attention_plan resolves that batch once --
+ * the split of all sequences' KV blocks over the GPU's attention consumers, each position's
+ * pool row and valid-token count -- into a caller buffer of ti_paged_attention_plan_bytes(batch)
+ * bytes (16-byte aligned).  ti_paged_attention_decode_planned computes exactly what
+ * ti_paged_attention_decode does (default partitioning) but loads the plan instead of
+ * rebuilding it.  The plan stays valid while context_lens and the block tables are unchanged; the calls
+ * that read it must follow it on the same stream.  A plan of another batch raises
+ * TI_DEVERR_ATTN_PLAN.  For shapes the planned kernel does not serve (head_dim != 64, an odd
+ * number of kv heads, more than 8 query heads per kv head, batch > 4096, contexts too long for
+ * the batch size) the plan is a zero header and the planned call behaves as the plain one. */
+size_t ti_paged_attention_plan_bytes(int batch);
+int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_stride,
+                            const int32_t* row_index, const int32_t* context_lens, int batch,
+                            int num_heads, int num_kv_heads, int head_dim, int max_blocks_per_seq,
+                            int64_t num_blocks, void* plan, size_t plan_bytes, void* stream);
+int ti_paged_attention_decode_planned(void* out, int64_t out_seq_stride, const void* q,
+                                      int64_t q_seq_stride, const void* k_cache,
+                                      const void* v_cache, int64_t num_blocks,
+                                      const int32_t* block_tables, int64_t bt_stride,
+                                      const int32_t* row_index, const int32_t* context_lens,
+                                      int batch, int num_heads, int num_kv_heads, int head_dim,
+                                      int block_size, int max_blocks_per_seq, int dtype,
+                                      void* workspace, size_t workspace_bytes, const void* plan,
+                                      void* stream);
 
 /* ---- paged decode attention without caller scratch ---------------------------------------------
  * No counterpart in the reference.  Same computation and arguments as

@@ -1,0 +1,120 @@
+"""The per-step attention plan (ti_paged_attention_plan) and the attention call that reads it
+(ti_paged_attention_decode_planned), through the C ABI.
+
+* the planned call runs the same kernel with the same split of the batch as the plain call, so
+  its output must equal the plain call's bit for bit (ragged batches, long contexts cut into
+  many pieces, four kv heads, negative and out-of-pool block-table entries, empty rows);
+* a plan of another batch is rejected on the device (TI_DEVERR_ATTN_PLAN), the context stays
+  usable; the plan buffer is sized for the larger batch so every read stays inside it;
+* a shape the planned kernel does not serve (head_dim 128) gets a zero header and the planned
+  call equals the plain one.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, B, NH, KVH, D, NB, lo, hi, dev):
+    rng = np.random.default_rng(seed)
+    bs = 16
+    ctx = rng.integers(lo, hi + 1, B).astype(np.int32)
+    mb = (hi + bs - 1) // bs
+    perm = rng.permutation(NB)
+    bt = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        n = (int(ctx[b]) + bs - 1) // bs
+        bt[b, :n] = perm[off:off + n]
+        off += n
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, NH, D, device=dev, generator=g).bfloat16()
+    k = torch.randn(NB, KVH, bs, D, device=dev, generator=g).bfloat16()
+    v = torch.randn(NB, KVH, bs, D, device=dev, generator=g).bfloat16()
+    return q, k, v, bt, ctx, mb
+
+
+def _args(q, k, v, bt, ctx, mb, out):
+    B, NH, D = q.shape
+    NB, KVH = k.shape[0], k.shape[1]
+    return [out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(),
+            NB, bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), B, NH, KVH, D, 16, mb]
+
+
+def _plain_and_planned(lib, N, q, k, v, bt_np, ctx_np, mb, plan_batch=None):
+    dev = q.device
+    B, NH, D = q.shape
+    NB, KVH = k.shape[0], k.shape[1]
+    bt, ctx = torch.from_numpy(bt_np).to(dev), torch.from_numpy(ctx_np).to(dev)
+    s = torch.cuda.current_stream().cuda_stream
+    need = lib.ti_paged_attention_workspace_bytes(B, NH, KVH, D, mb, 0)
+    ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    ref = torch.full_like(q, 3.0)
+    N.check(lib.ti_paged_attention_decode(*_args(q, k, v, bt, ctx, mb, ref), N.dtype_code(q.dtype),
+                                          0, ws.data_ptr(), need, s))
+    plan = torch.zeros(lib.ti_paged_attention_plan_bytes(max(B, plan_batch or B)),
+                       dtype=torch.uint8, device=dev)
+    pb = plan_batch or B
+    N.check(lib.ti_paged_attention_plan(bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), pb, NH,
+                                        KVH, D, mb, NB, plan.data_ptr(), plan.numel(), s))
+    got = torch.full_like(q, 3.0)
+    N.check(lib.ti_paged_attention_decode_planned(*_args(q, k, v, bt, ctx, mb, got),
+                                                  N.dtype_code(q.dtype), ws.data_ptr(), need,
+                                                  plan.data_ptr(), s))
+    torch.cuda.synchronize()
+    return ref, got, plan
+
+
+CASES = [(4, 256, 14, 2, 64, 256 * 128, 128, 2048), (1, 12, 14, 2, 64, 3200, 1, 4096),
+         (5, 40, 16, 4, 64, 2000, 1, 700), (6, 3, 14, 2, 64, 64, 1, 300)]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_planned_equals_plain(cuda_device, case):
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    q, k, v, bt, ctx, mb = _case(*case, dev=cuda_device)
+    ref, got, _ = _plain_and_planned(lib, N, q, k, v, bt, ctx, mb)
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+
+
+def test_planned_edge_cases(cuda_device):
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    q, k, v, bt, ctx, mb = _case(2, 6, 14, 2, 64, 600, 200, 1500, dev=cuda_device)
+    ctx[0] = 0
+    bt[1, 3] = -1
+    bt[2, 20] = -1
+    bt[3, 0] = -1
+    bt[4, 5] = 600 + 7
+    ref, got, _ = _plain_and_planned(lib, N, q, k, v, bt, ctx, mb)
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    assert (got[0].float() == 3.0).all() and torch.isnan(got[3].float()).all()
+
+
+def test_plan_of_another_batch_is_rejected(cuda_device):
+    import ctypes
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    bits = ctypes.c_uint(0)
+    N.check(lib.ti_device_status(ctypes.byref(bits), 1, s))
+    q, k, v, bt, ctx, mb = _case(7, 64, 14, 2, 64, 6000, 1, 1500, dev=cuda_device)
+    _plain_and_planned(lib, N, q, k, v, bt, ctx, mb, plan_batch=50)
+    N.check(lib.ti_device_status(ctypes.byref(bits), 1, s))
+    assert bits.value & N.TI_DEVERR_ATTN_PLAN
+    # the context is still usable: a matching plan works afterwards
+    ref, got, _ = _plain_and_planned(lib, N, q, k, v, bt, ctx, mb)
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    N.check(lib.ti_device_status(ctypes.byref(bits), 1, s))
+    assert bits.value == 0
+
+
+def test_unplanned_shape_gets_zero_header(cuda_device):
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    q, k, v, bt, ctx, mb = _case(3, 5, 8, 2, 128, 300, 1, 900, dev=cuda_device)
+    ref, got, plan = _plain_and_planned(lib, N, q, k, v, bt, ctx, mb)
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    assert (plan[:32] == 0).all()

@@ -55,3 +55,10 @@ def test_library_calls_without_gpu(native):
     rc = lib.ti_paged_attention_decode(None, 0, None, 0, None, None, 1, None, 0, None, None, 1,
                                        14, 2, 64, 16, 4, 0, 0, None, 0, None)
     assert rc == 1 and b"null" in lib.ti_last_error()
+    # attention plan: size query and argument checks
+    assert lib.ti_paged_attention_plan_bytes(256) > lib.ti_paged_attention_plan_bytes(8) > 0
+    rc = lib.ti_paged_attention_plan(None, 0, None, None, 4, 14, 2, 64, 8, 100, None, 0, None)
+    assert rc == 1 and b"null" in lib.ti_last_error()
+    rc = lib.ti_paged_attention_decode_planned(None, 0, None, 0, None, None, 1, None, 0, None,
+                                               None, 1, 14, 2, 64, 16, 4, 0, None, 0, None, None)
+    assert rc == 1 and b"null" in lib.ti_last_error()

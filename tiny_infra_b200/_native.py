@@ -45,9 +45,15 @@ SIGNATURES: dict[str, tuple] = {
     "ti_gemm_qkv_rope": (I32, [P, I64, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P,
                                P, I32, I32, P]),
     "ti_sample": (I32, [P, I64, I32, I32, I32, P, P, P, P, P, P, P, I32, P]),
+    "ti_paged_attention_plan_bytes": (SZ, [I32]),
+    "ti_paged_attention_plan": (I32, [P, I64, P, P, I32, I32, I32, I32, I32, I64, P, SZ, P]),
+    "ti_paged_attention_decode_planned": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, I32, I32,
+                                                I32, I32, I32, I32, I32, P, SZ, P, P]),
 }
 
 TI_EPI_STORE, TI_EPI_SWIGLU, TI_EPI_RESIDUAL, TI_EPI_ARGMAX = 0, 1, 2, 3
+# device status bits (ti_device_status)
+TI_DEVERR_ATTN_WAIT, TI_DEVERR_GEMM_WAIT, TI_DEVERR_PREFILL_WAIT, TI_DEVERR_ATTN_PLAN = 1, 2, 4, 8
 
 _lib = None
 _lock = threading.Lock()
@@ -95,7 +101,8 @@ def launch_count() -> int:
 
 
 def device_status(clear: bool = True, device: torch.device | None = None) -> int:
-    """TI_DEVERR_* bits raised by bounded waits inside kernels since the last clear."""
+    """TI_DEVERR_* bits raised by kernels (bounded waits that gave up, rejected plans) since
+    the last clear."""
     bits = ctypes.c_uint(0)
     s = torch.cuda.current_stream(device).cuda_stream
     check(lib().ti_device_status(ctypes.byref(bits), int(clear), s))

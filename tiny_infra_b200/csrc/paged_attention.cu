@@ -75,7 +75,22 @@ struct Params {
   int32_t* ws_stop;         // [B, KVH, max_parts]
   int32_t* ws_count;        // [B, KVH]
   int32_t* ws_pieces;       // [B, KVH] v4: pieces of each unit (written by its first piece)
+  const int32_t* plan;      // v5: the batch's stream resolved once (ti_paged_attention_plan)
 };
+
+// SM count of the current device (the persistent kernels' grid), cached per device.
+static int sm_count() {
+  static int cached_dev = -1, sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+      sms = 148;
+    cached_dev = dev;
+  }
+  return sms;
+}
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads)
@@ -1165,7 +1180,6 @@ decode_kernel_v4(const __grid_constant__ CUtensorMap kmap,
   const uint32_t bar = bar_all + warp * kV4Stages * 8;
   const uint64_t pol = l2_policy_evict_first();
   const int G = p.group;
-  const int NHU = HP * G;
   const int g = lane >> 2, t4 = lane & 3;
 
   // issue cursor: the next stream position with a readable block (after a negative entry the
@@ -1384,12 +1398,54 @@ struct CfgV5 {
   static constexpr int kBars = 2 * kV5Pairs * kV5Stages * 8;    // full, then empty
   static constexpr int kIds = kV4IdCap * 4;
   static constexpr int kVtok = kV4IdCap;
-  static constexpr int kOffBytes = (kV2MaxBatch + 1) * 4;
+  static constexpr int kOffBytes = ((kV2MaxBatch + 1) * 4 + 15) / 16 * 16;
   static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
   static_assert(kTotal <= 227 * 1024, "v5 shared memory");
+  static_assert((kRing + kBars) % 16 == 0 && kIds % 16 == 0 && kVtok % 16 == 0, "int4 copies");
 };
 
-template <typename T>
+// Plan layout (int32 words; base 16-byte aligned), written by plan_kernel for the v5 chunking:
+//   [0] total positions  [1] chunk  [2] consumers (CTAs x kV5Pairs)  [3] batch
+//   [4] ids word offset  [5] vtok byte offset  [6] kV5Pairs  [7] kV4IdCap
+//   [8 ..) s_off[0 .. batch] (padded to 4 words), then per CTA a kV4IdCap slot of ids (int32)
+//   and, after all id slots, per CTA a kV4IdCap slot of vtok (bytes).
+__host__ __device__ inline int64_t plan_ids_word(int batch) { return 8 + (batch + 1 + 3) / 4 * 4; }
+__host__ __device__ inline int64_t plan_vtok_byte(int batch, int ctas) {
+  return (plan_ids_word(batch) + (int64_t)ctas * kV4IdCap) * 4;
+}
+inline size_t plan_bytes(int batch, int ctas) {
+  return (size_t)((plan_vtok_byte(batch, ctas) + (int64_t)ctas * kV4IdCap + 15) / 16 * 16);
+}
+
+// One CTA per v5 CTA: the v5 prologue (resolve_stream), its ids / vtok kept in the plan's slot.
+template <int NT>
+__global__ void __launch_bounds__(NT)
+plan_kernel(Params p, int batch, int32_t* plan) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int s_off[kV2MaxBatch + 1];
+  __shared__ int s_wsum[NT / 32];
+  int32_t* ids = plan + plan_ids_word(batch) + (int64_t)blockIdx.x * kV4IdCap;
+  uint8_t* vtok = reinterpret_cast<uint8_t*>(plan) + plan_vtok_byte(batch, gridDim.x) +
+                  (int64_t)blockIdx.x * kV4IdCap;
+  int chunk = 0, cb = 0, ce = 0;
+  resolve_stream<2, NT>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb, ce);
+  if (blockIdx.x == 0) {
+    for (int r = threadIdx.x; r <= batch; r += NT) plan[8 + r] = s_off[r];
+    if (threadIdx.x == 0) {
+      plan[0] = s_off[batch];
+      plan[1] = chunk;
+      plan[2] = gridDim.x * kV5Pairs;
+      plan[3] = batch;
+      plan[4] = (int)plan_ids_word(batch);
+      plan[5] = (int)plan_vtok_byte(batch, gridDim.x);
+      plan[6] = kV5Pairs;
+      plan[7] = kV4IdCap;
+    }
+  }
+}
+
+template <typename T, bool PLANNED>
 __global__ void __launch_bounds__(kV5Threads, 1)
 decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
                  const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
@@ -1419,8 +1475,40 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     fence_mbar_init();
   }
   int chunk, cb, ce;
-  if (!resolve_stream<2, kV5Threads>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb, ce))
-    return;
+  if constexpr (PLANNED) {
+    // one round of loads: header, s_off, this CTA's id and vtok slots
+    __shared__ int s_hdr[2];
+    const int32_t* pl = p.plan;
+    const int n_off = (batch + 1 + 3) / 4;
+    const int4* g_off = reinterpret_cast<const int4*>(pl + 8);
+    const int4* g_ids = reinterpret_cast<const int4*>(pl + plan_ids_word(batch) +
+                                                      (int64_t)blockIdx.x * kV4IdCap);
+    const int4* g_vt = reinterpret_cast<const int4*>(
+        reinterpret_cast<const uint8_t*>(pl) + plan_vtok_byte(batch, gridDim.x) +
+        (int64_t)blockIdx.x * kV4IdCap);
+    constexpr int n_ids = kV4IdCap / 4, n_vt = kV4IdCap / 16;
+    for (int i = tid; i < n_off + n_ids + n_vt; i += kV5Threads) {
+      if (i < n_off) reinterpret_cast<int4*>(s_off)[i] = g_off[i];
+      else if (i < n_off + n_ids) reinterpret_cast<int4*>(ids)[i - n_off] = g_ids[i - n_off];
+      else reinterpret_cast<int4*>(vtok)[i - n_off - n_ids] = g_vt[i - n_off - n_ids];
+    }
+    if (tid == 0) {
+      const bool ok = pl[3] == batch && pl[2] == (int)gridDim.x * kV5Pairs &&
+                      pl[1] > 0 && (int64_t)pl[1] * kV5Pairs <= kV4IdCap;
+      if (!ok) raise_device_error(TI_DEVERR_ATTN_PLAN);   // a plan of another batch / grid
+      s_hdr[0] = ok ? pl[0] : 0;
+      s_hdr[1] = ok ? pl[1] : 1;
+    }
+    __syncthreads();
+    chunk = s_hdr[1];
+    cb = blockIdx.x * kV5Pairs * chunk;
+    if (cb >= s_hdr[0]) return;
+    ce = min(s_hdr[0], cb + kV5Pairs * chunk);
+  } else {
+    if (!resolve_stream<2, kV5Threads>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb,
+                                       ce))
+      return;
+  }
   // end of the unit that contains stream position pp
   auto unit_end = [&](int pp) {
     int lo = 0, hi = batch;
@@ -1498,6 +1586,10 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     const int pend = min(end, pstart + nb);
     const int piece = pos / chunk - pstart / chunk;
     const int pieces = (pstart + nb - 1) / chunk - pstart / chunk + 1;
+    if (pieces > p.max_parts) {                // only a mismatched plan gets here
+      raise_device_error(TI_DEVERR_ATTN_PLAN);
+      return;
+    }
     const int head0 = (unit * 2 + sub) * G;   // first query head of this warp's kv head
     {
       const T* qh = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride +
@@ -1566,24 +1658,22 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   }
 }
 
-template <typename T>
+template <typename T, bool PLANNED>
 static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
                      cudaStream_t stream) {
   using C = CfgV5;
   static int set_dev = -1;
-  static int sms = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (set_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v5<T>,
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_v5<T, PLANNED>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v5)");
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
     set_dev = dev;
   }
-  int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T>, dim3(sms),
-                         dim3(kV5Threads), C::kTotal, stream, 1, km, vm, p, batch);
+  int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
+                         dim3(sm_count()), dim3(kV5Threads), C::kTotal, stream, 1, km, vm, p,
+                         batch);
   if (rc) return rc;
   const int units = p.num_kv_heads / 2;
   return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
@@ -1672,12 +1762,24 @@ extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, i
   return bytes + 256;
 }
 
-extern "C" int ti_paged_attention_decode(
+// Whether a decode call of this shape runs the v5 kernel (and can use a plan).
+static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks) {
+  if (!attn::use_v2(head_dim, batch) || num_kv_heads <= 0 || num_heads % num_kv_heads) return false;
+  if (num_kv_heads % 2 || num_heads / num_kv_heads > 8 || max_blocks <= 0) return false;
+  const int forced = attn::forced_kernel();
+  if (forced != 0 && forced != 5) return false;
+  const int64_t worst = (int64_t)batch * (num_kv_heads / 2) * max_blocks;
+  return (int64_t)attn::v2_chunk(worst, attn::sm_count() * attn::kV5Pairs, max_blocks) *
+             attn::kV5Pairs <= attn::kV4IdCap;
+}
+
+static int decode_impl(
     void* out, int64_t out_seq_stride, const void* q, int64_t q_seq_stride, const void* k_cache,
     const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int64_t bt_stride,
     const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
     int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
-    int partition_blocks, void* workspace, size_t workspace_bytes, void* stream) {
+    int partition_blocks, void* workspace, size_t workspace_bytes, void* stream,
+    const int32_t* plan) {
   clear_error();
   if (batch == 0) return TI_OK;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens)
@@ -1750,11 +1852,14 @@ extern "C" int ti_paged_attention_decode(
     }
     const int64_t worst = (int64_t)batch * (num_kv_heads / hp) * max_blocks_per_seq;
     const int forced = attn::forced_kernel();
-    if (hp == 2 && p.group <= 8 && (forced == 0 || forced == 5) &&
-        attn::v2_chunk(worst, sms * attn::kV5Pairs, max_blocks_per_seq) * attn::kV5Pairs <=
-            attn::kV4IdCap)
-      return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16>(p, km, vm, batch, s)
-                                    : attn::launch_v5<__half>(p, km, vm, batch, s);
+    if (v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
+      p.plan = plan;
+      if (plan)
+        return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, true>(p, km, vm, batch, s)
+                                      : attn::launch_v5<__half, true>(p, km, vm, batch, s);
+      return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, false>(p, km, vm, batch, s)
+                                    : attn::launch_v5<__half, false>(p, km, vm, batch, s);
+    }
     const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq);
     if (p.group <= 8 && forced != 2 && chunk_ub * attn::kV4Warps <= attn::kV4IdCap) {
       if (hp == 2)
@@ -1775,4 +1880,73 @@ extern "C" int ti_paged_attention_decode(
                           : attn::launch<__nv_bfloat16, 128>(p, km, vm, batch, s);
   return head_dim == 64 ? attn::launch<__half, 64>(p, km, vm, batch, s)
                         : attn::launch<__half, 128>(p, km, vm, batch, s);
+}
+
+extern "C" int ti_paged_attention_decode(
+    void* out, int64_t out_seq_stride, const void* q, int64_t q_seq_stride, const void* k_cache,
+    const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int64_t bt_stride,
+    const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
+    int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
+    int partition_blocks, void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_impl(out, out_seq_stride, q, q_seq_stride, k_cache, v_cache, num_blocks,
+                     block_tables, bt_stride, row_index, context_lens, batch, num_heads,
+                     num_kv_heads, head_dim, block_size, max_blocks_per_seq, dtype,
+                     partition_blocks, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" size_t ti_paged_attention_plan_bytes(int batch) {
+  return batch < 0 ? 0 : attn::plan_bytes(batch, attn::sm_count());
+}
+
+extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_stride,
+                                       const int32_t* row_index, const int32_t* context_lens,
+                                       int batch, int num_heads, int num_kv_heads, int head_dim,
+                                       int max_blocks_per_seq, int64_t num_blocks, void* plan,
+                                       size_t plan_bytes, void* stream) {
+  clear_error();
+  if (batch == 0) return TI_OK;
+  if (!block_tables || !context_lens || !plan)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: null pointer");
+  if (batch < 0 || num_blocks <= 0)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: negative batch or empty pool");
+  if (reinterpret_cast<uintptr_t>(plan) & 15)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: buffer must be 16-byte aligned");
+  if (!v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
+    // the planned decode takes the unplanned path for this shape; a zero header (chunk 0)
+    // also turns the projection's L2 warm-up off
+    if (plan_bytes < 32)
+      return set_error(TI_ERR_WORKSPACE, "attention plan: buffer too small");
+    cudaError_t e = cudaMemsetAsync(plan, 0, 32, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TI_OK : set_cuda_error(e, "attention plan header");
+  }
+  if (plan_bytes < ti_paged_attention_plan_bytes(batch))
+    return set_error(TI_ERR_WORKSPACE, "attention plan: buffer too small");
+  attn::Params p{};
+  p.block_tables = block_tables; p.bt_stride = bt_stride; p.row_index = row_index;
+  p.context_lens = context_lens;
+  p.num_heads = num_heads; p.num_kv_heads = num_kv_heads; p.group = num_heads / num_kv_heads;
+  p.max_blocks = max_blocks_per_seq; p.num_blocks = num_blocks;
+  return launch_kernel("attention plan launch", attn::plan_kernel<512>, dim3(attn::sm_count()),
+                       dim3(512), 0, reinterpret_cast<cudaStream_t>(stream), 1, p, batch,
+                       reinterpret_cast<int32_t*>(plan));
+}
+
+extern "C" int ti_paged_attention_decode_planned(
+    void* out, int64_t out_seq_stride, const void* q, int64_t q_seq_stride, const void* k_cache,
+    const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int64_t bt_stride,
+    const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
+    int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
+    void* workspace, size_t workspace_bytes, const void* plan, void* stream) {
+  if (!plan) {
+    clear_error();
+    return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: null plan");
+  }
+  if (reinterpret_cast<uintptr_t>(plan) & 15) {
+    clear_error();
+    return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: plan must be 16-byte aligned");
+  }
+  return decode_impl(out, out_seq_stride, q, q_seq_stride, k_cache, v_cache, num_blocks,
+                     block_tables, bt_stride, row_index, context_lens, batch, num_heads,
+                     num_kv_heads, head_dim, block_size, max_blocks_per_seq, dtype, 0, workspace,
+                     workspace_bytes, stream, reinterpret_cast<const int32_t*>(plan));
 }

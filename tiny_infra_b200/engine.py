@@ -47,6 +47,8 @@ class DecodeEngine:
             R, c.num_attention_heads, c.num_key_value_heads, c.head_dim,
             kv_cache.max_blocks_per_seq, 0)
         self.ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        self.plan = torch.zeros(N.lib().ti_paged_attention_plan_bytes(R), dtype=torch.uint8,
+                                device=dev)
         self.graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
         self.launches_per_step: dict[tuple, int] = {}
         # sampled steps (allocated on first use): logits [R, V] and the per-row sampling
@@ -84,7 +86,7 @@ class DecodeEngine:
             self.ctx_lens.data_ptr(), self.hidden.data_ptr(), m.weights["embed"].data_ptr(),
             c.hidden_size, c.vocab_size, rows, dt, s))
         m._layers(self._batch(rows), kv, self.cos, self.sin, self.hidden[:rows], s,
-                  bufs=self.bufs, ws=self.ws)
+                  bufs=self.bufs, ws=self.ws, plan=self.plan)
         N.check(lib.ti_rmsnorm(self.xf.data_ptr(), self.hidden.data_ptr(), N.TI_DTYPE_FP32,
                                m.weights["norm"].data_ptr(), c.rms_norm_eps, rows,
                                c.hidden_size, dt, s))

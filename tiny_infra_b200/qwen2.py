@@ -66,6 +66,7 @@ class Qwen2ForCausalLM:
             raise RuntimeError("unsupported model dimensions")
         self.weights: dict[str, torch.Tensor] = {}
         self._ws = N.Workspace()
+        self._plan_ws = N.Workspace()
         self._bufs: dict[str, torch.Tensor] = {}
         self.tied = False
 
@@ -223,7 +224,8 @@ class Qwen2ForCausalLM:
 
     def _layers(self, pb: PackedBatch, kv_cache, cos: torch.Tensor, sin: torch.Tensor,
                 hidden: torch.Tensor, stream: int, num_layers: int | None = None,
-                bufs: dict | None = None, ws: torch.Tensor | None = None) -> None:
+                bufs: dict | None = None, ws: torch.Tensor | None = None,
+                plan: torch.Tensor | None = None) -> None:
         c, W, lib = self.config, self.weights, N.lib()
         dt = N.dtype_code(self.dtype)
         T, H, D = pb.num_tokens, c.hidden_size, c.head_dim
@@ -237,6 +239,14 @@ class Qwen2ForCausalLM:
         if pb.decode and ws is None:
             need = lib.ti_paged_attention_workspace_bytes(pb.num_seqs, NH, KVH, D, maxb, 0)
             ws = self._ws.get(self.device, need)
+        if pb.decode:
+            # the batch's attention work split, resolved once for all layers
+            if plan is None:
+                plan = self._plan_ws.get(self.device,
+                                         lib.ti_paged_attention_plan_bytes(pb.num_seqs))
+            N.check(lib.ti_paged_attention_plan(
+                bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
+                pb.num_seqs, NH, KVH, D, maxb, nb, plan.data_ptr(), plan.numel(), stream))
         split_o = self._splits(NH * D)
         split_d = self._splits(I)
         for li in range(c.num_layers if num_layers is None else num_layers):
@@ -249,11 +259,11 @@ class Qwen2ForCausalLM:
                 pb.slot_mapping.data_ptr(), cos.data_ptr(), sin.data_ptr(),
                 pb.positions.data_ptr(), kv_cache.block_size, dt, stream))
             if pb.decode:
-                N.check(lib.ti_paged_attention_decode(
+                N.check(lib.ti_paged_attention_decode_planned(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
                     bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
-                    pb.num_seqs, NH, KVH, D, kv_cache.block_size, maxb, dt, 0, ws.data_ptr(),
-                    ws.numel(), stream))
+                    pb.num_seqs, NH, KVH, D, kv_cache.block_size, maxb, dt, ws.data_ptr(),
+                    ws.numel(), plan.data_ptr(), stream))
             else:
                 N.check(lib.ti_paged_prefill_attention(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
