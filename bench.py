@@ -33,6 +33,7 @@ METRIC = "decode tokens/sec @256 ragged seqs per B200 (1/2/4/8); paged-attn HBM 
 SEQS = 256
 CTX_LO, CTX_HI = 128, 2048
 CPU_SAMPLE_SEQS = 32
+WINDOW = 16          # decode steps between context-length resets (stationary workload)
 
 
 def _args():
@@ -68,6 +69,8 @@ def _config(world, extra=None):
                      "random-init bf16 weights (std 0.02, tied), KV pre-filled N(0,1)",
          "seqs_per_gpu": SEQS, "ctx_range": [CTX_LO, CTX_HI], "block_size": 16,
          "parallelism": f"replicas x{world} (no collectives)",
+         "context_window": f"lengths reset to the sampled ctx every {WINDOW} steps: each step "
+                           f"decodes at ctx + 0..{WINDOW - 1}",
          "l2": "inputs larger than L2 (~4.4 GB read per step), no flush"}
     if extra:
         c.update(extra)
@@ -194,16 +197,21 @@ def attention_roofline(engine, kv, cfg, ctx, reps, peak_gbs):
     q = torch.randn(n, NH * D, device=kv.device, dtype=torch.bfloat16)
     out = torch.empty_like(q)
     slots = torch.arange(n, dtype=torch.int32, device=kv.device)
-    lens = kv.seq_len[:n].clone()
+    lens = torch.from_numpy(np.asarray(ctx, np.int32) + WINDOW // 2).to(kv.device)
     s = torch.cuda.current_stream().cuda_stream
+    # as in the decode step: the batch's plan once, then the planned attention per layer
+    N.check(lib.ti_paged_attention_plan(
+        kv.block_tables.data_ptr(), kv.block_tables.stride(0), slots.data_ptr(), lens.data_ptr(),
+        n, NH, KVH, D, kv.max_blocks_per_seq, kv.total_physical_blocks, engine.plan.data_ptr(),
+        engine.plan.numel(), s))
 
     def launch():
-        N.check(lib.ti_paged_attention_decode(
+        N.check(lib.ti_paged_attention_decode_planned(
             out.data_ptr(), NH * D, q.data_ptr(), NH * D, kv.key_cache[0].data_ptr(),
             kv.value_cache[0].data_ptr(), kv.total_physical_blocks, kv.block_tables.data_ptr(),
             kv.block_tables.stride(0), slots.data_ptr(), lens.data_ptr(), n, NH, KVH, D,
-            kv.block_size, kv.max_blocks_per_seq, N.TI_DTYPE_BF16, 0, engine.ws.data_ptr(),
-            engine.ws.numel(), s))
+            kv.block_size, kv.max_blocks_per_seq, N.TI_DTYPE_BF16, engine.ws.data_ptr(),
+            engine.ws.numel(), engine.plan.data_ptr(), s))
 
     for _ in range(5):
         launch()
@@ -218,7 +226,7 @@ def attention_roofline(engine, kv, cfg, ctx, reps, peak_gbs):
     tot = int(lens.sum().item())
     algo = tot * KVH * D * 2 * 2 + 2 * n * NH * D * 2      # K+V of every context token, q, out
     achieved = algo / t / 1e9
-    return {"bound": "hbm", "kernel": "attn::decode_kernel_v4 + merge_pieces_kernel (paged decode attention)",
+    return {"bound": "hbm", "kernel": "attn::decode_kernel_v5 (planned) + merge_pieces_kernel (paged decode attention)",
             "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": _traffic_from_profiles(),
             "algorithmic_bytes_per_launch": algo, "us_per_launch": round(t * 1e6, 2)}
@@ -355,17 +363,28 @@ def run_ours(a, rank, world, local):
     peak, peak_kind = _peaks()
 
     # ---- device-resident decode (value) ----
-    plan = engine.plan_steps(slots, steps_total)
+    # Stationary contexts: every WINDOW steps each sequence's length goes back to its sampled
+    # value, so every timed step decodes at ctx0 + 0..WINDOW-1 (the configured distribution)
+    # instead of drifting by the number of steps.  The block allocations of one window are
+    # planned once (re-applying them is idempotent).
+    ctx0_dev = kv.seq_len[:SEQS].clone()
+    plan = engine.plan_steps(slots, WINDOW)
     rows = plan.shape[1]
     engine.d_in[1, :SEQS].copy_(torch.arange(SEQS, dtype=torch.int32))
     engine.d_in[0, :SEQS].copy_(first)
     sampler = ClockSampler(local)
     sampler.start()
-    # warm-up (also captures the graph)
-    for k in range(a.warmup):
-        engine.d_in[2, :rows].copy_(plan[k])
+
+    def resident_step(k):
+        if k % WINDOW == 0:
+            kv.seq_len[:SEQS].copy_(ctx0_dev)
+        engine.d_in[2, :rows].copy_(plan[k % WINDOW])
         engine._replay(rows)
         engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
+
+    # warm-up (also captures the graph)
+    for k in range(a.warmup):
+        resident_step(k)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -373,10 +392,8 @@ def run_ours(a, rank, world, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = N.launch_count()
     e0.record()
-    for k in range(a.warmup, steps_total):
-        engine.d_in[2, :rows].copy_(plan[k])
-        engine._replay(rows)
-        engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
+    for k in range(a.steps):
+        resident_step(k)
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -387,16 +404,26 @@ def run_ours(a, rank, world, local):
     value = world * SEQS * a.steps / secs
 
     # ---- e2e through the public per-step API (host tokens in/out) ----
+    # same stationary contexts: host and device lengths go back to ctx0 every WINDOW steps (the
+    # allocator then hands out fresh blocks for the window's block boundary; the pool has room)
+    ctx0_host = np.asarray(ctx, np.int32)
+
+    def e2e_step(k, toks):
+        if k % WINDOW == 0:
+            kv.alloc.seq_len[:SEQS] = ctx0_host
+            kv.seq_len[:SEQS].copy_(ctx0_dev)
+        return engine.step(slots, toks)
+
     toks = engine.next_tok[:SEQS].cpu().numpy()
-    for _ in range(2):
-        toks = engine.step(slots, toks)
+    for k in range(2):
+        toks = e2e_step(k, toks)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e2 = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
     e2[0].record()
-    for _ in range(a.steps):
-        toks = engine.step(slots, toks)
+    for k in range(a.steps):
+        toks = e2e_step(k, toks)
     e2[1].record()
     torch.cuda.synchronize()
     esecs = replicas.max_over_ranks(e2[0].elapsed_time(e2[1]) / 1e3, device)
@@ -422,7 +449,7 @@ def run_ours(a, rank, world, local):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    kv_bytes = int(ctx.sum() + SEQS * (a.warmup + a.steps / 2)) * cfg.num_layers * 2 * 2 * 64 * 2
+    kv_bytes = int(ctx.sum() + SEQS * (WINDOW + 1) / 2) * cfg.num_layers * 2 * 2 * 64 * 2
     step_bytes = model.weight_bytes() + kv_bytes
     ms = secs / a.steps * 1e3
     line = {
