@@ -146,6 +146,7 @@ class DecodeEngine:
             raise ValueError(f"decode batch {n} exceeds the engine's {self.max_rows} rows")
         rows = self.bucket(n) if self.use_graphs else n
         rows = min(rows, self.max_rows)
+        slots = np.asarray(slots, np.int32)        # one conversion of a host list per step
         new_block = self.kv.plan_decode(slots)
         h = self.h_in.numpy()
         h[0, :n] = tokens
@@ -168,6 +169,7 @@ class DecodeEngine:
         n = len(slots)
         if n == 0:
             return np.zeros(0, np.int32)
+        slots = np.asarray(slots, np.int32)
         rows = self.stage(slots, tokens)
         sampled = params is not None and not params.all_greedy
         if sampled:
@@ -180,8 +182,8 @@ class DecodeEngine:
             self.d_params[:, :rows].copy_(self.h_params[:, :rows], non_blocking=True)
         self._replay(rows, sampled)
         self.h_out[:n].copy_(self.next_tok[:n], non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        self.kv.advance(slots, 1)
+        self.kv.advance(slots, 1)      # host mirror, while the step runs (the device advances
+        torch.cuda.current_stream().synchronize()   # its own copy in the step's last kernel)
         return self.h_out[:n].numpy().copy()
 
     # ---- device-resident decoding (no host round trip between steps) -----------------------
