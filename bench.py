@@ -49,7 +49,8 @@ def _args():
                          "a Poisson request stream through the continuous batcher")
     ap.add_argument("--requests", type=int, default=1024, help="serving: number of requests")
     ap.add_argument("--rate", type=float, default=64.0, help="serving: arrivals per second")
-    ap.add_argument("--kernel", choices=["attention", "gate_up"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "gate_up", "rmsnorm", "sampler",
+                                         "prefill_gemm", "prefill_attention"], default=None,
                     help="time one kernel alone instead of the decode step")
     ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
@@ -474,6 +475,25 @@ def run_ours(a, rank, world, local):
     return 0
 
 
+def _kernel_line_flops(a, metric_value, t, flops, workload, data, extra_cfg=None):
+    """JSON line of a tensor-bound kernel mode: TFLOP/s of its algorithmic FLOPs against the
+    measured bf16 GEMM peak (burst: the kernel is timed alone)."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    peak, kind = (float(json.load(open(p))["bf16_tflops"]), "measured") if os.path.exists(p) \
+        else (1590.0, "fallback")
+    tfs = flops / t / 1e12
+    cfg = {"workload": workload, "l2": "weights cycled over buffers larger than L2, no flush"}
+    cfg.update(extra_cfg or {})
+    print(json.dumps({
+        "metric": metric_value, "value": round(tfs, 1), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": data, "config": cfg,
+        "roofline": {"bound": "tensor", "achieved": round(tfs, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tfs / peak, 4), "peak_kind": kind,
+                     "algorithmic_flops_per_launch": int(flops)}}), flush=True)
+
+
 def _kernel_line(a, metric_value, t, algo, workload, data, extra_cfg=None):
     peak, kind = _peaks()
     gbs = algo / t / 1e9
@@ -575,6 +595,141 @@ def run_gate_up_kernel(a):
     return 0
 
 
+def run_rmsnorm_kernel(a):
+    """RMSNorm of the fused-elementwise workload: 4096 tokens x hidden 896, float32 residual
+    stream in, bf16 out, eps 1e-6, cycling over 12 inputs (176 MB > L2); GB/s of its
+    algorithmic bytes (x read once, out written once, the weight)."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    dev = torch.device("cuda:0")
+    T, H, L = 4096, 896, 12
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    xs = [torch.randn(T, H, device=dev, generator=g) for _ in range(L)]
+    w = torch.randn(H, device=dev, generator=g).to(torch.bfloat16)
+    outs = [torch.empty(T, H, device=dev, dtype=torch.bfloat16) for _ in range(L)]
+    lib = N.lib()
+
+    def launch(i):
+        N.check(lib.ti_rmsnorm(outs[i].data_ptr(), xs[i].data_ptr(), N.TI_DTYPE_FP32, w.data_ptr(),
+                               1e-6, T, H, N.TI_DTYPE_BF16, torch.cuda.current_stream().cuda_stream))
+    t = _time_launches(launch, L, a.steps, a.warmup)
+    _kernel_line(a, "rmsnorm HBM GB/s", t, T * H * 4 + T * H * 2 + H * 2,
+                 f"RMSNorm, {T} tokens x {H}, fp32 in / bf16 out, {L} inputs cycled",
+                 "synthetic (N(0,1) residual stream and weight)")
+    return 0
+
+
+def run_sampler_kernel(a):
+    """Device sampler on one decode step's logits: 256 rows x 151936 (bf16), temperature 0.7,
+    top-k 50, top-p 0.9 (the serving configuration's sampling), two logits buffers cycled
+    (156 MB > L2); GB/s of one read of the logits."""
+    import torch
+    from tiny_infra_b200 import sampler as S
+    dev = torch.device("cuda:0")
+    R, V, L = 256, 151936, 2
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    logits = [(torch.randn(R, V, device=dev, generator=g) * 3.0).to(torch.bfloat16)
+              for _ in range(L)]
+    rng = np.random.default_rng(a.seed)
+    sp = S.SamplingParams([0.7] * R, [50] * R, [0.9] * R, rng.random(R).tolist(), V)
+    pd = torch.from_numpy(sp.packed()).to(dev)
+    out = torch.empty(R, dtype=torch.int32, device=dev)
+    t = _time_launches(lambda i: S.launch_sample(logits[i], pd, out), L, a.steps, a.warmup)
+    _kernel_line(a, "sampler HBM GB/s", t, R * V * 2 + R * 16 + R * 4,
+                 f"temperature / top-k / top-p sampling, {R} rows x {V} bf16 logits, "
+                 f"T 0.7, k 50, p 0.9, {L} logits buffers cycled",
+                 "synthetic (N(0,3) logits, seeded uniforms)")
+    return 0
+
+
+def run_prefill_gemm_kernel(a):
+    """gate/up + SwiGLU at prefill size: 4096 tokens x 896 -> 2 x 4864 (71.4 GFLOP, the packed
+    token count of the fused-elementwise workload), 24 layers' weights cycled; TFLOP/s on the
+    tcgen05 tensor pipe against the measured bf16 GEMM peak."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    from tiny_infra_b200.qwen2 import GATE_UP_TILE
+    dev = torch.device("cuda:0")
+    M, H, I, L = 4096, 896, 4864, 24
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    x = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    ws = [(torch.randn(2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+          for _ in range(L)]
+    act = torch.empty(M, I, device=dev, dtype=torch.bfloat16)
+    lib = N.lib()
+
+    def launch(i):
+        N.check(lib.ti_gemm(N.TI_EPI_SWIGLU, x.data_ptr(), H, ws[i].data_ptr(), H, M, 2 * I, H,
+                            act.data_ptr(), I, None, None, None, N.TI_DTYPE_BF16, GATE_UP_TILE, 1,
+                            torch.cuda.current_stream().cuda_stream))
+    t = _time_launches(launch, L, a.steps, a.warmup)
+    _kernel_line_flops(a, "prefill gate_up GEMM TFLOP/s", t, 2.0 * M * 2 * I * H,
+                       f"gate/up projection + SwiGLU, M={M}, N={2 * I}, K={H}, block_n "
+                       f"{GATE_UP_TILE}, {L} layers' weights cycled",
+                       "synthetic (N(0,1) activations, N(0,0.02) weights)")
+    return 0
+
+
+def run_prefill_attention_kernel(a):
+    """Ragged causal prefill attention over the paged pool, the fused-elementwise packing: 4096
+    new tokens in 16 sequences of seeded lengths, each chunk at a seeded start position so that
+    its tokens lie in [0, 32768), attending to every earlier position of its sequence; 14/2
+    heads, D 64, bf16, one layer (its KV > L2).  TFLOP/s of the causal QK^T and PV products."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(a.seed)
+    S_, T, NH, KVH, D, bs = 16, 4096, 14, 2, 64, 16
+    cut = np.sort(rng.choice(np.arange(1, T), S_ - 1, replace=False))
+    lens = np.diff(np.concatenate([[0], cut, [T]])).astype(np.int32)
+    start = np.array([rng.integers(0, 32768 - n + 1) for n in lens], np.int32)
+    nblk = (start + lens + bs - 1) // bs
+    NB = int(nblk.sum()) + 16
+    mb = int(nblk.max())
+    perm = rng.permutation(NB)
+    bt = np.full((S_, mb), -1, np.int32)
+    off = 0
+    for i in range(S_):
+        bt[i, :nblk[i]] = perm[off:off + nblk[i]]
+        off += int(nblk[i])
+    cu = np.zeros(S_ + 1, np.int32)
+    cu[1:] = np.cumsum(lens)
+    ts, tq = [], []
+    for i in range(S_):
+        for q0 in range(0, int(lens[i]), 16):
+            ts.append(i)
+            tq.append(q0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    q = torch.randn(T, NH, D, device=dev, generator=g).to(torch.bfloat16)
+    kc = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+    vc = torch.randn(NB, KVH, bs, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    as_dev = lambda x: torch.from_numpy(np.ascontiguousarray(x, np.int32)).to(dev)  # noqa: E731
+    d_bt, d_start, d_cu = as_dev(bt), as_dev(start), as_dev(cu)
+    d_ts, d_tq, d_rows = as_dev(ts), as_dev(tq), as_dev(np.arange(S_))
+    lib = N.lib()
+
+    def launch(_):
+        N.check(lib.ti_paged_prefill_attention(
+            out.data_ptr(), NH * D, q.data_ptr(), NH * D, kc.data_ptr(), vc.data_ptr(), NB,
+            d_bt.data_ptr(), d_bt.stride(0), d_rows.data_ptr(), d_start.data_ptr(), d_cu.data_ptr(),
+            d_ts.data_ptr(), d_tq.data_ptr(), len(ts), NH, KVH, D, bs, N.TI_DTYPE_BF16,
+            torch.cuda.current_stream().cuda_stream))
+    t = _time_launches(launch, 1, a.steps, a.warmup)
+    keys = sum(int(s0) * int(n) + int(n) * (int(n) + 1) // 2 for s0, n in zip(start, lens))
+    flops = 4.0 * keys * D * NH                     # QK^T and PV, 2 FLOP per MAC
+    _kernel_line_flops(a, "prefill attention TFLOP/s", t, flops,
+                       f"ragged causal prefill attention, {T} tokens in {S_} sequences, starts "
+                       f"in [0, 32768), 14/2 heads, D=64, paged pool of {NB} blocks",
+                       "synthetic (N(0,1) q/k/v, random block permutation)",
+                       {"kv_bytes_unique": int(nblk.sum()) * KVH * bs * D * 2 * 2})
+    return 0
+
+
 def run_serving(a):
     """A stream of generation requests through ContinuousBatcher (one GPU): Poisson arrivals
     (--rate per second, seeded), prompt ids U[0, 151936), prompt lengths U[32, 1024], output
@@ -663,6 +818,14 @@ def main():
         return run_serving(a) if rank == 0 else 0
     if a.kernel == "attention":
         return run_attention_kernel(a) if rank == 0 else 0
+    if a.kernel == "rmsnorm":
+        return run_rmsnorm_kernel(a) if rank == 0 else 0
+    if a.kernel == "sampler":
+        return run_sampler_kernel(a) if rank == 0 else 0
+    if a.kernel == "prefill_gemm":
+        return run_prefill_gemm_kernel(a) if rank == 0 else 0
+    if a.kernel == "prefill_attention":
+        return run_prefill_attention_kernel(a) if rank == 0 else 0
     if a.kernel == "gate_up":
         return run_gate_up_kernel(a) if rank == 0 else 0
     if a.impl == "reference":

@@ -114,6 +114,28 @@ def test_edge_cases(cuda_device):
     assert toks[2:] == [int(np.argmax(logits[2])), int(np.argmax(logits[3]))]
 
 
+def test_topk_fast_path_and_overflow(cuda_device):
+    """Rows with a top-k cut of at most 512 take the compacted-candidate route; a row whose
+    top-k keeps more than 4096 tied elements falls back to the radix selects.  Both must give
+    the reference's answer: with 6000 equal maxima and k = 10 every tie is kept (x >= the 10th
+    largest), each with weight exp(0), so u = 0.5 draws the 3001st tied index; k = 512 and
+    k = 1 on a random row follow the oracle's kept set and CDF."""
+    rng = np.random.default_rng(8)
+    V = 8192
+    logits = bf16_round(rng.standard_normal((3, V)).astype(np.float32))
+    ties = np.sort(rng.choice(V, 6000, replace=False))
+    logits[0, :] = -3.0
+    logits[0, ties] = 1.0
+    dev = torch.from_numpy(logits).to(cuda_device, torch.bfloat16)
+    temps, ks, ps, us = [1.0, 0.9, 1.2], [10, 512, 1], [1.0, 0.95, 1.0], [0.5, 0.37, 0.8]
+    # the batch rule keeps top-k only in rows whose k is the batch's largest: run rows alone
+    toks = [_run(dev[i:i + 1], [temps[i]], [ks[i]], [ps[i]], [us[i]])[0] for i in range(3)]
+    assert toks[0] == int(ties[3000])
+    for i in (1, 2):
+        cand = OS.filter_logits(logits[i:i + 1], [temps[i]], [ks[i]], [1.0])[0]
+        _check_row(cand, ps[i], toks[i], us[i])
+
+
 def test_seq_len_advance(cuda_device):
     from tiny_infra_b200 import sampler as S
     V = 1000

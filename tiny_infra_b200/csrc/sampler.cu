@@ -19,6 +19,14 @@
 //     ordered by ascending index (a final pass scans the tied elements in index order).
 // The draw uses a caller-provided uniform u in [0, 1): the token is the first one, in
 // descending order, whose cumulative kept weight exceeds u * (total kept weight).
+//
+// Rows with a top-k cut of at most 512 (the common case) take a faster route to the same
+// answers: the k-th largest of the 512 threads' maxima bounds the row's k-th largest value from
+// below (those k maxima are k elements at least that large), so one more pass compacts every
+// element at or above it into shared memory; the candidates are sorted (value descending, index
+// ascending) and the cutoff, the top-p boundary and the draw are read off their prefix sums of
+// the same fixed-point weights.  When more than kCand elements reach the bound (ties), the row
+// falls back to the radix selects, whose histograms are per warp.
 #include <algorithm>
 #include <type_traits>
 
@@ -31,6 +39,7 @@ namespace smp {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 256;
+constexpr int kCand = 4096;        // compacted top-k candidates (power of two)
 
 __device__ __forceinline__ uint32_t f2key(float x) {   // order-preserving: larger x, larger key
   const uint32_t b = __float_as_uint(x);
@@ -41,7 +50,13 @@ __device__ __forceinline__ float key2f(uint32_t k) {
 }
 
 struct Shared {
-  unsigned long long hist[kBins];
+  union {
+    unsigned long long hist[kWarps][kBins];   // radix selects: one histogram per warp
+    unsigned long long cand[kCand];           // fast path: (key << 32) | ~index, then weights
+  };
+  unsigned long long bin_sum[kBins];
+  float tmax[kThreads];
+  int cand_n;
   unsigned long long scan[kWarps];
   float red_v[kWarps];
   int red_i[kWarps];
@@ -65,6 +80,46 @@ struct Row {
   }
 };
 
+// f(x, j) for every element j of the row, in no particular order: 16-byte loads, U of them in
+// flight per thread (the scalar strided loop was load-latency bound); rows whose start is not
+// 16-byte aligned, and the tail, go element by element.
+template <typename T, typename F>
+__device__ __forceinline__ void row_scan(const Row<T>& row, int V, F&& f) {
+  constexpr int kVec = 16 / (int)sizeof(T);
+  constexpr int U = 8;
+  const int nvec = (reinterpret_cast<uintptr_t>(row.p) & 15) == 0 ? V / kVec : 0;
+  const uint4* pv = reinterpret_cast<const uint4*>(row.p);
+  int v = threadIdx.x;
+  for (; v + (U - 1) * kThreads < nvec; v += U * kThreads) {
+    uint4 buf[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) buf[u] = __ldg(pv + v + u * kThreads);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const T* e = reinterpret_cast<const T*>(&buf[u]);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        float x;
+        if constexpr (std::is_same<T, float>::value) x = e[i];
+        else x = Elem<T>::to_f(e[i]);
+        f(x * row.inv_t, (v + u * kThreads) * kVec + i);
+      }
+    }
+  }
+  for (; v < nvec; v += kThreads) {
+    const uint4 b = __ldg(pv + v);
+    const T* e = reinterpret_cast<const T*>(&b);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      float x;
+      if constexpr (std::is_same<T, float>::value) x = e[i];
+      else x = Elem<T>::to_f(e[i]);
+      f(x * row.inv_t, v * kVec + i);
+    }
+  }
+  for (int j = nvec * kVec + (int)threadIdx.x; j < V; j += kThreads) f(row.x(j), j);
+}
+
 // Weight of element with value x in 32.32 fixed point (exp(x - m), x <= m), 0 when not a
 // candidate.
 __device__ __forceinline__ unsigned long long weight(float x, float m) {
@@ -85,20 +140,26 @@ __device__ void select_first_exceeding(Shared& sh, const Row<T>& row, int V, uin
   bool found = true;
 #pragma unroll 1
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < kBins; b += kThreads) sh.hist[b] = 0ull;
+    for (int b = tid; b < kWarps * kBins; b += kThreads) (&sh.hist[0][0])[b] = 0ull;
     __syncthreads();
-    for (int j = tid; j < V; j += kThreads) {
-      const float x = row.x(j);
+    row_scan(row, V, [&](float x, int) {
       const uint32_t k = f2key(x);
-      if (k < lowkey || (k & pmask) != prefix) continue;
-      atomicAdd(&sh.hist[(k >> shift) & 255u], COUNT ? 1ull : weight(x, m));
+      if (k < lowkey || (k & pmask) != prefix) return;
+      atomicAdd(&sh.hist[warp][(k >> shift) & 255u], COUNT ? 1ull : weight(x, m));
+    });
+    __syncthreads();
+    for (int b = tid; b < kBins; b += kThreads) {
+      unsigned long long t = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += sh.hist[w][b];
+      sh.bin_sum[b] = t;
     }
     __syncthreads();
     if (warp == 0) {
       // lane l owns bins 255 - 8l ... 248 - 8l (descending); suffix sums in that order
       unsigned long long own[8], s = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) { own[i] = sh.hist[255 - 8 * lane - i]; s += own[i]; }
+      for (int i = 0; i < 8; ++i) { own[i] = sh.bin_sum[255 - 8 * lane - i]; s += own[i]; }
       unsigned long long before = s;                 // inclusive scan over lanes
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -179,8 +240,114 @@ __device__ void select_first_exceeding(Shared& sh, const Row<T>& row, int V, uin
   __syncthreads();
 }
 
+
+// Bitonic sort of sh.cand[0 .. n2) in descending order (n2 a power of two, at most kCand); all
+// threads of the CTA take part.
+__device__ void sort_desc(Shared& sh, int n2) {
+  for (int size = 2; size <= n2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n2 / 2; i += kThreads) {
+        const int a = 2 * i - (i & (stride - 1)), b = a + stride;
+        const bool desc = (a & size) == 0;
+        const unsigned long long x = sh.cand[a], y = sh.cand[b];
+        if ((x < y) == desc) { sh.cand[a] = y; sh.cand[b] = x; }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Top-k fast path (1 <= k <= kThreads): returns false (uniformly) when more than kCand elements
+// reach the bound, leaving the row to the radix selects; otherwise sets `token` exactly as they
+// would.  sh.tmax holds each thread's maximum of the scaled row.
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
+__device__ bool topk_fast(Shared& sh, const Row<T>& row, int V, int k, float m, float p, float u,
+                          int& token) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the k-th largest thread maximum: a lower bound of the row's k-th largest value
+  sh.cand[tid] = ((unsigned long long)f2key(sh.tmax[tid]) << 32) | (uint32_t)tid;
+  if (tid == 0) sh.cand_n = 0;
+  __syncthreads();
+  sort_desc(sh, kThreads);
+  const uint32_t bound = (uint32_t)(sh.cand[k - 1] >> 32);
+  __syncthreads();
+  // compact the elements at or above the bound: (key << 32) | ~index
+  row_scan(row, V, [&](float x, int j) {   // few elements pass: one shared atomic each
+    const uint32_t key = f2key(x);
+    if (key < bound) return;
+    const int slot = atomicAdd(&sh.cand_n, 1);
+    if (slot < kCand) sh.cand[slot] = ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)j;
+  });
+  __syncthreads();
+  const int n = sh.cand_n;
+  if (n > kCand) return false;
+  int n2 = 1;
+  while (n2 < n) n2 <<= 1;
+  for (int i = n + tid; i < n2; i += kThreads) sh.cand[i] = 0ull;   // sorts last
+  __syncthreads();
+  sort_desc(sh, n2);
+  // kept: the leading entries with key >= the k-th largest key (k <= n)
+  const uint32_t cut = (uint32_t)(sh.cand[k - 1] >> 32);
+  constexpr int E = kCand / kThreads;
+  unsigned long long w[E], mine = 0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = tid * E + e;
+    w[e] = 0ull;
+    if (i < n) {
+      const uint32_t key = (uint32_t)(sh.cand[i] >> 32);
+      if (key >= cut) w[e] = weight(key2f(key), m);
+    }
+    mine += w[e];
+  }
+  unsigned long long incl = mine;   // block-wide scan in thread (= descending) order
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sh.scan[warp] = incl;
+  __syncthreads();
+  unsigned long long wbase = 0, Z = 0;
+  for (int q = 0; q < kWarps; ++q) {
+    if (q < warp) wbase += sh.scan[q];
+    Z += sh.scan[q];
+  }
+  const unsigned long long excl = wbase + incl - mine;
+  // first kept entry whose cumulative weight exceeds `target` -> its cumulative weight / index
+  auto find = [&](unsigned long long target, bool want_index) {
+    if (tid == 0) sh.sel_found = 0;
+    __syncthreads();
+    if (excl <= target && excl + mine > target) {
+      unsigned long long run = excl;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        run += w[e];
+        if (run > target) {
+          sh.sel_found = 1;
+          sh.sel_cum = run;
+          sh.sel_index = want_index ? (int)~(uint32_t)(sh.cand[tid * E + e] & 0xffffffffull) : -1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  };
+  unsigned long long zk = Z;
+  if (p < 1.f) {
+    const double tgt = (double)p * (double)Z;
+    if (tgt < (double)Z) {
+      find(tgt <= 0.0 ? 0ull : (unsigned long long)tgt, false);
+      if (sh.sel_found) zk = sh.sel_cum;
+    }
+  }
+  find((unsigned long long)((double)u * (double)zk), true);
+  if (sh.sel_found && sh.sel_index >= 0) token = sh.sel_index;
+  return true;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 2)
 sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temps,
               const int32_t* __restrict__ cut_ks, const float* __restrict__ top_ps,
               const float* __restrict__ uniforms, int32_t* __restrict__ out,
@@ -197,10 +364,10 @@ sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __re
   // ---- max and first argmax
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int j = tid; j < V; j += kThreads) {
-    const float x = row.x(j);
+  row_scan(row, V, [&](float x, int j) {
     if (x > best || (x == best && j < bi)) { best = x; bi = j; }
-  }
+  });
+  sh.tmax[tid] = best;   // this thread's maximum (top-k fast path)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float v = __shfl_xor_sync(0xffffffffu, best, o);
@@ -220,20 +387,22 @@ sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __re
   const float m = sh.red_v[0];
   int token = sh.red_i[0] == 0x7fffffff ? 0 : sh.red_i[0];   // an all-NaN row yields 0
 
-  if (temp != 0.f && m > -INFINITY) {
+  const int k = temp != 0.f && m > -INFINITY ? cut_ks[r] : 0;
+  const float u = fminf(fmaxf(uniforms[r], 0.f), 0.99999994f);
+  bool fast = false;
+  if (k > 0 && k <= kThreads && k < V) fast = topk_fast<T>(sh, row, V, k, m, top_ps[r], u, token);
+  if (temp != 0.f && m > -INFINITY && !fast) {
     // ---- top-k cutoff: keep x >= the k-th largest value (k = 0: keep everything)
     uint32_t lowkey = 0;
-    const int k = cut_ks[r];
     if (k > 0 && k < V) {
       select_first_exceeding<T, true, true>(sh, row, V, 0u, m, (unsigned long long)(k - 1));
       if (sh.sel_found) lowkey = sh.sel_key;       // keep x >= the k-th largest value
     }
     // ---- total weight of the candidates
     unsigned long long z = 0;
-    for (int j = tid; j < V; j += kThreads) {
-      const float x = row.x(j);
+    row_scan(row, V, [&](float x, int) {
       if (f2key(x) >= lowkey) z += weight(x, m);
-    }
+    });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
     if (lane == 0) sh.scan[warp] = z;
@@ -254,7 +423,6 @@ sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __re
       }
     }
     // ---- the draw: first element whose cumulative weight exceeds u * zk
-    const float u = fminf(fmaxf(uniforms[r], 0.f), 0.99999994f);
     const unsigned long long t2 = (unsigned long long)((double)u * (double)zk);
     select_first_exceeding<T, false, false>(sh, row, V, lowkey, m, t2);
     if (sh.sel_found && sh.sel_index >= 0) token = sh.sel_index;
