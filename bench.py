@@ -726,7 +726,9 @@ def run_prefill_attention_kernel(a):
                        f"ragged causal prefill attention, {T} tokens in {S_} sequences, starts "
                        f"in [0, 32768), 14/2 heads, D=64, paged pool of {NB} blocks",
                        "synthetic (N(0,1) q/k/v, random block permutation)",
-                       {"kv_bytes_unique": int(nblk.sum()) * KVH * bs * D * 2 * 2})
+                       {"kv_bytes_unique": int(nblk.sum()) * KVH * bs * D * 2 * 2,
+                        "l2": "one layer's pool; its unique KV fits L2 after the first touch "
+                              "(compute-bound kernel), no flush"})
     return 0
 
 

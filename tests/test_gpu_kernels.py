@@ -233,11 +233,13 @@ def test_swiglu(cuda_device, dtype):
         custom_swiglu.forward(xt[:, :12].contiguous())   # I = 6 is not a multiple of 8
 
 
-def test_rmsnorm(cuda_device):
-    """RMSNorm over hidden 896 (eps 1e-6) on the float32 residual stream, bf16 output."""
+@pytest.mark.parametrize("T", [4096, 4095, 37])
+def test_rmsnorm(cuda_device, T):
+    """RMSNorm over hidden 896 (eps 1e-6) on the float32 residual stream, bf16 output: large
+    batches run two rows per warp (4095: the last pass has one row), small ones one."""
     from tiny_infra_b200 import _native as N
     rng = np.random.default_rng(8)
-    T, H = 4096, 896
+    H = 896
     x = (rng.standard_normal((T, H)) * 3).astype(np.float32)
     w = bf16_round(rng.standard_normal(H).astype(np.float32))
     xt = torch.from_numpy(x).to(cuda_device)
