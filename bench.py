@@ -697,11 +697,14 @@ def run_prefill_attention_kernel(a):
         off += int(nblk[i])
     cu = np.zeros(S_ + 1, np.int32)
     cu[1:] = np.cumsum(lens)
-    ts, tq = [], []
+    ts, tq, work = [], [], []
     for i in range(S_):
         for q0 in range(0, int(lens[i]), 16):
             ts.append(i)
             tq.append(q0)
+            work.append(int(start[i]) + min(q0 + 16, int(lens[i])))
+    order = np.argsort(-np.asarray(work, np.int64), kind="stable")   # as the model orders them
+    ts, tq = [ts[o] for o in order], [tq[o] for o in order]
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed)
     q = torch.randn(T, NH, D, device=dev, generator=g).to(torch.bfloat16)

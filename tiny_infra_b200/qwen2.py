@@ -183,13 +183,18 @@ class Qwen2ForCausalLM:
         decode = bool((counts == 1).all())
         tseq, tq0 = None, None
         if not decode:
-            ts, tq = [], []
+            # query tiles of 16 tokens, longest causal prefix first: a tile's work grows with
+            # its last position, and the GPU starts CTAs in grid order, so the long ones should
+            # not be left for the tail of the launch
+            ts, tq, work = [], [], []
             for i in range(nseq):
                 for q0 in range(0, int(counts[i]), 16):
                     ts.append(i)
                     tq.append(q0)
-            tseq = torch.tensor(ts, dtype=torch.int32, device=dev)
-            tq0 = torch.tensor(tq, dtype=torch.int32, device=dev)
+                    work.append(int(start[i]) + min(q0 + 16, int(counts[i])))
+            order = np.argsort(-np.asarray(work, np.int64), kind="stable")
+            tseq = torch.tensor(np.asarray(ts, np.int32)[order], dtype=torch.int32, device=dev)
+            tq0 = torch.tensor(np.asarray(tq, np.int32)[order], dtype=torch.int32, device=dev)
         as_dev = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)  # noqa: E731
         return PackedBatch(
             input_ids=as_dev(np.asarray(token_ids, np.int32), torch.int32),
