@@ -44,7 +44,7 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["decode", "serving"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "serving", "long"], default="decode",
                     help="decode: the 256-sequence decode step (the headline metric); serving: "
                          "a Poisson request stream through the continuous batcher")
     ap.add_argument("--requests", type=int, default=1024, help="serving: number of requests")
@@ -816,11 +816,132 @@ def run_serving(a):
     return 0
 
 
+def run_long(a, rank, world, local):
+    """Long-context decode across replicas: 2048 requests (--requests) partitioned round robin
+    over the N ranks, contexts U[8192, 32768] (KV pre-filled N(0,1)), 128 greedy output tokens
+    each, 256 slots per replica; each replica decodes its share in batches of up to 256
+    requests.  value = all ranks' generated tokens / the max over ranks of the device time of
+    the decode steps (weak scaling: the request count is fixed, so per-GPU work shrinks as N
+    grows -- "scaling": "strong")."""
+    import torch
+    import torch.distributed as dist
+    from tiny_infra_b200 import _native as N
+    from tiny_infra_b200 import replicas
+    from tiny_infra_b200.cache_manager import KVCacheManager
+    from tiny_infra_b200.config import QwenConfig
+    from tiny_infra_b200.engine import DecodeEngine
+    from tiny_infra_b200.qwen2 import Qwen2ForCausalLM
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=device)
+    LO, HI, OUT, SLOTS = 8192, 32768, 128, 256
+    total_req = a.requests if a.requests != 1024 else 2048
+    rng = np.random.default_rng(a.seed)
+    ctx_all = rng.integers(LO, HI + 1, total_req).astype(np.int32)
+    mine = replicas.partition(total_req, world, rank)
+    ctx_mine = ctx_all[mine]
+    cfg = QwenConfig()
+    sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=a.seed, tied=True, device=device)
+    model = Qwen2ForCausalLM(cfg, device=device).load_reference_state_dict(sd)
+    max_seq = HI + OUT + 16
+    blocks = SLOTS * ((max_seq + 15) // 16)          # every slot at the longest context
+    kv = KVCacheManager(SLOTS, max_seq, cfg.num_layers, cfg.num_key_value_heads, cfg.head_dim,
+                        device=device, num_blocks=blocks)
+    g = torch.Generator(device=device)
+    g.manual_seed(a.seed + 1 + rank)
+    for li in range(cfg.num_layers):
+        kv.key_cache[li].normal_(generator=g)
+        kv.value_cache[li].normal_(generator=g)
+    engine = DecodeEngine(model, kv)
+
+    def load_batch(ctx):
+        n = len(ctx)
+        slots = list(range(n))
+        for sl in range(SLOTS):
+            if kv.seq_len_host(sl) or kv.alloc.block_tables[sl, 0] >= 0:
+                kv.free_batch_slot(sl)
+        kv.plan_tokens(slots, [int(c) for c in ctx])
+        kv.advance_device(slots, [int(c) for c in ctx])
+        plan = engine.plan_steps(slots, OUT)
+        first = torch.from_numpy(rng.integers(0, cfg.vocab_size, n).astype(np.int32)).to(device)
+        return slots, plan, first
+
+    def run_batch(slots, plan, first, steps):
+        n = len(slots)
+        rows = plan.shape[1]
+        engine.d_in[1, :n].copy_(torch.arange(n, dtype=torch.int32))
+        engine.d_in[1, n:rows] = -1
+        engine.d_in[0, :n].copy_(first)
+        for k in range(steps):
+            engine.d_in[2, :rows].copy_(plan[k])
+            engine._replay(rows)
+            engine.d_in[0, :n].copy_(engine.next_tok[:n])
+
+    # warm-up (graph capture) on the first batch, then every batch timed from its start
+    sl, pl, fi = load_batch(ctx_mine[:SLOTS])
+    run_batch(sl, pl, fi, max(1, a.warmup))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    secs, tokens, kv_tok = 0.0, 0, 0
+    for b0 in range(0, len(ctx_mine), SLOTS):
+        ctx = ctx_mine[b0:b0 + SLOTS]
+        sl, pl, fi = load_batch(ctx)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run_batch(sl, pl, fi, OUT)
+        e1.record()
+        torch.cuda.synchronize()
+        secs += e0.elapsed_time(e1) / 1e3
+        tokens += len(ctx) * OUT
+        kv_tok += int(ctx.sum()) * OUT + len(ctx) * OUT * (OUT + 1) // 2
+    clocks = sampler.stop()
+    status = N.device_status()
+    tsecs = replicas.max_over_ranks(secs, device)
+    all_tokens = total_req * OUT
+    steps = -(-len(ctx_mine) // SLOTS) * OUT
+    if world > 1:
+        dist.barrier()
+    engine.graphs.clear()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = _peaks()
+    step_bytes = model.weight_bytes() + kv_tok / steps * cfg.num_layers * 2 * 2 * 64 * 2
+    print(json.dumps({
+        "metric": "long-context decode tokens/s (2048 requests, ctx U[8192,32768], 128 tokens)",
+        "value": round(all_tokens / tsecs, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": max(1, a.warmup), "ms_per_step": round(tsecs / steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, random token ids, N(0,1) KV)",
+        "config": {"workload": f"{total_req} requests round robin over {world} replica(s), ctx "
+                               f"U[{LO},{HI}], {OUT} greedy tokens, {SLOTS} slots per replica, "
+                               "KV pre-filled (no prefill)",
+                   "parallelism": f"replicas x{world} (no collectives)",
+                   "l2": "inputs far larger than L2 (~65 GB of KV per step), no flush"},
+        "step_roofline": {"bytes_per_step": int(step_bytes),
+                          "achieved_gbs": round(step_bytes / (tsecs / steps) / 1e9, 1),
+                          "peak_gbs": peak, "peak_kind": peak_kind,
+                          "frac": round(step_bytes / (tsecs / steps) / 1e9 / peak, 4)},
+        "clocks": clocks, "device_status": status}), flush=True)
+    return 0
+
+
 def main():
     a = _args()
     rank, world, local = _dist()
     if a.workload == "serving":
         return run_serving(a) if rank == 0 else 0
+    if a.workload == "long":
+        return run_long(a, rank, world, local)
     if a.kernel == "attention":
         return run_attention_kernel(a) if rank == 0 else 0
     if a.kernel == "rmsnorm":

@@ -75,22 +75,29 @@ class BlockAllocator:
         k = 0
         try:
             for b, n in zip(slots, counts):
+                b, n = int(b), int(n)
                 start = int(self.seq_len[b])
                 if strict_len and start > self.max_seq_len:                        # :60-61
                     raise ValueError("Sequence length exceeds maximum allowed length.")
-                for t in range(n):
-                    pos = start + t
-                    if pos >= self.max_seq_len:                                     # :79-80
-                        raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
-                    lb = pos // bs
-                    if self.block_tables[b, lb] == -1:
-                        if not self.free_blocks:                                    # :87-88
-                            raise RuntimeError("OOM : No free physical blocks available for allocation.")
-                        phys = self.free_blocks.popleft()
-                        self.block_tables[b, lb] = phys
-                        updates.append((b, lb, phys))
-                    out[k] = int(self.block_tables[b, lb]) * bs + pos % bs
-                    k += 1
+                # tokens before the first position >= max_seq_len (:79-80); a slot's blocks are
+                # taken in ascending logical order, as token-by-token allocation does
+                n_ok = max(0, min(n, self.max_seq_len - start))
+                if n_ok:
+                    lbs = np.arange(start // bs, (start + n_ok - 1) // bs + 1)
+                    need = lbs[self.block_tables[b, lbs] == -1]
+                    take = min(len(need), len(self.free_blocks))
+                    if take:
+                        fb = self.free_blocks
+                        phys = np.array([fb.popleft() for _ in range(take)], np.int32)
+                        self.block_tables[b, need[:take]] = phys
+                        updates.extend(zip([b] * take, need[:take].tolist(), phys.tolist()))
+                    if take < len(need):                                            # :87-88
+                        raise RuntimeError("OOM : No free physical blocks available for allocation.")
+                    pos = np.arange(start, start + n_ok, dtype=np.int64)
+                    out[k:k + n_ok] = self.block_tables[b, pos // bs].astype(np.int64) * bs + pos % bs
+                    k += n_ok
+                if n_ok < n:
+                    raise ValueError(f"Sequence length exceeds maximum allowed length for batch index {b}.")
         except (ValueError, RuntimeError) as e:
             e.updates = updates
             raise
