@@ -222,3 +222,32 @@ def test_engine_greedy_64_tokens(cuda_device):
     print(f"greedy decisions {decisions}, identical {decisions - len(near_tie_mismatch)}, "
           f"near-tie differences {near_tie_mismatch} (tau {tau:.3g})")
     assert decisions == 256
+
+
+def test_load_qwen_reference_checkpoint(cuda_device, tmp_path):
+    """tiny_infra_b200.loader.load_qwen on a checkpoint in the reference's extracted format
+    (engine/loader.py:34-72; 2 full-width layers, bf16, untied lm_head) gives exactly the
+    weights -- and the logits -- of load_reference_state_dict on the same tensors."""
+    from safetensors.torch import save_file
+
+    from tiny_infra_b200.config import QwenConfig
+    from tiny_infra_b200.loader import load_qwen, reference_key_map
+    from tiny_infra_b200.qwen2 import Qwen2ForCausalLM
+    cfg = QwenConfig(num_layers=2, vocab_size=4096)
+    sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=5, tied=False, device="cpu")
+    inv = {v: k for k, v in reference_key_map(2).items()}
+    save_file({inv[k]: v.contiguous() for k, v in sd.items()}, str(tmp_path / "w.safetensors"))
+    got = load_qwen(str(tmp_path / "w.safetensors"), device=cuda_device, config=cfg)
+    ref = Qwen2ForCausalLM(cfg, device=cuda_device).load_reference_state_dict(
+        {k: v.to(cuda_device) for k, v in sd.items()})
+    assert set(got.weights) == set(ref.weights) and got.tied == ref.tied is False
+    for k in ref.weights:
+        assert torch.equal(got.weights[k], ref.weights[k]), k
+    from tiny_infra_b200.cache_manager import KVCacheManager
+    ids = torch.randint(0, 4096, (1, 9), dtype=torch.int32, device=cuda_device)
+    outs = []
+    for m in (got, ref):
+        kv = KVCacheManager(1, 64, 2, cfg.num_key_value_heads, cfg.head_dim)
+        cos, sin = m.rope_tables(64)
+        outs.append(m(ids, torch.zeros(1, dtype=torch.int32, device=cuda_device), kv, cos, sin))
+    assert torch.equal(outs[0], outs[1])
