@@ -227,7 +227,9 @@ def test_engine_greedy_64_tokens(cuda_device):
 def test_load_qwen_reference_checkpoint(cuda_device, tmp_path):
     """tiny_infra_b200.loader.load_qwen on a checkpoint in the reference's extracted format
     (engine/loader.py:34-72; 2 full-width layers, bf16, untied lm_head) gives exactly the
-    weights -- and the logits -- of load_reference_state_dict on the same tensors."""
+    weights of load_reference_state_dict on the same tensors, and the same logits up to the
+    run-to-run order of the residual GEMMs' split-K additions (2e-2 of the logit scale, as the
+    other forward tests)."""
     from safetensors.torch import save_file
 
     from tiny_infra_b200.config import QwenConfig
@@ -250,4 +252,5 @@ def test_load_qwen_reference_checkpoint(cuda_device, tmp_path):
         kv = KVCacheManager(1, 64, 2, cfg.num_key_value_heads, cfg.head_dim)
         cos, sin = m.rope_tables(64)
         outs.append(m(ids, torch.zeros(1, dtype=torch.int32, device=cuda_device), kv, cos, sin))
-    assert torch.equal(outs[0], outs[1])
+    a, b = outs[0].float(), outs[1].float()
+    assert (a - b).abs().max().item() <= 2e-2 * b.abs().max().item()
