@@ -34,6 +34,7 @@ SEQS = 256
 CTX_LO, CTX_HI = 128, 2048
 CPU_SAMPLE_SEQS = 32
 WINDOW = 16          # decode steps between context-length resets (stationary workload)
+REF_MAX_SECONDS = 60.0   # reference arm: cap on the timed oracle steps' work
 
 
 def _args():
@@ -269,8 +270,10 @@ def oracle_sample(sd, kv, ctx, seed):
     return W, cfg, cache, cos, sin, tokens
 
 
-def oracle_decode_steps(state, steps, min_seconds=0.0):
-    """Run oracle decode steps (greedy, tokens fed back); returns (steps run, seconds)."""
+def oracle_decode_steps(state, steps, min_seconds=0.0, max_seconds=None, ctx0=None):
+    """Run oracle decode steps (greedy, tokens fed back); returns (steps run, seconds).  With
+    ``ctx0`` the lengths go back to it every WINDOW steps (the GPU arm's stationary contexts);
+    ``max_seconds`` stops early (at least one step)."""
     from oracle import model as OM
     W, cfg, cache, cos, sin, tokens = state
     n = len(tokens)
@@ -278,11 +281,15 @@ def oracle_decode_steps(state, steps, min_seconds=0.0):
     t0 = time.perf_counter()
     done = 0
     while done < steps or (time.perf_counter() - t0) < min_seconds:
+        if ctx0 is not None and done % WINDOW == 0:
+            cache.seq_len[idx] = ctx0
         logits = OM.forward(W, cfg, tokens[:, None], idx, cache, cos, sin)
         cache.seq_len[idx] += 1
         tokens = np.argmax(logits[:, -1], axis=-1)
         done += 1
         if min_seconds and done >= 2 and (time.perf_counter() - t0) >= min_seconds:
+            break
+        if max_seconds is not None and (time.perf_counter() - t0) >= max_seconds:
             break
     state[5][:] = tokens
     return done, time.perf_counter() - t0
@@ -327,11 +334,14 @@ def run_reference(a, rank, world):
     cache.seq_len[:] = ctx
     cos, sin = OK.rope_table(cache.max_seq_len, cfg.head_dim, cfg.rope_theta)
     state = [W, cfg, cache, cos, sin, rng.integers(0, cfg.vocab_size, n)]
-    oracle_decode_steps(state, a.warmup)
-    done, secs = oracle_decode_steps(state, a.steps)
+    # warm-up bounded to 2 steps, timed steps to REF_MAX_SECONDS of work (the run has to end
+    # within minutes: one oracle step of 32 sequences takes ~1 s); contexts reset every WINDOW
+    # steps as in the GPU arm
+    oracle_decode_steps(state, min(a.warmup, 2), ctx0=ctx)
+    done, secs = oracle_decode_steps(state, a.steps, max_seconds=REF_MAX_SECONDS, ctx0=ctx)
     value = n * done / secs
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(secs / done * 1e3, 2),
+            "steps": done, "warmup": min(a.warmup, 2), "ms_per_step": round(secs / done * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
             "config": _config(1, {"sample": f"{n} of the 256 sequences per step"}),
@@ -438,8 +448,8 @@ def run_ours(a, rank, world, local):
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         torch.set_num_threads(_cores())
         st = list(oracle_sample(sd, kv, ctx, a.seed))
-        oracle_decode_steps(st, 1)
-        done, csecs = oracle_decode_steps(st, 2, min_seconds=10.0)
+        oracle_decode_steps(st, 1, ctx0=ctx[:CPU_SAMPLE_SEQS])
+        done, csecs = oracle_decode_steps(st, 2, min_seconds=10.0, ctx0=ctx[:CPU_SAMPLE_SEQS])
         cpu = {"value": round(CPU_SAMPLE_SEQS * done / csecs, 2), "unit": "tokens/s",
                "cores": _cores(), "kind": "port",
                "sample": f"{CPU_SAMPLE_SEQS} of the 256 sequences, {done} greedy decode steps, "
