@@ -42,6 +42,7 @@
 
 #include "capi_internal.h"
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace ti {
 namespace gemm {
@@ -50,62 +51,6 @@ constexpr int BM = 128;
 constexpr int BK = 64;                 // one 128-byte swizzle atom of bf16 per row
 constexpr int kThreads = 192;
 
-// ---- tcgen05 wrappers --------------------------------------------------------------------
-__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// 32 lanes x 32 columns of 32-bit: thread t of the warp receives 32 consecutive columns of
-// TMEM lane (quadrant base + t).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor, K-major operand in the canonical SWIZZLE_128B layout:
-// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), LBO unused (1), version 1.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
 // Instruction descriptor for kind::f16: fp32 accumulator, A/B bf16 (1) or fp16 (0), both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 __host__ __device__ constexpr uint32_t instr_desc(int n, bool bf16) {
@@ -551,7 +496,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     if constexpr (CL > 1) {
       if (red_live) pre.load(e, red_row, n0, red_c);
     }
-    ok = mbar_wait(accum, 0, TI_DEVERR_GEMM_WAIT);
+    // tcgen05.ld is warp-collective: the warp goes on only when all its lanes saw the phase
+    ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, TI_DEVERR_GEMM_WAIT));
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     if constexpr (CL == 1) {
@@ -763,7 +709,7 @@ lmhead_argmax_kernel(const __grid_constant__ CUtensorMap amap,
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int b = local & 1, use = local >> 1;
-      if (!mbar_wait(accf0 + 8 * b, use & 1, TI_DEVERR_GEMM_WAIT)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(accf0 + 8 * b, use & 1, TI_DEVERR_GEMM_WAIT))) break;
       tc_fence_after();
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {

@@ -12,8 +12,13 @@
 // warp G is a TMA producer that streams the sequence's KV blocks (16 tokens x D per block and
 // kv head, SWIZZLE_128B) through a 4-stage ring; all G compute warps share every K/V tile, so
 // each KV byte is read once per CTA for the whole GQA group.
+#include <cstdlib>
+#include <type_traits>
+#include <cstring>
+
 #include "capi_internal.h"
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace ti {
 namespace prefill {
@@ -232,6 +237,295 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
                        dim3((p.group + 1) * 32), Smem<HD>::kTotal, s, 1, km, vm, p);
 }
 
+
+// ==========================================================================================
+// tcgen05 variant (head_dim 64, GQA groups <= 8): one CTA per (query tile of 16 tokens, kv
+// head); the 128 MMA rows are (query head slot h < 8) x (token t < 16), row = 16 h + t.
+//   S = Q K^T   M=128, N=64 keys, K=64 dims: Q (K-major) once in shared memory, a 64-key chunk of
+//               K (4 pool blocks, K-major) per step; fp32 S in one of two TMEM buffers;
+//   softmax     warps 2-5, one row per thread, straight from TMEM: causal mask, running max kept
+//               until a row's max grows by more than 2^8 (then O is rescaled in TMEM), P = 2^(s-m)
+//               split into bf16 hi + lo (~2^-17 relative, as the mma.sync kernels) and written
+//               to shared memory in the MMA's K-major layout;
+//   O += P V    M=128, N=64 dims, K=64 keys, twice (hi, lo), with V read in place as an MN-major
+//               operand (rows = keys); fp32 O in TMEM.
+// Warp 0 streams K/V chunks through a 3-stage TMA ring, warp 1 issues the MMAs (S of chunk j
+// before P.V of chunk j-1, so the softmax of j overlaps the P.V of j-1).  Every wait is bounded.
+// ==========================================================================================
+namespace tc {
+__device__ __forceinline__ void st_shared_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z,
+                                             uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+constexpr int kChunk = 64;                     // keys per step
+constexpr int kStages = 3;
+constexpr int kTile = kChunk * 128;            // 64 rows x 128 bytes: K or V of one chunk
+constexpr int kQ = 0, kPhi = 16384, kPlo = 32768, kKV = 49152;
+constexpr int kStageBytes = 2 * kTile;
+constexpr int kBarOff = kKV + kStages * kStageBytes;       // 98304
+constexpr int kSmem = kBarOff + 256 + 1024;                 // barriers + alignment slack
+constexpr int kTmemCols = 256;                 // S buffers at 0 and 64, O at 128
+constexpr int kThreads = 192;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                  Params p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bars = sb + kBarOff;
+  const uint32_t kv_full = bars, kv_empty = bars + 8 * kStages;
+  const uint32_t s_full = bars + 16 * kStages, s_free = s_full + 16;
+  const uint32_t p_ready = s_free + 16, pv_done = p_ready + 8;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kBarOff + 128);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, kvh = blockIdx.y;
+  const int G = p.group;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < kStages; ++i) {
+        mbar_init(kv_full + 8 * i, 1);
+        mbar_init(kv_empty + 8 * i, 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(s_full + 8 * i, 1);
+        mbar_init(s_free + 8 * i, 4);
+      }
+      mbar_init(p_ready, 4);
+      mbar_init(pv_done, 1);
+      fence_mbar_init();
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(tslot), kTmemCols);
+  }
+  pdl_wait();   // q, the pool's K/V and the tables come from earlier kernels
+
+  const int seq = p.tile_seq[tile];
+  const int q0 = p.tile_q0[tile];
+  const int row0 = p.cu_seqlens[seq] + q0;
+  const int nq = min(kTileQ, p.cu_seqlens[seq + 1] - row0);
+  const int start = p.start_pos[seq];
+  const int nkeys = start + q0 + nq;                  // keys 0 .. last query position
+  const int nchunks = (nkeys + kChunk - 1) / kChunk;
+  const int32_t* bt = p.block_tables + (int64_t)p.row_index[seq] * p.bt_stride;
+
+  // ---- Q tile: row 16 h + t = query head kvh*G + h of token row0 + t (zero when h >= G or
+  //      t >= nq), swizzled K-major
+  for (int i = tid; i < 128 * 8; i += kThreads) {
+    const int r = i >> 3, c = i & 7, h = r >> 4, t = r & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < G && t < nq)
+      v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) +
+                                          (int64_t)(row0 + t) * p.q_stride +
+                                          (int64_t)(kvh * G + h) * 64 + c * 8);
+    *reinterpret_cast<uint4*>(smem + kQ + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---- producer: chunk j = blocks 4j .. 4j+3 (past the keys: block 0, masked later)
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();   // later query tiles re-read these blocks
+      for (int j = 0; j < nchunks; ++j) {
+        const int st = j % kStages;
+        if (j >= kStages &&
+            !mbar_wait(kv_empty + 8 * st, ((j / kStages) - 1) & 1, TI_DEVERR_PREFILL_WAIT))
+          break;
+        const uint32_t dst = sb + kKV + st * kStageBytes;
+        mbar_arrive_expect_tx(kv_full + 8 * st, kStageBytes);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int blk = 4 * j + b;
+          int pb = blk * kBlock < nkeys ? bt[blk] : 0;
+          if (pb < 0 || (int64_t)pb >= p.num_blocks) pb = 0;   // never read outside the pool
+          const int y = (pb * p.num_kv_heads + kvh) * kBlock;
+          tma_load_2d_hint(dst + b * 2048, &kmap, kv_full + 8 * st, 0, y, pol);
+          tma_load_2d_hint(dst + kTile + b * 2048, &vmap, kv_full + 8 * st, 0, y, pol);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+      constexpr uint32_t id_s = idesc_f16(128, kChunk, bf, false, false);
+      constexpr uint32_t id_pv = idesc_f16(128, 64, bf, false, true);
+      bool ok = true;
+      for (int j = 0; j <= nchunks && ok; ++j) {
+        if (j < nchunks) {
+          const int st = j % kStages, b = j & 1;
+          ok = mbar_wait(kv_full + 8 * st, (j / kStages) & 1, TI_DEVERR_PREFILL_WAIT);
+          if (ok && j >= 2) ok = mbar_wait(s_free + 8 * b, ((j >> 1) - 1) & 1, TI_DEVERR_PREFILL_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t kt = sb + kKV + st * kStageBytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma(tmem + b * kChunk, smem_desc_sw128(sb + kQ + 32 * k, false),
+                   smem_desc_sw128(kt + 32 * k, false), id_s, k > 0 ? 1u : 0u);
+          tc_commit(s_full + 8 * b);
+        }
+        if (j >= 1) {
+          const int jp = j - 1, sp = jp % kStages;
+          ok = mbar_wait(p_ready, jp & 1, TI_DEVERR_PREFILL_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vt = sb + kKV + sp * kStageBytes + kTile;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma(tmem + 128, smem_desc_sw128(sb + kPhi + 32 * k, false),
+                   smem_desc_sw128(vt + 2048 * k, true), id_pv, (jp > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma(tmem + 128, smem_desc_sw128(sb + kPlo + 32 * k, false),
+                   smem_desc_sw128(vt + 2048 * k, true), id_pv, 1u);
+          tc_commit(pv_done);
+          tc_commit(kv_empty + 8 * sp);
+        }
+      }
+    }
+  } else {
+    // ---- softmax and epilogue: thread <-> row (TMEM lane) r
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int h = r >> 4, t = r & 15;
+    const int qp = start + q0 + t;                    // query position of the row
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    // the TMEM loads / stores after a wait are warp-collective: a warp goes on only when all
+    // its lanes saw the phase (a timeout in one lane stops the whole warp)
+    auto wait_all = [&](uint32_t bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, TI_DEVERR_PREFILL_WAIT));
+    };
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nchunks; ++j) {
+      const int b = j & 1;
+      if (!wait_all(s_full + 8 * b, (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      float sv[kChunk];
+      tmem_ld32(trow + b * kChunk, sv);
+      tmem_ld32(trow + b * kChunk + 32, sv + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free + 8 * b);
+      const int k0 = j * kChunk;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kChunk; ++c) {
+        sv[c] = (k0 + c <= qp) ? sv[c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[c]);
+      }
+      // chunk 0 holds key 0 <= every query position, so m is finite from the start
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m = mx;
+      } else if (mx > m + 8.f) {
+        alpha = fast_exp2(m - mx);
+        m = mx;
+        rescale = true;
+      }
+      l *= alpha;
+      uint32_t hi[kChunk / 2], lo[kChunk / 2];
+#pragma unroll
+      for (int c = 0; c < kChunk; c += 2) {
+        const float p0 = fast_exp2(sv[c] - m), p1 = fast_exp2(sv[c + 1] - m);
+        l += p0 + p1;
+        const uint32_t h2 = Elem<T>::pack2(p0, p1);
+        const float2 hf = Elem<T>::unpack2(h2);
+        hi[c / 2] = h2;
+        lo[c / 2] = Elem<T>::pack2(p0 - hf.x, p1 - hf.y);
+      }
+      if (j >= 1) {   // P.V of the previous chunk is done: P buffers free, O current
+        if (!wait_all(pv_done, (j - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp takes the branch
+        // when any of its rows rescales (alpha is 1 for the others)
+        if (__any_sync(0xffffffffu, rescale)) {
+          float ov[32];
+#pragma unroll
+          for (int c = 0; c < 64; c += 32) {
+            tmem_ld32(trow + 128 + c, ov);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(trow + 128 + c, ov);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {   // 16-byte chunk c = keys 8c .. 8c+7
+        const uint32_t off = (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+        st_shared_v4(sb + kPhi + off, hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+        st_shared_v4(sb + kPlo + off, lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    if (ok && wait_all(pv_done, (nchunks - 1) & 1)) {
+      tc_fence_after();
+      float ov[64];
+      tmem_ld32(trow + 128, ov);
+      tmem_ld32(trow + 160, ov + 32);
+      if (h < G && t < nq) {
+        const float inv = 1.f / l;
+        T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(row0 + t) * p.out_stride +
+                 (int64_t)(kvh * G + h) * 64;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          uint4 u;
+          u.x = Elem<T>::pack2(ov[c] * inv, ov[c + 1] * inv);
+          u.y = Elem<T>::pack2(ov[c + 2] * inv, ov[c + 3] * inv);
+          u.z = Elem<T>::pack2(ov[c + 4] * inv, ov[c + 5] * inv);
+          u.w = Elem<T>::pack2(ov[c + 6] * inv, ov[c + 7] * inv);
+          *reinterpret_cast<uint4*>(dst + c) = u;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T>
+static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int num_tiles,
+                  cudaStream_t s) {
+  static int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(prefill tc)");
+    set_dev = dev;
+  }
+  return launch_kernel("prefill attention launch", prefill_tc_kernel<T>,
+                       dim3(num_tiles, p.num_kv_heads), dim3(kThreads), kSmem, s, 1, km, vm, p);
+}
+}  // namespace tc
+
+// TI_PREFILL_ATTN_KERNEL=mma forces the mma.sync kernel (comparisons and tests).
+static bool use_tc(int head_dim, int group) {
+  const char* e = getenv("TI_PREFILL_ATTN_KERNEL");
+  if (e && !strcmp(e, "mma")) return false;
+  return head_dim == 64 && group <= 8;
+}
 }  // namespace prefill
 }  // namespace ti
 
@@ -284,6 +578,9 @@ extern "C" int ti_paged_prefill_attention(
                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (prefill::use_tc(head_dim, p.group))
+    return dtype == TI_DTYPE_BF16 ? prefill::tc::launch<__nv_bfloat16>(p, km, vm, num_tiles, s)
+                                  : prefill::tc::launch<__half>(p, km, vm, num_tiles, s);
   if (dtype == TI_DTYPE_BF16)
     return head_dim == 64 ? prefill::launch<__nv_bfloat16, 64>(p, km, vm, num_tiles, s)
                           : prefill::launch<__nv_bfloat16, 128>(p, km, vm, num_tiles, s);
