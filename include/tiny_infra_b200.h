@@ -186,6 +186,10 @@ int ti_embedding(float* out, const void* table, const int32_t* ids, int num_toke
  *   TI_EPI_SWIGLU    out[M, N/2] = silu(gate) * up (fused_swiglu.cu:39-50), where every group
  *                    of block_n weight rows holds block_n/2 gate rows followed by the matching
  *                    block_n/2 up rows
+ *   TI_EPI_SWIGLU16  out[M, N/2] = silu(gate) * up with every 16 weight rows holding 8 gate rows
+ *                    followed by the matching 8 up rows (N % 16 == 0); block_n and split_k are
+ *                    ignored: the library picks the tile width (up to 256 rows: 80 or 144, so
+ *                    that one wave of CTAs covers the GPU; above: 256)
  *   TI_EPI_RESIDUAL  out (float32 [M, N], ldo) += D
  *   TI_EPI_ARGMAX    aux_val/aux_idx [M, N/block_n] = (max, first argmax) of each row within each
  *                    block_n column tile; `out` (dtype logits) is also written when not NULL
@@ -202,6 +206,7 @@ int ti_embedding(float* out, const void* table, const int32_t* ids, int num_toke
 #define TI_EPI_SWIGLU 1
 #define TI_EPI_RESIDUAL 2
 #define TI_EPI_ARGMAX 3
+#define TI_EPI_SWIGLU16 5
 int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
             int K, void* out, int64_t ldo, const void* bias, float* aux_val, int32_t* aux_idx,
             int dtype, int block_n, int split_k, void* stream);

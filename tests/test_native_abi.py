@@ -62,3 +62,9 @@ def test_library_calls_without_gpu(native):
     rc = lib.ti_paged_attention_decode_planned(None, 0, None, 0, None, None, 1, None, 0, None,
                                                None, 1, 14, 2, 64, 16, 4, 0, None, 0, None, None)
     assert rc == 1 and b"null" in lib.ti_last_error()
+    # SwiGLU16 gate/up GEMM: N must be a multiple of 16 (checked before any CUDA call; the
+    # operand addresses are never dereferenced)
+    fake = 1 << 20
+    rc = lib.ti_gemm(native.TI_EPI_SWIGLU16, fake, 896, fake, 896, 256, 9720, 896, fake,
+                     4864, None, None, None, native.TI_DTYPE_BF16, 0, 1, None)
+    assert rc != 0 and b"N % 16" in lib.ti_last_error()

@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 TI_EPI_STORE, TI_EPI_SWIGLU, TI_EPI_RESIDUAL, TI_EPI_ARGMAX = 0, 1, 2, 3
+TI_EPI_SWIGLU16 = 5
 # device status bits (ti_device_status)
 TI_DEVERR_ATTN_WAIT, TI_DEVERR_GEMM_WAIT, TI_DEVERR_PREFILL_WAIT, TI_DEVERR_ATTN_PLAN = 1, 2, 4, 8
 

@@ -8,6 +8,9 @@
 //   TI_EPI_STORE     out = D (+ bias)                       q/k/v projection (bias), logits
 //   TI_EPI_SWIGLU    out = silu(gate) * up                   gate/up projection + SwiGLU
 //                    (fused_swiglu.cu:39-50; no [T, 2I] intermediate, no torch.cat)
+//   TI_EPI_SWIGLU16  the same with gate/up rows interleaved in groups of 8, so that any tile
+//                    width that is a multiple of 16 pairs them: decode batches take 80- or
+//                    144-wide tiles that fill the SMs in one wave
 //   TI_EPI_RESIDUAL  x_f32 += D                              o_proj / down_proj + residual add
 //                    (models/qwen_25.py:182,191), one red.add per element
 //   TI_EPI_ARGMAX    per-row (max, first argmax) of each N tile, logits optionally stored
@@ -115,8 +118,12 @@ struct Best {
 // 64 for 64-byte output rows) with the 16-byte chunk index XORed by row % 8 (PB = 128) or
 // (row / 2) % 4 (PB = 64), so that thread-per-row writes and chunk-per-thread reads are both
 // free of bank conflicts; store_tile then writes it out line by line.
+// Rows whose 16-byte chunk count is odd (80- and 144-byte rows of the 80- / 144-wide SwiGLU16
+// tiles) are staged row-major without a swizzle (PB = the row's bytes): 8 consecutive rows then
+// start on 8 different 16-byte bank groups, and chunk-per-thread reads are contiguous.
 template <int PB>
 __device__ __forceinline__ uint32_t stage_off(int r, int byte_col, int R) {
+  if constexpr (PB != 64 && PB != 128) return (uint32_t)(r * PB + byte_col);
   const int panel = byte_col / PB;
   const int chunk = (byte_col % PB) >> 4;
   const int sw = PB == 128 ? (r & 7) : ((r >> 1) & 3);
@@ -166,9 +173,9 @@ __device__ __forceinline__ void epilogue_bar() {   // the 4 epilogue warps
 template <typename T, int BN, int KIND>
 struct Out {
   using OT = typename std::conditional<KIND == TI_EPI_RESIDUAL, float, T>::type;
-  static constexpr int kCols = KIND == TI_EPI_SWIGLU ? BN / 2 : BN;
+  static constexpr int kCols = KIND == TI_EPI_SWIGLU || KIND == TI_EPI_SWIGLU16 ? BN / 2 : BN;
   static constexpr int kBytes = kCols * (int)sizeof(OT);   // per staged row
-  static constexpr int kPanelBytes = kBytes < 128 ? 64 : 128;
+  static constexpr int kPanelBytes = (kBytes / 16) % 2 ? kBytes : kBytes < 128 ? 64 : 128;
   static_assert(kBytes % kPanelBytes == 0, "whole panels");
 };
 
@@ -293,6 +300,27 @@ __device__ __forceinline__ void epilogue_chunk(const EpiArgs& e, int row, bool l
   }
 }
 
+// SwiGLU16 epilogue of one accumulator row (TMEM lane of this thread): every 32 accumulator
+// columns are two groups of (8 gate, 8 matching up) and give 16 outputs; a tile width of 16
+// mod 32 ends on one group (the 16 columns read past it are allocated TMEM that the MMA did not
+// write, and are dropped).
+template <typename T, int BN>
+__device__ __forceinline__ void swiglu16_rows(uint32_t trow, int lr, uint32_t stage) {
+  constexpr int PB = Out<T, BN, TI_EPI_SWIGLU16>::kPanelBytes;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float v[32], o[16];
+    tmem_ld32(trow + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i] = silu_mul(v[i], v[8 + i]);
+      o[8 + i] = silu_mul(v[16 + i], v[24 + i]);
+    }
+    if (c + 32 <= BN) stage_vals<T, 16, PB>(stage, BM, lr, c / 2, o);
+    else stage_vals<T, 8, PB>(stage, BM, lr, c / 2, o);
+  }
+}
+
 // Write the staged tile (R rows starting at global row y0) to global memory: the 128 epilogue
 // threads walk it in 16-byte chunks, consecutive threads on consecutive chunks of a row, so
 // each warp store covers whole lines; the residual adds with red.global.add (one add per
@@ -331,13 +359,15 @@ __device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int
     if (!e.out) return;
   }
   using OT = typename O::OT;
-  const int x0 = KIND == TI_EPI_SWIGLU ? n0 / 2 : n0;
+  const int x0 = KIND == TI_EPI_SWIGLU || KIND == TI_EPI_SWIGLU16 ? n0 / 2 : n0;
   uint8_t* base = reinterpret_cast<uint8_t*>(e.out) + (int64_t)x0 * (int64_t)sizeof(OT);
   const int64_t pitch = e.ldo * (int64_t)sizeof(OT);
+  // the last SwiGLU16 tile may reach past N: its chunks beyond N / 2 outputs are not stored
+  const int live_chunks = KIND == TI_EPI_SWIGLU16 ? min(CPR, (e.N / 2 - x0) / 8) : CPR;
   for (int idx = t; idx < R * CPR; idx += 128) {
     const int r = idx / CPR, ch = idx % CPR;
     const int row = y0 + r;
-    if (row >= e.M) continue;
+    if (row >= e.M || ch >= live_chunks) continue;
     const uint4 v = ld_shared_v4(stage + stage_off<PB>(r, ch * 16, R));
     uint8_t* dst = base + row * pitch + ch * 16;
     if constexpr (KIND == TI_EPI_RESIDUAL) {
@@ -356,7 +386,7 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int kRing = STAGES * kStage;
   // split-K across a cluster of CL CTAs: each CTA leaves its fp32 partial tile in shared memory
   // (over the drained stage ring, rows padded by 16 bytes against bank conflicts) and finishes
@@ -505,7 +535,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       const int row = m0 + lr;
       const bool live = row < e.M;
       Best best{-INFINITY, 0x7fffffff};
-      if (ok && nk > 0) {
+      if constexpr (KIND == TI_EPI_SWIGLU16) {
+        if (ok && nk > 0) swiglu16_rows<T, BN>(trow, lr, sbase);
+      } else if (ok && nk > 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float lo[32], hi[32];
@@ -833,7 +865,7 @@ static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, 
     const int nkb = K / BK;
     const int zs = CL > 1 ? CL : zsplits;
     const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
-    dim3 grid(N / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
     return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, K, per, e);
   }
 }
@@ -950,6 +982,45 @@ static int launch_qkv(const CUtensorMap& am, const CUtensorMap& bm, int M, int N
              : dispatch_cl<T, 64, 4, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
 }
 
+#ifndef TI_GEMM_STAGES_80
+#define TI_GEMM_STAGES_80 8
+#endif
+#ifndef TI_GEMM_STAGES_144
+#define TI_GEMM_STAGES_144 6
+#endif
+// SwiGLU16 tile width: up to kDeepRingMaxM rows the narrowest of 80 / 144 whose tiles cover all
+// rows in one wave of the GPU (at 256 tokens and N = 2 x 4864: 136 CTAs of 144 columns instead
+// of 76 of 256, so more SMs stream the weights and each re-reads less of the activations);
+// above, 256 (many waves).
+static int swiglu16_bn(int M, int N) {
+  static int cached_dev = -1, sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cached_dev != dev) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    cached_dev = dev;
+  }
+  if (M <= kDeepRingMaxM) {
+    const int64_t mt = (M + BM - 1) / BM;
+    if (mt * ((N + 79) / 80) <= sms) return 80;
+    if (mt * ((N + 143) / 144) <= sms) return 144;
+  }
+  return 256;
+}
+template <typename T>
+static int launch_swiglu16(int bn, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
+                           int K, const EpiArgs& e, cudaStream_t s) {
+  switch (bn) {
+    case 80: return launch_t<T, 80, TI_GEMM_STAGES_80, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s);
+    case 144: return launch_t<T, 144, TI_GEMM_STAGES_144, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s);
+    default:
+      return M <= kDeepRingMaxM
+                 ? launch_t<T, 256, TI_GEMM_STAGES_256, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s)
+                 : launch_t<T, 256, 2, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s);
+  }
+}
+
 }  // namespace gemm
 }  // namespace ti
 
@@ -965,9 +1036,16 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
     return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: null operand or bad size");
   if (dtype != TI_DTYPE_BF16 && dtype != TI_DTYPE_FP16)
     return set_error(TI_ERR_UNSUPPORTED, "gemm: dtype must be bf16 or fp16");
-  if (block_n <= 0) block_n = 128;
-  if (N % block_n || K % gemm::BK)
-    return set_error(TI_ERR_UNSUPPORTED, "gemm: N must be a multiple of block_n and K of 64");
+  if (epilogue == TI_EPI_SWIGLU16) {   // the library picks the tile width; no split-K
+    if (N % 16 || K % gemm::BK)
+      return set_error(TI_ERR_UNSUPPORTED, "gemm: SwiGLU16 needs N % 16 == 0 and K % 64 == 0");
+    block_n = gemm::swiglu16_bn(M, N);
+    split_k = 1;
+  } else {
+    if (block_n <= 0) block_n = 128;
+    if (N % block_n || K % gemm::BK)
+      return set_error(TI_ERR_UNSUPPORTED, "gemm: N must be a multiple of block_n and K of 64");
+  }
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15 || (lda % 8) || (ldb % 8))
     return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: operands must be 16-byte aligned with ld % 8 == 0");
   const int cl = epilogue == TI_EPI_RESIDUAL ? std::max(1, std::min(split_k, gemm::kMaxResidualSplit))
@@ -1012,6 +1090,7 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
     case TI_EPI_SWIGLU: return gemm::dispatch_bn<T, TI_EPI_SWIGLU>(block_n, cl, am, bm, M, N, K, e, s); \
     case TI_EPI_RESIDUAL: return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, cl, am, bm, M, N, K, e, s); \
     case TI_EPI_ARGMAX: return gemm::dispatch_bn<T, TI_EPI_ARGMAX>(block_n, 1, am, bm, M, N, K, e, s); \
+    case TI_EPI_SWIGLU16: return gemm::launch_swiglu16<T>(block_n, am, bm, M, N, K, e, s);   \
     default: return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue");             \
   }
   if (dtype == TI_DTYPE_BF16) { TI_GEMM_KIND(__nv_bfloat16) }

@@ -1,8 +1,8 @@
 """Weights in the reference's extracted checkpoint format (engine/loader.py:9-79): one
 .safetensors file with flat custom keys (``token_embeddings``, ``blocks.{i}.attn.q_proj.weight``,
 ``blocks.{i}.mlp.gate_proj`` ...), mapped to the reference module's state-dict names and loaded
-straight into this package's fused layouts (q/k/v in one matrix, gate/up interleaved per GEMM
-tile) by :meth:`Qwen2ForCausalLM.load_reference_state_dict`.
+straight into this package's fused layouts (q/k/v in one matrix, gate/up rows interleaved in
+groups of 8) by :meth:`Qwen2ForCausalLM.load_reference_state_dict`.
 """
 from __future__ import annotations
 

@@ -24,7 +24,7 @@ import torch
 from . import _native as N
 from .config import QwenConfig
 
-GATE_UP_TILE = 256          # block_n of the gate/up GEMM: 128 gate rows then 128 up rows
+GATE_UP_GROUP = 8           # gate/up weight rows interleaved 8 gate, 8 up (TI_EPI_SWIGLU16)
 LM_TILE = 128               # block_n of the lm_head GEMM (argmax partials per 128 columns)
 O_TILE = 64                 # block_n of the o_proj GEMM (+residual, split-K)
 DOWN_TILE = 128             # block_n of the down_proj GEMM (+residual, split-K)
@@ -62,7 +62,7 @@ class Qwen2ForCausalLM:
         if self.device.type != "cuda":
             raise RuntimeError("tiny_infra_b200 runs on a CUDA device only")
         c = self.config
-        if c.hidden_size % c.num_attention_heads or c.intermediate_size % (GATE_UP_TILE // 2):
+        if c.hidden_size % c.num_attention_heads or c.intermediate_size % GATE_UP_GROUP:
             raise RuntimeError("unsupported model dimensions")
         self.weights: dict[str, torch.Tensor] = {}
         self._ws = N.Workspace()
@@ -73,8 +73,9 @@ class Qwen2ForCausalLM:
     # ---- weights -------------------------------------------------------------------------
     def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
         """Load weights named as the reference module's state dict (models/qwen_25.py), fusing
-        q/k/v (+biases) into one [(NH+2KVH)*D, H] matrix and interleaving gate/up rows per
-        GEMM tile for the SwiGLU epilogue.  A missing ``lm_head.weight`` or one identical to the
+        q/k/v (+biases) into one [(NH+2KVH)*D, H] matrix and interleaving gate/up rows in
+        groups of 8 for the SwiGLU epilogue (any GEMM tile width that is a multiple of 16
+        then holds matching gate / up rows).  A missing ``lm_head.weight`` or one identical to the
         embedding means tied embeddings."""
         c, dev, dt = self.config, self.device, self.dtype
 
@@ -90,7 +91,7 @@ class Qwen2ForCausalLM:
         self.tied = lm is None or lm is sd["model.embed_tokens.weight"]
         W["lm_head"] = W["embed"] if self.tied else get("lm_head.weight")
         W["norm"] = get("model.norm.weight")
-        h = GATE_UP_TILE // 2
+        h = GATE_UP_GROUP
         for i in range(c.num_layers):
             p = f"model.layers.{i}"
             W[f"{i}.qkv"] = torch.cat([get(f"{p}.self_attn.q_proj.weight"),
@@ -280,9 +281,9 @@ class Qwen2ForCausalLM:
                                 O_TILE, split_o, stream))
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
                                    W[f"{li}.ln2"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
-            N.check(lib.ti_gemm(N.TI_EPI_SWIGLU, xn.data_ptr(), H, W[f"{li}.gate_up"].data_ptr(),
-                                H, T, 2 * I, H, act.data_ptr(), I, None, None, None, dt,
-                                GATE_UP_TILE, 1, stream))
+            N.check(lib.ti_gemm(N.TI_EPI_SWIGLU16, xn.data_ptr(), H,
+                                W[f"{li}.gate_up"].data_ptr(), H, T, 2 * I, H, act.data_ptr(), I,
+                                None, None, None, dt, 0, 1, stream))
             N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
                                 I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
                                 DOWN_TILE, split_d, stream))
