@@ -1912,8 +1912,7 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
   if (reinterpret_cast<uintptr_t>(plan) & 15)
     return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: buffer must be 16-byte aligned");
   if (!v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
-    // the planned decode takes the unplanned path for this shape; a zero header (chunk 0)
-    // also turns the projection's L2 warm-up off
+    // the planned decode takes the unplanned path for this shape (a zero header: chunk 0)
     if (plan_bytes < 32)
       return set_error(TI_ERR_WORKSPACE, "attention plan: buffer too small");
     cudaError_t e = cudaMemsetAsync(plan, 0, 32, reinterpret_cast<cudaStream_t>(stream));
