@@ -118,3 +118,47 @@ def test_unplanned_shape_gets_zero_header(cuda_device):
     ref, got, plan = _plain_and_planned(lib, N, q, k, v, bt, ctx, mb)
     assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
     assert (plan[:32] == 0).all()
+
+
+def test_v5_long_ranges(cuda_device, monkeypatch):
+    """64 sequences of 76k-90k tokens: more than 2048 stream positions per v5 CTA (the kernel
+    holds up to 4096; the planned call loads its slot in two rounds).  Planned equals plain bit
+    for bit, both agree with the v2 kernel, and three sequences agree with an fp32 torch
+    reference (tolerance: 2e-3 + half a bf16 ulp of the reference)."""
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    B, NH, KVH, D = 64, 14, 2, 64
+    rng = np.random.default_rng(8)
+    ctx_np = rng.integers(76000, 90001, B).astype(np.int32)
+    nblk = (ctx_np + 15) // 16
+    assert int(nblk.sum()) > 148 * 2048          # more than 2048 positions per CTA
+    NB = int(nblk.sum()) + 16
+    mb = int((90000 + 15) // 16)
+    perm = rng.permutation(NB).astype(np.int32)
+    bt_np = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        bt_np[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += int(nblk[b])
+    g = torch.Generator(device=cuda_device).manual_seed(8)
+    q = torch.randn(B, NH, D, device=cuda_device, generator=g).bfloat16()
+    k = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    v = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    ref5, got5, _ = _plain_and_planned(lib, N, q, k, v, bt_np, ctx_np, mb)
+    assert N.device_status() == 0
+    assert torch.equal(ref5.view(torch.int16), got5.view(torch.int16))
+    monkeypatch.setenv("TI_PAGED_ATTN_KERNEL", "v2")
+    ref2, _, _ = _plain_and_planned(lib, N, q, k, v, bt_np, ctx_np, mb)
+    monkeypatch.delenv("TI_PAGED_ATTN_KERNEL")
+    a, b2 = got5.float(), ref2.float()
+    assert ((a - b2).abs() <= 2e-3 + 2.0 ** -8 * b2.abs()).all(), float((a - b2).abs().max())
+    for b in (0, 31, 63):
+        n = int(ctx_np[b])
+        ids = torch.from_numpy(bt_np[b, :nblk[b]].astype(np.int64)).to(cuda_device)
+        kk = k[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        vv = v[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        qq = q[b].float().view(KVH, NH // KVH, D)
+        p = torch.softmax(qq @ kk.transpose(1, 2) / 8.0, dim=-1)
+        want = (p @ vv).reshape(NH, D)
+        err = (got5[b].float() - want).abs()
+        assert (err <= 2e-3 + 2.0 ** -9 * want.abs()).all(), float(err.max())

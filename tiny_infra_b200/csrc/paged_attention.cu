@@ -1391,30 +1391,37 @@ constexpr int kV5Pairs = 8;
 constexpr int kV5Stages = 3;
 constexpr int kV5Threads = (1 + 2 * kV5Pairs) * 32;
 
+// Stream positions of one v5 CTA held in shared memory (pool row and valid tokens of each):
+// 4096 cover 256 sequences of up to 32k tokens (the long-context replica workload).
+constexpr int kV5IdCap = 4096;
+
 struct CfgV5 {
   static constexpr int kTile = 2 * kBlock * 64 * 2;          // K (or V) of one block, 2 heads
   static constexpr int kStage = 2 * kTile;
   static constexpr int kRing = kV5Pairs * kV5Stages * kStage;   // 192 KB
   static constexpr int kBars = 2 * kV5Pairs * kV5Stages * 8;    // full, then empty
-  static constexpr int kIds = kV4IdCap * 4;
-  static constexpr int kVtok = kV4IdCap;
-  static constexpr int kOffBytes = ((kV2MaxBatch + 1) * 4 + 15) / 16 * 16;
-  static constexpr int kTotal = kRing + kBars + kIds + kVtok + kOffBytes + 1024;
-  static_assert(kTotal <= 227 * 1024, "v5 shared memory");
+  static constexpr int kIds = kV5IdCap * 4;
+  static constexpr int kVtok = kV5IdCap;
+  // then s_off[batch + 1] (padded to 16 bytes): the dynamic part, sized per launch
+  static constexpr int kFixed = kRing + kBars + kIds + kVtok + 1024;   // + alignment slack
+  static constexpr int kMaxSmem = 227 * 1024 - 256;   // 256 bytes for the static s_wsum / s_hdr
+  static constexpr int kMaxBatch = (kMaxSmem - kFixed) / 16 * 16 / 4 - 1;
+  static int total(int batch) { return kFixed + ((batch + 1) * 4 + 15) / 16 * 16; }
+  static_assert(kMaxBatch >= 1024, "v5 serves batches of at least 1024 sequences");
   static_assert((kRing + kBars) % 16 == 0 && kIds % 16 == 0 && kVtok % 16 == 0, "int4 copies");
 };
 
 // Plan layout (int32 words; base 16-byte aligned), written by plan_kernel for the v5 chunking:
 //   [0] total positions  [1] chunk  [2] consumers (CTAs x kV5Pairs)  [3] batch
-//   [4] ids word offset  [5] vtok byte offset  [6] kV5Pairs  [7] kV4IdCap
-//   [8 ..) s_off[0 .. batch] (padded to 4 words), then per CTA a kV4IdCap slot of ids (int32)
-//   and, after all id slots, per CTA a kV4IdCap slot of vtok (bytes).
+//   [4] ids word offset  [5] vtok byte offset  [6] kV5Pairs  [7] kV5IdCap
+//   [8 ..) s_off[0 .. batch] (padded to 4 words), then per CTA a kV5IdCap slot of ids (int32)
+//   and, after all id slots, per CTA a kV5IdCap slot of vtok (bytes).
 __host__ __device__ inline int64_t plan_ids_word(int batch) { return 8 + (batch + 1 + 3) / 4 * 4; }
 __host__ __device__ inline int64_t plan_vtok_byte(int batch, int ctas) {
-  return (plan_ids_word(batch) + (int64_t)ctas * kV4IdCap) * 4;
+  return (plan_ids_word(batch) + (int64_t)ctas * kV5IdCap) * 4;
 }
 inline size_t plan_bytes(int batch, int ctas) {
-  return (size_t)((plan_vtok_byte(batch, ctas) + (int64_t)ctas * kV4IdCap + 15) / 16 * 16);
+  return (size_t)((plan_vtok_byte(batch, ctas) + (int64_t)ctas * kV5IdCap + 15) / 16 * 16);
 }
 
 // One CTA per v5 CTA: the v5 prologue (resolve_stream), its ids / vtok kept in the plan's slot.
@@ -1425,9 +1432,9 @@ plan_kernel(Params p, int batch, int32_t* plan) {
   pdl_launch_dependents();
   __shared__ int s_off[kV2MaxBatch + 1];
   __shared__ int s_wsum[NT / 32];
-  int32_t* ids = plan + plan_ids_word(batch) + (int64_t)blockIdx.x * kV4IdCap;
+  int32_t* ids = plan + plan_ids_word(batch) + (int64_t)blockIdx.x * kV5IdCap;
   uint8_t* vtok = reinterpret_cast<uint8_t*>(plan) + plan_vtok_byte(batch, gridDim.x) +
-                  (int64_t)blockIdx.x * kV4IdCap;
+                  (int64_t)blockIdx.x * kV5IdCap;
   int chunk = 0, cb = 0, ce = 0;
   resolve_stream<2, NT>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb, ce);
   if (blockIdx.x == 0) {
@@ -1440,7 +1447,7 @@ plan_kernel(Params p, int batch, int32_t* plan) {
       plan[4] = (int)plan_ids_word(batch);
       plan[5] = (int)plan_vtok_byte(batch, gridDim.x);
       plan[6] = kV5Pairs;
-      plan[7] = kV4IdCap;
+      plan[7] = kV5IdCap;
     }
   }
 }
@@ -1476,16 +1483,18 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   }
   int chunk, cb, ce;
   if constexpr (PLANNED) {
-    // one round of loads: header, s_off, this CTA's id and vtok slots
+    // one round of loads: header, s_off and the first kV4IdCap positions of this CTA's id and
+    // vtok slots (the whole range for contexts up to ~2k tokens at 256 sequences); a longer
+    // range loads the rest in a second round once the header is known
     __shared__ int s_hdr[2];
     const int32_t* pl = p.plan;
     const int n_off = (batch + 1 + 3) / 4;
     const int4* g_off = reinterpret_cast<const int4*>(pl + 8);
     const int4* g_ids = reinterpret_cast<const int4*>(pl + plan_ids_word(batch) +
-                                                      (int64_t)blockIdx.x * kV4IdCap);
+                                                      (int64_t)blockIdx.x * kV5IdCap);
     const int4* g_vt = reinterpret_cast<const int4*>(
         reinterpret_cast<const uint8_t*>(pl) + plan_vtok_byte(batch, gridDim.x) +
-        (int64_t)blockIdx.x * kV4IdCap);
+        (int64_t)blockIdx.x * kV5IdCap);
     constexpr int n_ids = kV4IdCap / 4, n_vt = kV4IdCap / 16;
     for (int i = tid; i < n_off + n_ids + n_vt; i += kV5Threads) {
       if (i < n_off) reinterpret_cast<int4*>(s_off)[i] = g_off[i];
@@ -1494,7 +1503,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     }
     if (tid == 0) {
       const bool ok = pl[3] == batch && pl[2] == (int)gridDim.x * kV5Pairs &&
-                      pl[1] > 0 && (int64_t)pl[1] * kV5Pairs <= kV4IdCap;
+                      pl[1] > 0 && (int64_t)pl[1] * kV5Pairs <= kV5IdCap;
       if (!ok) raise_device_error(TI_DEVERR_ATTN_PLAN);   // a plan of another batch / grid
       s_hdr[0] = ok ? pl[0] : 0;
       s_hdr[1] = ok ? pl[1] : 1;
@@ -1504,6 +1513,14 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     cb = blockIdx.x * kV5Pairs * chunk;
     if (cb >= s_hdr[0]) return;
     ce = min(s_hdr[0], cb + kV5Pairs * chunk);
+    if (ce - cb > kV4IdCap) {   // the same for every thread of the CTA; ce - cb <= kV5IdCap
+      const int n_ids2 = (ce - cb + 3) / 4, n_vt2 = (ce - cb + 15) / 16;
+      for (int i = n_ids + tid; i < n_ids2; i += kV5Threads)
+        reinterpret_cast<int4*>(ids)[i] = g_ids[i];
+      for (int i = n_vt + tid; i < n_vt2; i += kV5Threads)
+        reinterpret_cast<int4*>(vtok)[i] = g_vt[i];
+      __syncthreads();
+    }
   } else {
     if (!resolve_stream<2, kV5Threads>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb,
                                        ce))
@@ -1667,13 +1684,15 @@ static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& 
   cudaGetDevice(&dev);
   if (set_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(decode_kernel_v5<T, PLANNED>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::total(C::kMaxBatch));
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention v5)");
     set_dev = dev;
   }
+  if (batch > C::kMaxBatch) return set_error(TI_ERR_UNSUPPORTED, "paged attention v5: batch too large");
   int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
-                         dim3(sm_count()), dim3(kV5Threads), C::kTotal, stream, 1, km, vm, p,
-                         batch);
+                         dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm,
+                         p, batch);
   if (rc) return rc;
   const int units = p.num_kv_heads / 2;
   return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
@@ -1768,9 +1787,10 @@ static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, in
   if (num_kv_heads % 2 || num_heads / num_kv_heads > 8 || max_blocks <= 0) return false;
   const int forced = attn::forced_kernel();
   if (forced != 0 && forced != 5) return false;
+  if (batch > attn::CfgV5::kMaxBatch) return false;
   const int64_t worst = (int64_t)batch * (num_kv_heads / 2) * max_blocks;
   return (int64_t)attn::v2_chunk(worst, attn::sm_count() * attn::kV5Pairs, max_blocks) *
-             attn::kV5Pairs <= attn::kV4IdCap;
+             attn::kV5Pairs <= attn::kV5IdCap;
 }
 
 static int decode_impl(
