@@ -1,6 +1,8 @@
 """Ragged causal prefill attention over the paged pool (ti_paged_prefill_attention) against the
 oracle (oracle.kernels.paged_prefill_attention, fp32), for both kernels: the tcgen05 one
-(TMEM accumulators, P split into bf16 hi + lo) and the mma.sync one (TI_PREFILL_ATTN_KERNEL=mma).
+(TMEM accumulators, P split into bf16 hi + lo; each tile's keys split over a cluster of two CTAs
+whose partials merge through distributed shared memory, or one CTA per tile with
+TI_PREFILL_ATTN_SPLIT=0) and the mma.sync one (TI_PREFILL_ATTN_KERNEL=mma).
 
 Cases: whole prompts from position 0, chunks starting at odd positions (chunked prefill),
 partial 16-token query tiles, a long prefix (several hundred 64-key steps), and a pool whose
@@ -69,17 +71,24 @@ def _run(dev, lens, starts, seed, grow=0.0, NH=14, KVH=2, D=64):
     assert N.device_status() == 0
 
 
-@pytest.mark.parametrize("kernel", ["tc", "mma"])
-def test_prefill_attention_ragged_chunks(cuda_device, monkeypatch, kernel):
+def _select(monkeypatch, kernel):
+    """tc: the tcgen05 kernel with every tile split over a cluster of two CTAs (the default);
+    tc1: the same kernel, one CTA per tile (TI_PREFILL_ATTN_SPLIT=0); mma: the mma.sync kernel."""
     if kernel == "mma":
         monkeypatch.setenv("TI_PREFILL_ATTN_KERNEL", "mma")
+    if kernel == "tc1":
+        monkeypatch.setenv("TI_PREFILL_ATTN_SPLIT", "0")
+
+
+@pytest.mark.parametrize("kernel", ["tc", "tc1", "mma"])
+def test_prefill_attention_ragged_chunks(cuda_device, monkeypatch, kernel):
+    _select(monkeypatch, kernel)
     _run(cuda_device, [37, 16, 5, 130, 64, 1], [0, 100, 2047, 0, 513, 77], seed=1)
 
 
-@pytest.mark.parametrize("kernel", ["tc", "mma"])
+@pytest.mark.parametrize("kernel", ["tc", "tc1", "mma"])
 def test_prefill_attention_long_prefix_and_rising_max(cuda_device, monkeypatch, kernel):
-    if kernel == "mma":
-        monkeypatch.setenv("TI_PREFILL_ATTN_KERNEL", "mma")
+    _select(monkeypatch, kernel)
     _run(cuda_device, [48, 200], [20000, 0], seed=2)
     _run(cuda_device, [33, 160], [3000, 0], seed=3, grow=0.004)
 

@@ -267,6 +267,12 @@ constexpr int kBarOff = kKV + kStages * kStageBytes;       // 98304
 constexpr int kSmem = kBarOff + 256 + 1024;                 // barriers + alignment slack
 constexpr int kTmemCols = 256;                 // S buffers at 0 and 64, O at 128
 constexpr int kThreads = 192;
+// Split-key cluster: each CTA's un-normalised partial (O rows, then (m, l) per row) goes over
+// its drained K/V ring; rows padded to 68 floats so that 8 consecutive rows start on 8
+// different 16-byte bank groups.
+constexpr int kPartStride = 68;
+constexpr int kPartMl = kKV + 128 * kPartStride * 4;
+static_assert(kPartMl + 128 * 16 <= kBarOff, "partials fit the K/V ring");
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
@@ -314,6 +320,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
   const int nkeys = start + q0 + nq;                  // keys 0 .. last query position
   const int nchunks = (nkeys + kChunk - 1) / kChunk;
   const int32_t* bt = p.block_tables + (int64_t)p.row_index[seq] * p.bt_stride;
+  // Split-key cluster (gridDim.z == 2): CTA 0 takes key chunks [0, c_mid), CTA 1 the rest, and
+  // the two partials are merged through distributed shared memory, so a long prefix costs each
+  // CTA about half of it.  c_mid never passes the tile's first query position: every row of
+  // CTA 1 sees a key in its first chunk, so its running max is finite from the start.
+  const bool split = gridDim.z > 1;
+  const int c_mid = split ? min(nchunks / 2, (start + q0) / kChunk) : 0;
+  const int c_begin = split && blockIdx.z == 1 ? c_mid : 0;
+  const int n_local = split ? (blockIdx.z == 0 ? c_mid : nchunks - c_mid) : nchunks;
 
   // ---- Q tile: row 16 h + t = query head kvh*G + h of token row0 + t (zero when h >= G or
   //      t >= nq), swizzled K-major
@@ -337,10 +351,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     // ---- producer: chunk j = blocks 4j .. 4j+3 (past the keys: block 0, masked later)
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_last();   // later query tiles re-read these blocks
-      for (int j = 0; j < nchunks; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages &&
-            !mbar_wait(kv_empty + 8 * st, ((j / kStages) - 1) & 1, TI_DEVERR_PREFILL_WAIT))
+      for (int jj = 0; jj < n_local; ++jj) {
+        const int j = c_begin + jj, st = jj % kStages;
+        if (jj >= kStages &&
+            !mbar_wait(kv_empty + 8 * st, ((jj / kStages) - 1) & 1, TI_DEVERR_PREFILL_WAIT))
           break;
         const uint32_t dst = sb + kKV + st * kStageBytes;
         mbar_arrive_expect_tx(kv_full + 8 * st, kStageBytes);
@@ -362,8 +376,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       constexpr uint32_t id_s = idesc_f16(128, kChunk, bf, false, false);
       constexpr uint32_t id_pv = idesc_f16(128, 64, bf, false, true);
       bool ok = true;
-      for (int j = 0; j <= nchunks && ok; ++j) {
-        if (j < nchunks) {
+      for (int j = 0; j <= n_local && ok; ++j) {   // this CTA's chunks, counted from 0
+        if (j < n_local) {
           const int st = j % kStages, b = j & 1;
           ok = mbar_wait(kv_full + 8 * st, (j / kStages) & 1, TI_DEVERR_PREFILL_WAIT);
           if (ok && j >= 2) ok = mbar_wait(s_free + 8 * b, ((j >> 1) - 1) & 1, TI_DEVERR_PREFILL_WAIT);
@@ -409,7 +423,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     };
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nchunks; ++j) {
+    for (int j = 0; j < n_local; ++j) {   // this CTA's chunks, counted from 0
       const int b = j & 1;
       if (!wait_all(s_full + 8 * b, (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
@@ -419,14 +433,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free + 8 * b);
-      const int k0 = j * kChunk;
+      const int k0 = (c_begin + j) * kChunk;
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kChunk; ++c) {
         sv[c] = (k0 + c <= qp) ? sv[c] * p.scale_log2 : -INFINITY;
         mx = fmaxf(mx, sv[c]);
       }
-      // chunk 0 holds key 0 <= every query position, so m is finite from the start
+      // the first chunk holds a key <= every query position, so m is finite from the start
       float alpha = 1.f;
       bool rescale = false;
       if (j == 0) {
@@ -474,11 +488,25 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
     }
-    if (ok && wait_all(pv_done, (nchunks - 1) & 1)) {
+    bool have = false;
+    float ov[64];
+    if (ok && n_local > 0 && wait_all(pv_done, (n_local - 1) & 1)) {
       tc_fence_after();
-      float ov[64];
       tmem_ld32(trow + 128, ov);
       tmem_ld32(trow + 160, ov + 32);
+      have = true;
+    }
+    if (split) {
+      // this CTA's partial row (zeros, m = -inf and l = 0 without chunks) for the cluster merge
+      const uint32_t po = sb + kKV + (uint32_t)(r * kPartStride) * 4;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4)
+        st_shared_v4(po + c * 4, __float_as_uint(have ? ov[c] : 0.f),
+                     __float_as_uint(have ? ov[c + 1] : 0.f), __float_as_uint(have ? ov[c + 2] : 0.f),
+                     __float_as_uint(have ? ov[c + 3] : 0.f));
+      st_shared_v4(sb + kPartMl + r * 16, __float_as_uint(have ? m : -INFINITY),
+                   __float_as_uint(have ? l : 0.f), 0u, 0u);
+    } else if (have) {
       if (h < G && t < nq) {
         const float inv = 1.f / l;
         T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(row0 + t) * p.out_stride +
@@ -495,12 +523,52 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       }
     }
   }
+  if (split) {
+    __syncwarp();     // warps 0 / 1: lane 0 ran the producer / MMA loop alone
+    cluster_sync();   // both CTAs' partials are in shared memory
+    if (warp >= 2) {
+      // rows [64 z, 64 z + 64) of the tile: two threads per row, 32 dims each; the two partials
+      // are read in a fixed order (deterministic)
+      const int i = tid - 64;
+      const int row = (int)blockIdx.z * 64 + (i >> 1), half = i & 1;
+      const int hh = row >> 4, tt = row & 15;
+      const uint32_t po = sb + kKV + (uint32_t)(row * kPartStride + half * 32) * 4;
+      const uint32_t pm = sb + kPartMl + (uint32_t)row * 16;
+      const float4 a = ld_peer_f4(map_peer(pm, 0)), b = ld_peer_f4(map_peer(pm, 1));
+      const float mm = fmaxf(a.x, b.x);
+      const float fa = a.x == -INFINITY ? 0.f : fast_exp2(a.x - mm);
+      const float fb = b.x == -INFINITY ? 0.f : fast_exp2(b.x - mm);
+      const float inv = 1.f / (fa * a.y + fb * b.y);
+      const uint32_t pa = map_peer(po, 0), pb = map_peer(po, 1);
+      if (hh < G && tt < nq) {
+        T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(row0 + tt) * p.out_stride +
+                 (int64_t)(kvh * G + hh) * 64 + half * 32;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          const float4 x0 = ld_peer_f4(pa + c * 4), x1 = ld_peer_f4(pa + c * 4 + 16);
+          const float4 y0 = ld_peer_f4(pb + c * 4), y1 = ld_peer_f4(pb + c * 4 + 16);
+          uint4 u;
+          u.x = Elem<T>::pack2((fa * x0.x + fb * y0.x) * inv, (fa * x0.y + fb * y0.y) * inv);
+          u.y = Elem<T>::pack2((fa * x0.z + fb * y0.z) * inv, (fa * x0.w + fb * y0.w) * inv);
+          u.z = Elem<T>::pack2((fa * x1.x + fb * y1.x) * inv, (fa * x1.y + fb * y1.y) * inv);
+          u.w = Elem<T>::pack2((fa * x1.z + fb * y1.z) * inv, (fa * x1.w + fb * y1.w) * inv);
+          *reinterpret_cast<uint4*>(dst + c) = u;
+        }
+      }
+    }
+    cluster_sync();   // the peer has finished reading this CTA's partials
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+static bool split_keys() {
+  const char* e = getenv("TI_PREFILL_ATTN_SPLIT");
+  return !(e && !strcmp(e, "0"));
 }
 
 template <typename T>
@@ -515,8 +583,10 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(prefill tc)");
     set_dev = dev;
   }
+  // every tile as a cluster of two CTAs splitting its keys (TI_PREFILL_ATTN_SPLIT=0: one CTA)
+  const int z = split_keys() ? 2 : 1;
   return launch_kernel("prefill attention launch", prefill_tc_kernel<T>,
-                       dim3(num_tiles, p.num_kv_heads), dim3(kThreads), kSmem, s, 1, km, vm, p);
+                       dim3(num_tiles, p.num_kv_heads, z), dim3(kThreads), kSmem, s, z, km, vm, p);
 }
 }  // namespace tc
 
