@@ -434,12 +434,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free + 8 * b);
       const int k0 = (c_begin + j) * kChunk;
+      // only chunks that reach past the tile's first query position need the causal mask (the
+      // test is the same for the whole CTA)
+      if (k0 + kChunk - 1 > start + q0) {
+#pragma unroll
+        for (int c = 0; c < kChunk; ++c) sv[c] = (k0 + c <= qp) ? sv[c] : -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kChunk; ++c) {
-        sv[c] = (k0 + c <= qp) ? sv[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[c]);
-      }
+      for (int c = 0; c < kChunk; ++c) mx = fmaxf(mx, sv[c]);
+      mx *= p.scale_log2;   // the scale is positive: max(s) * scale = max(s * scale)
       // the first chunk holds a key <= every query position, so m is finite from the start
       float alpha = 1.f;
       bool rescale = false;
@@ -454,7 +458,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
       uint32_t hi[kChunk / 2], lo[kChunk / 2];
 #pragma unroll
       for (int c = 0; c < kChunk; c += 2) {
-        const float p0 = fast_exp2(sv[c] - m), p1 = fast_exp2(sv[c + 1] - m);
+        const float p0 = fast_exp2(fmaf(sv[c], p.scale_log2, -m));   // 2^(s scale - m)
+        const float p1 = fast_exp2(fmaf(sv[c + 1], p.scale_log2, -m));
         l += p0 + p1;
         const uint32_t h2 = Elem<T>::pack2(p0, p1);
         const float2 hf = Elem<T>::unpack2(h2);
