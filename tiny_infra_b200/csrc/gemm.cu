@@ -948,6 +948,9 @@ static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap&
   }
 }
 
+#ifndef TI_QKV_MAX_SPLIT
+#define TI_QKV_MAX_SPLIT 8
+#endif
 #ifndef TI_GEMM_STAGES_QKV
 #define TI_GEMM_STAGES_QKV TI_GEMM_STAGES_64
 #endif
@@ -956,7 +959,7 @@ template <typename T>
 static int launch_qkv(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                       const EpiArgs& e, cudaStream_t s) {
   return M <= kDeepRingMaxM
-             ? dispatch_cl<T, 64, TI_GEMM_STAGES_QKV, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s)
+             ? dispatch_cl<T, 64, TI_GEMM_STAGES_QKV, TI_EPI_QKV_ROPE>(TI_QKV_MAX_SPLIT, am, bm, M, N, K, e, s)
              : dispatch_cl<T, 64, 4, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
 }
 
