@@ -1394,6 +1394,9 @@ constexpr int kV5Threads = (1 + 2 * kV5Pairs) * 32;
 // Stream positions of one v5 CTA held in shared memory (pool row and valid tokens of each):
 // 4096 cover 256 sequences of up to 32k tokens (the long-context replica workload).
 constexpr int kV5IdCap = 4096;
+// Positions the planned call loads with the plan header in its first round (the whole range of
+// a 256-sequence batch of contexts up to ~2k tokens); longer ranges take a second round.
+constexpr int kV5FirstRound = 2048;
 
 struct CfgV5 {
   static constexpr int kTile = 2 * kBlock * 64 * 2;          // K (or V) of one block, 2 heads
@@ -1483,9 +1486,8 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   }
   int chunk, cb, ce;
   if constexpr (PLANNED) {
-    // one round of loads: header, s_off and the first kV4IdCap positions of this CTA's id and
-    // vtok slots (the whole range for contexts up to ~2k tokens at 256 sequences); a longer
-    // range loads the rest in a second round once the header is known
+    // one round of loads: header, s_off and the first kV5FirstRound positions of this CTA's id
+    // and vtok slots; a longer range loads the rest in a second round once the header is known
     __shared__ int s_hdr[2];
     const int32_t* pl = p.plan;
     const int n_off = (batch + 1 + 3) / 4;
@@ -1495,7 +1497,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     const int4* g_vt = reinterpret_cast<const int4*>(
         reinterpret_cast<const uint8_t*>(pl) + plan_vtok_byte(batch, gridDim.x) +
         (int64_t)blockIdx.x * kV5IdCap);
-    constexpr int n_ids = kV4IdCap / 4, n_vt = kV4IdCap / 16;
+    constexpr int n_ids = kV5FirstRound / 4, n_vt = kV5FirstRound / 16;
     for (int i = tid; i < n_off + n_ids + n_vt; i += kV5Threads) {
       if (i < n_off) reinterpret_cast<int4*>(s_off)[i] = g_off[i];
       else if (i < n_off + n_ids) reinterpret_cast<int4*>(ids)[i - n_off] = g_ids[i - n_off];
@@ -1513,7 +1515,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     cb = blockIdx.x * kV5Pairs * chunk;
     if (cb >= s_hdr[0]) return;
     ce = min(s_hdr[0], cb + kV5Pairs * chunk);
-    if (ce - cb > kV4IdCap) {   // the same for every thread of the CTA; ce - cb <= kV5IdCap
+    if (ce - cb > kV5FirstRound) {   // the same for every thread of the CTA; ce - cb <= kV5IdCap
       const int n_ids2 = (ce - cb + 3) / 4, n_vt2 = (ce - cb + 15) / 16;
       for (int i = n_ids + tid; i < n_ids2; i += kV5Threads)
         reinterpret_cast<int4*>(ids)[i] = g_ids[i];
