@@ -104,6 +104,16 @@ def test_scheduler_matches_reference_trace():
 
     asyncio.run(drive())
     assert [r.generated_tokens for r in requests] == g["final"]
+    # the serving counters agree with the trace
+    st = sched.stats()
+    assert st["emitted_tokens"] == sum(len(t) for t in g["final"])
+    assert st["requests_finished"] + st["requests_failed"] == len(requests)
+    assert st["prefill_tokens"] == sum(len(r.prompt_tokens) for r in requests
+                                       if r.generated_tokens or r.error is None)
+    assert st["ticks"] >= st["decode_steps"] > 0 and st["mean_tick_s"] > 0.0
+    used = sum(1 for row in kv.alloc.block_tables.tolist() for b in row if b != -1)
+    assert abs(st["pool_occupancy"] - used / st["pool_blocks"]) < 1e-12
+    assert st["active_slots"] == sum(r is not None for r in sched.active_slots)
 
 
 def test_generate_stream_end_to_end():

@@ -17,11 +17,21 @@ order, so a failing request fails alone); decode is one CUDA-graph replay of
 plus the device sampler); sampling uses each request's own Philox stream
 (``sampler.sample_next_token``).  A backend only has to provide ``prefill(slots, requests)`` and
 ``decode(slots, requests)``; tests drive the scheduler with a host-only stand-in.
+
+Observability (no counterpart in the reference, which only prints): ``stats()`` returns host-side
+counters of the serving loop -- ticks, prompt tokens prefilled, tokens emitted, finished and
+failed requests, the last and mean tick time and the KV pool's occupancy -- kept with a clock
+read per tick and no device synchronisation; with ``TI_NVTX=1`` each tick's prefill and decode
+phases are NVTX ranges (``tick.prefill`` / ``tick.decode``) for Nsight timelines.
 """
 from __future__ import annotations
 
 import asyncio
+import contextlib
 import logging
+import os
+import time
+from dataclasses import dataclass
 from typing import AsyncGenerator, List, Optional
 
 import numpy as np
@@ -30,6 +40,26 @@ import torch
 log = logging.getLogger(__name__)
 
 _END_OF_STREAM = object()   # sentinel closing a request's token stream
+
+
+@dataclass
+class SchedulerStats:
+    """Host-side counters of a ContinuousBatcher (see ``ContinuousBatcher.stats``)."""
+    ticks: int = 0
+    prefill_tokens: int = 0        # prompt tokens prefilled (chunks included)
+    emitted_tokens: int = 0        # tokens handed to consumers (prefill's first + decode)
+    decode_steps: int = 0
+    requests_finished: int = 0
+    requests_failed: int = 0
+    last_tick_s: float = 0.0
+    total_tick_s: float = 0.0
+
+
+def _nvtx_range(name: str):
+    """An NVTX range when TI_NVTX=1 (read per call: cheap, and settable at run time)."""
+    if os.environ.get("TI_NVTX") == "1":
+        return torch.cuda.nvtx.range(name)
+    return contextlib.nullcontext()
 
 
 class GenerationRequest:
@@ -75,6 +105,21 @@ class ContinuousBatcher:
         self.eos_token_id = eos_token_id
         self.backend = backend if backend is not None else EngineBackend(
             model, kv_cache, self.cos_cache, self.sin_cache)
+        self._stats = SchedulerStats()
+
+    def stats(self) -> dict:
+        """Counters of the serving loop so far, plus the KV pool's occupancy (blocks held by
+        sequences / all blocks) and the number of occupied slots."""
+        st = self._stats
+        d = dict(st.__dict__)
+        d["mean_tick_s"] = st.total_tick_s / st.ticks if st.ticks else 0.0
+        alloc = getattr(self.kv_cache, "alloc", None)
+        if alloc is not None:
+            total = int(alloc.total_physical_blocks)
+            d["pool_blocks"] = total
+            d["pool_occupancy"] = (total - len(alloc.free_blocks)) / total if total else 0.0
+        d["active_slots"] = sum(r is not None for r in self.active_slots)
+        return d
 
     def _init_rope_cache(self):
         """cos/sin [max_seq_len, head_dim/2] float32 with base 1e6 (engine/scheduler.py:36-48)."""
@@ -140,18 +185,25 @@ class ContinuousBatcher:
         return any(req is not None for req in self.active_slots)
 
     def _step_generation(self):
+        t0 = time.perf_counter()
         prefill_indices, decode_indices = [], []
         for slot_idx, req in enumerate(self.active_slots):
             if req is not None:
                 (decode_indices if req.is_prefilled else prefill_indices).append(slot_idx)
         if prefill_indices:
-            self._execute_prefill_batch(prefill_indices)
+            with _nvtx_range("tick.prefill"):
+                self._execute_prefill_batch(prefill_indices)
         if decode_indices:
             try:
-                self._execute_decode(decode_indices)
+                with _nvtx_range("tick.decode"):
+                    self._execute_decode(decode_indices)
             except Exception as e:   # noqa: BLE001 - the reference fails the whole decode batch
                 for slot_idx in decode_indices:
                     self._finish_request(slot_idx, reason="Error during decode", error=e)
+        st = self._stats
+        st.ticks += 1
+        st.last_tick_s = time.perf_counter() - t0
+        st.total_tick_s += st.last_tick_s
 
     def _finish_request(self, slot_idx: int, reason: str, error: Optional[BaseException] = None):
         req = self.active_slots[slot_idx]
@@ -163,14 +215,17 @@ class ContinuousBatcher:
         self.kv_cache.free_batch_slot(slot_idx)
         self.active_slots[slot_idx] = None
         if error:
+            self._stats.requests_failed += 1
             log.warning("slot %d request terminated due to error: %s", slot_idx, error)
         else:
+            self._stats.requests_finished += 1
             log.debug("slot %d request completed: %s", slot_idx, reason)
 
     def _emit(self, slot_idx: int, token: int, phase: str) -> None:
         req = self.active_slots[slot_idx]
         req.generated_tokens.append(token)
         req.token_queue.put_nowait(token)
+        self._stats.emitted_tokens += 1
         hit_eos = self.eos_token_id is not None and token == self.eos_token_id
         hit_max = len(req.generated_tokens) >= req.max_new_tokens
         if hit_eos or hit_max:
@@ -206,6 +261,7 @@ class ContinuousBatcher:
                 self._finish_request(slot_idx, reason="Error during prefill", error=res)
                 continue
             req.prefill_pos += n
+            self._stats.prefill_tokens += n
             if req.prefill_pos >= len(req.prompt_tokens):
                 self._emit(slot_idx, int(res), "prefill")
 
@@ -213,6 +269,7 @@ class ContinuousBatcher:
         """One batched decode step (engine/scheduler.py:250-281)."""
         reqs = [self.active_slots[s] for s in decode_indices]
         tokens = self.backend.decode(decode_indices, reqs)
+        self._stats.decode_steps += 1
         for slot_idx, tok in zip(decode_indices, tokens):
             self._emit(slot_idx, int(tok), "")
 
