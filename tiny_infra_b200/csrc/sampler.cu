@@ -120,6 +120,50 @@ __device__ __forceinline__ void row_scan(const Row<T>& row, int V, F&& f) {
   for (int j = nvec * kVec + (int)threadIdx.x; j < V; j += kThreads) f(row.x(j), j);
 }
 
+// The same walk over 16-bit rows a vector at a time: fv(b, j0) gets each aligned 16-byte vector
+// (8 raw elements, first index j0), fs(x, j) the raw elements of an unaligned row and of the
+// tail; a thread sees its vectors in increasing index order, then its tail elements.  The passes use it to test a whole
+// vector with a few packed instructions (its maximum) and look at single elements only in the
+// rare vectors that can matter: the per-element work was what bounded them.
+template <typename T, typename FV, typename FS>
+__device__ __forceinline__ void row_scan_vec(const Row<T>& row, int V, FV&& fv, FS&& fs) {
+  static_assert(sizeof(T) == 2, "16-bit rows");
+  constexpr int U = 8;
+  const int nvec = (reinterpret_cast<uintptr_t>(row.p) & 15) == 0 ? V / 8 : 0;
+  const uint4* pv = reinterpret_cast<const uint4*>(row.p);
+  int v = threadIdx.x;
+  for (; v + (U - 1) * kThreads < nvec; v += U * kThreads) {
+    uint4 buf[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) buf[u] = __ldg(pv + v + u * kThreads);
+#pragma unroll
+    for (int u = 0; u < U; ++u) fv(buf[u], (v + u * kThreads) * 8);
+  }
+  for (; v < nvec; v += kThreads) fv(__ldg(pv + v), v * 8);
+  for (int j = nvec * 8 + (int)threadIdx.x; j < V; j += kThreads) fs(Elem<T>::to_f(row.p[j]), j);
+}
+
+// Largest of a 16-byte vector's 8 elements: NaN-ignoring (a number wins over NaN) or, with
+// PROPAGATE = true, NaN when any element is NaN.
+template <typename T, bool PROPAGATE>
+__device__ __forceinline__ float vec_max(const uint4& b) {
+  using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+  const T2* h = reinterpret_cast<const T2*>(&b);
+  T2 a, c;
+  if constexpr (PROPAGATE) {
+    a = __hmax2_nan(h[0], h[1]);
+    c = __hmax2_nan(h[2], h[3]);
+    a = __hmax2_nan(a, c);
+  } else {
+    a = __hmax2(h[0], h[1]);
+    c = __hmax2(h[2], h[3]);
+    a = __hmax2(a, c);
+  }
+  const float lo = Elem<T>::to_f(a.x), hi = Elem<T>::to_f(a.y);
+  if constexpr (PROPAGATE) return (lo != lo || hi != hi) ? lo + hi : fmaxf(lo, hi);
+  else return fmaxf(lo, hi);
+}
+
 // Weight of element with value x in 32.32 fixed point (exp(x - m), x <= m), 0 when not a
 // candidate.
 __device__ __forceinline__ unsigned long long weight(float x, float m) {
@@ -272,12 +316,29 @@ __device__ bool topk_fast(Shared& sh, const Row<T>& row, int V, int k, float m, 
   const uint32_t bound = (uint32_t)(sh.cand[k - 1] >> 32);
   __syncthreads();
   // compact the elements at or above the bound: (key << 32) | ~index
-  row_scan(row, V, [&](float x, int j) {   // few elements pass: one shared atomic each
+  auto keep = [&](float x, int j) {   // few elements pass: one shared atomic each
     const uint32_t key = f2key(x);
     if (key < bound) return;
     const int slot = atomicAdd(&sh.cand_n, 1);
     if (slot < kCand) sh.cand[slot] = ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)j;
-  });
+  };
+  bool scanned = false;
+  if constexpr (sizeof(T) == 2) {
+    if (row.inv_t > 0.f) {
+      // an element's key reaches the bound only if its scaled value is not below the bound's
+      // value, so a vector whose scaled maximum is below it holds none (the maximum propagates
+      // NaN: such vectors take the exact per-element test)
+      const float thr = key2f(bound);
+      row_scan_vec(row, V, [&](const uint4& b, int j0) {
+        if (vec_max<T, true>(b) * row.inv_t < thr) return;
+        const T* e = reinterpret_cast<const T*>(&b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) keep(Elem<T>::to_f(e[i]) * row.inv_t, j0 + i);
+      }, [&](float x, int j) { keep(x * row.inv_t, j); });
+      scanned = true;
+    }
+  }
+  if (!scanned) row_scan(row, V, keep);
   __syncthreads();
   const int n = sh.cand_n;
   if (n > kCand) return false;
@@ -364,9 +425,34 @@ sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __re
   // ---- max and first argmax
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  row_scan(row, V, [&](float x, int j) {
+  auto take = [&](float x, int j) {
     if (x > best || (x == best && j < bi)) { best = x; bi = j; }
-  });
+  };
+  if constexpr (sizeof(T) == 2) {
+    if (row.inv_t > 0.f) {
+      // raw values: a positive scale keeps the order (and rounds monotonically), so the scaled
+      // maximum is the raw one scaled and the first index of either is the same for scale 1
+      // (greedy rows, the only ones that use it); a thread's vectors come in increasing index
+      // order, so a vector whose maximum only ties the thread's best holds no earlier index
+      float braw = -INFINITY;
+      row_scan_vec(row, V, [&](const uint4& b, int j0) {
+        const float vm = vec_max<T, false>(b);
+        if (vm > braw) {
+          const T* e = reinterpret_cast<const T*>(&b);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (Elem<T>::to_f(e[i]) == vm) { braw = vm; bi = j0 + i; break; }
+        }
+      }, [&](float x, int j) {
+        if (x > braw) { braw = x; bi = j; }
+      });
+      best = braw * row.inv_t;
+    } else {
+      row_scan(row, V, take);
+    }
+  } else {
+    row_scan(row, V, take);
+  }
   sh.tmax[tid] = best;   // this thread's maximum (top-k fast path)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
