@@ -1,6 +1,6 @@
 """Generate golden vectors by running the reference project's own Python code on the CPU.
 
-Run in a container where the reference checkout is available (it is not on the GPU box):
+Run where the reference checkout is available (a CUDA machine need not have it):
 
     python tests/golden/make_golden.py --ref /root/reference
 

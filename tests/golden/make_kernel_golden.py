@@ -1,6 +1,6 @@
 """Record the outputs of the reference project's own CUDA kernels on seeded inputs.
 
-Runs on a GPU box, with the reference kernels prebuilt from the reference sources by
+Runs on a machine with a B200, with the reference kernels prebuilt from the reference sources by
 ``oracle/build_ref.py`` (into ``oracle/_ref``):
 
     python tests/golden/make_kernel_golden.py --out tests/golden/kernel_golden.npz
