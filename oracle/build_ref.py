@@ -8,8 +8,8 @@ lie in the reference checkout, the three kernel/binding pairs the reference ship
     src/fused_swiglu.cu + src/swiglu_binding.cpp  -> oracle/_ref/custom_swiglu/*.so
 
 as PyTorch extensions for sm_100a (the reference builds with ``-arch=native``, setup.py:18).
-The built modules travel with the repository to the GPU box (``oracle/_ref`` is git-ignored but
-not excluded from the snapshot); there ``load_ref(name)`` imports them so that
+The built modules travel with a copy of the repository to a machine with a B200 (``oracle/_ref``
+is git-ignored, not excluded from copies); there ``load_ref(name)`` imports them so that
 ``tests/golden/make_kernel_golden.py`` can record the reference kernels' outputs.
 
     python oracle/build_ref.py --ref /root/reference
