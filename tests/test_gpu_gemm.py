@@ -90,22 +90,27 @@ def test_swiglu_epilogue(cuda_device, bn):
     _close_bf16(out.float().cpu().numpy(), g / (1 + np.exp(-g)) * u)
 
 
-@pytest.mark.parametrize("M,I", [(256, 4864), (200, 4864), (100, 1032), (256, 1032),
-                                 (4096, 4864), (300, 1032), (1, 4864)])
-def test_swiglu16_epilogue(cuda_device, M, I):
+@pytest.mark.parametrize("M,I,dt", [(256, 4864, "bf16"), (200, 4864, "bf16"),
+                                    (100, 1032, "bf16"), (256, 1032, "bf16"),
+                                    (4096, 4864, "bf16"), (300, 1032, "bf16"), (1, 4864, "bf16"),
+                                    (256, 4864, "fp16"), (4096, 1032, "fp16")])
+def test_swiglu16_epilogue(cuda_device, M, I, dt):
     """gate/up + SwiGLU with gate/up rows interleaved in groups of 8 (TI_EPI_SWIGLU16), the
     model's layout: the library picks 80-, 144- or 256-wide tiles by M (80 at M <= 128 and
     2I = 2064: a ragged last tile of 64 columns; 144 at M = 200 / 256 and 2I = 9728: a last tile
     of 80; 256 above 256 rows, ragged at 2I = 2064).  Output columns past I stay untouched."""
     from tiny_infra_b200 import _native as N_
     K = 896
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+    rnd = bf16_round if dt == "bf16" else (lambda x: x.astype(np.float16).astype(np.float32))
     rng = np.random.default_rng(M + I)
-    a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
-    wg = bf16_round((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
-    wu = bf16_round((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
+    a = rnd(rng.standard_normal((M, K)).astype(np.float32))
+    wg = rnd((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
+    wu = rnd((rng.standard_normal((I, K)) * 0.05).astype(np.float32))
     inter = np.stack([wg.reshape(I // 8, 8, K), wu.reshape(I // 8, 8, K)], axis=1).reshape(2 * I, K)
-    out = torch.full((M, I + 8), 7.0, dtype=torch.bfloat16, device="cuda")
-    _gemm(N_.TI_EPI_SWIGLU16, _dev(a), _dev(inter), M, 2 * I, K, out=out, ldo=I + 8, block_n=0)
+    out = torch.full((M, I + 8), 7.0, dtype=tdt, device="cuda")
+    _gemm(N_.TI_EPI_SWIGLU16, _dev(a, tdt), _dev(inter, tdt), M, 2 * I, K, out=out, ldo=I + 8,
+          block_n=0)
     g, u = a @ wg.T, a @ wu.T
     got = out.float().cpu().numpy()
     _close_bf16(got[:, :I], g / (1 + np.exp(-g)) * u)
