@@ -477,10 +477,11 @@ struct CfgV2 {
 };
 
 // chunk of the block stream per warp: balanced, but at least max_blocks / 16 (so that a unit is
-// cut into at most kV2MaxPieces pieces, which bounds the split-K workspace) and at least 4
+// cut into at most kV2MaxPieces pieces, which bounds the split-K workspace) and at least 2 (small
+// batches: 8 sequences of up to 512 tokens take 9.7 us with 2, 11.2 us with 4, measured)
 __host__ __device__ inline int v2_chunk(int64_t total_blocks, int warps, int max_blocks) {
   int64_t c = (total_blocks + warps - 1) / warps;
-  const int lo = max(4, (max_blocks + 15) / 16);
+  const int lo = max(2, (max_blocks + 15) / 16);
   return (int)(c < lo ? lo : c);
 }
 
