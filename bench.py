@@ -24,7 +24,23 @@ import sys
 import threading
 import time
 
-import numpy as np
+
+def _cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# The CPU arms (the reference arm, and the cpu_baseline leg) run the numpy oracle, whose BLAS
+# reads its thread count when numpy is first imported; torchrun exports OMP_NUM_THREADS=1 to
+# every rank.  Rank 0 does all the CPU work (the other ranks only wait), so it gets every host
+# core before numpy loads.
+if os.environ.get("RANK", "0") == "0":
+    for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = str(_cores())
+
+import numpy as np  # noqa: E402
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -45,6 +61,9 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--seqs", type=int, default=SEQS,
+                    help="decode workload: sequences per GPU (256: the headline; 32: the "
+                         "full-model decode configuration of 32 sequences)")
     ap.add_argument("--workload", choices=["decode", "serving", "long"], default="decode",
                     help="decode: the 256-sequence decode step (the headline metric); serving: "
                          "a Poisson request stream through the continuous batcher")
@@ -67,12 +86,13 @@ def _dist():
 
 
 def _config(world, extra=None):
-    c = {"workload": "qwen2.5-0.5b decode step, 256 ragged seqs/GPU, ctx U[128,2048], greedy, "
-                     "random-init bf16 weights (std 0.02, tied), KV pre-filled N(0,1)",
+    c = {"workload": f"qwen2.5-0.5b decode step, {SEQS} ragged seqs/GPU, ctx U[128,2048], "
+                     "greedy, random-init bf16 weights (std 0.02, tied), KV pre-filled N(0,1)",
          "seqs_per_gpu": SEQS, "ctx_range": [CTX_LO, CTX_HI], "block_size": 16,
          "parallelism": f"replicas x{world} (no collectives)",
          "context_window": f"lengths reset to the sampled ctx every {WINDOW} steps: each step "
-                           f"decodes at ctx + 0..{WINDOW - 1}",
+                           f"decodes at ctx + 0..{WINDOW - 1}; timed steps replayed as one "
+                           f"CUDA graph per {WINDOW}-step window",
          "l2": "inputs larger than L2 (~4.4 GB read per step), no flush"}
     if extra:
         c.update(extra)
@@ -159,7 +179,7 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------------------------
 def build_workload(device, seed, steps_total):
-    """Engine replica with 256 sequences at their sampled context lengths, KV pre-filled."""
+    """Engine replica with SEQS sequences at their sampled context lengths, KV pre-filled."""
     import torch
     from tiny_infra_b200.cache_manager import KVCacheManager
     from tiny_infra_b200.config import QwenConfig
@@ -295,11 +315,14 @@ def oracle_decode_steps(state, steps, min_seconds=0.0, max_seconds=None, ctx0=No
     return done, time.perf_counter() - t0
 
 
-def _cores():
+def _blas_threads():
+    """Threads the numpy BLAS actually runs with (threadpoolctl), else the host core count."""
     try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count()
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else _cores()
+    except Exception:  # threadpoolctl missing or unable to inspect the library
+        return _cores()
 
 
 # ---------------------------------------------------------------------------------------------
@@ -344,8 +367,8 @@ def run_reference(a, rank, world):
             "steps": done, "warmup": min(a.warmup, 2), "ms_per_step": round(secs / done * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": _config(1, {"sample": f"{n} of the 256 sequences per step"}),
-            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": _cores(),
+            "config": _config(1, {"sample": f"{n} of the {SEQS} sequences per step"}),
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": _blas_threads(),
                              "kind": "port",
                              "sample": f"{n} sequences of the workload per decode step, "
                                        f"{done} steps, numpy fp32 restatement of the reference path"},
@@ -365,8 +388,9 @@ def run_ours(a, rank, world, local):
     device = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=device)
+        # replicas: the only cross-rank steps are the barrier and the max over ranks of the
+        # timed region, host-side work for gloo (no NCCL: the data path has no collective)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     steps_total = a.warmup + a.steps
     # the engine is built for warm-up + timed + e2e steps, and at least one context window
     cfg, sd, model, kv, engine, slots, ctx, first = build_workload(
@@ -393,24 +417,48 @@ def run_ours(a, rank, world, local):
         engine._replay(rows)
         engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
 
-    # warm-up (also captures the graph)
+    # warm-up (also captures the one-step graph)
     for k in range(a.warmup):
         resident_step(k)
+    torch.cuda.synchronize()
+
+    # The timed steps run as whole windows: one CUDA graph holds a window's WINDOW steps
+    # (length reset, each step's new blocks, all its kernels, the token feedback), so the host
+    # issues one replay per window instead of four calls per step.  Every step does the same
+    # work as a one-step replay.
+    def window_graph(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for k in range(n):
+                if k == 0:
+                    kv.seq_len[:SEQS].copy_(ctx0_dev)
+                engine.d_in[2, :rows].copy_(plan[k])
+                engine._launch(rows)
+                engine.d_in[0, :SEQS].copy_(engine.next_tok[:SEQS])
+        return g
+
+    full, rem = divmod(a.steps, WINDOW)
+    g_full = window_graph(WINDOW) if full else None
+    g_rem = window_graph(rem) if rem else None
+    for g in (g_full, g_rem):            # first replay uploads the graph (untimed)
+        if g is not None:
+            g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = N.launch_count()
     e0.record()
-    for k in range(a.steps):
-        resident_step(k)
+    for _ in range(full):
+        g_full.replay()
+    if g_rem is not None:
+        g_rem.replay()
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    secs = replicas.max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
+    secs = replicas.max_over_ranks(e0.elapsed_time(e1) / 1e3)
     launches = engine.launches_per_step.get((rows, False), 0) * a.steps
     value = world * SEQS * a.steps / secs
 
@@ -438,7 +486,7 @@ def run_ours(a, rank, world, local):
         toks = e2e_step(k, toks)
     e2[1].record()
     torch.cuda.synchronize()
-    esecs = replicas.max_over_ranks(e2[0].elapsed_time(e2[1]) / 1e3, device)
+    esecs = replicas.max_over_ranks(e2[0].elapsed_time(e2[1]) / 1e3)
     e2e = world * SEQS * a.steps / esecs
 
     roof = attention_roofline(engine, kv, cfg, ctx, 50, peak) if rank == 0 else None
@@ -451,12 +499,13 @@ def run_ours(a, rank, world, local):
         oracle_decode_steps(st, 1, ctx0=ctx[:CPU_SAMPLE_SEQS])
         done, csecs = oracle_decode_steps(st, 2, min_seconds=10.0, ctx0=ctx[:CPU_SAMPLE_SEQS])
         cpu = {"value": round(CPU_SAMPLE_SEQS * done / csecs, 2), "unit": "tokens/s",
-               "cores": _cores(), "kind": "port",
-               "sample": f"{CPU_SAMPLE_SEQS} of the 256 sequences, {done} greedy decode steps, "
+               "cores": _blas_threads(), "kind": "port",
+               "sample": f"{CPU_SAMPLE_SEQS} of the {SEQS} sequences, {done} greedy decode steps, "
                          "numpy fp32 restatement of the reference path (oracle/)"}
     if world > 1:
         dist.barrier()
     engine.graphs.clear()
+    del g_full, g_rem
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -853,8 +902,7 @@ def run_long(a, rank, world, local):
     device = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=device)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
     LO, HI, OUT, SLOTS = 8192, 32768, 128, 256
     total_req = a.requests if a.requests != 1024 else 2048
     rng = np.random.default_rng(a.seed)
@@ -921,7 +969,7 @@ def run_long(a, rank, world, local):
         kv_tok += int(ctx.sum()) * OUT + len(ctx) * OUT * (OUT + 1) // 2
     clocks = sampler.stop()
     status = N.device_status()
-    tsecs = replicas.max_over_ranks(secs, device)
+    tsecs = replicas.max_over_ranks(secs)
     all_tokens = total_req * OUT
     steps = -(-len(ctx_mine) // SLOTS) * OUT
     if world > 1:
@@ -953,8 +1001,12 @@ def run_long(a, rank, world, local):
 
 
 def main():
+    global SEQS, METRIC
     a = _args()
     rank, world, local = _dist()
+    if a.seqs != SEQS:
+        SEQS = a.seqs
+        METRIC = f"decode tokens/sec @{SEQS} ragged seqs per B200; paged-attn HBM GB/s"
     if a.workload == "serving":
         return run_serving(a) if rank == 0 else 0
     if a.workload == "long":

@@ -191,6 +191,9 @@ int ti_embedding(float* out, const void* table, const int32_t* ids, int num_toke
  *                    ignored: the library picks the tile width (up to 256 rows: 80 or 144, so
  *                    that one wave of CTAs covers the GPU; above: 256)
  *   TI_EPI_RESIDUAL  out (float32 [M, N], ldo) += D
+ *   TI_EPI_RESIDUAL_DET  the same, bit-reproducible: the K slices of a tile run on a
+ *                    thread-block cluster (1, 2, 4 or 8 slices) and are summed in a fixed order
+ *                    before the one add per element (parity runs; ~13 % slower decode steps)
  *   TI_EPI_ARGMAX    aux_val/aux_idx [M, N/block_n] = (max, first argmax) of each row within each
  *                    block_n column tile; `out` (dtype logits) is also written when not NULL
  * split_k is an upper bound on the split-K factor; it is lowered until the launch fits one wave
@@ -207,6 +210,7 @@ int ti_embedding(float* out, const void* table, const int32_t* ids, int num_toke
 #define TI_EPI_RESIDUAL 2
 #define TI_EPI_ARGMAX 3
 #define TI_EPI_SWIGLU16 5
+#define TI_EPI_RESIDUAL_DET 6
 int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
             int K, void* out, int64_t ldo, const void* bias, float* aux_val, int32_t* aux_idx,
             int dtype, int block_n, int split_k, void* stream);

@@ -12,7 +12,7 @@ The built modules travel with a copy of the repository to a machine with a B200 
 is git-ignored, not excluded from copies); there ``load_ref(name)`` imports them so that
 ``tests/golden/make_kernel_golden.py`` can record the reference kernels' outputs.
 
-    python oracle/build_ref.py --ref /root/reference
+    python oracle/build_ref.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -24,6 +24,18 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
+# Where this recipe and tests/golden/make_golden.py look for the reference checkout when neither
+# --ref nor TINY_INFRA_REF names one: the one place the checkout's location is written down.
+_CHECKOUT = "/root/reference"
+
+
+def reference_root(arg: str | None = None) -> str | None:
+    """The reference checkout to read: ``arg``, else $TINY_INFRA_REF, else the build
+    container's checkout if it exists there; None when there is none (e.g. on a GPU box)."""
+    for cand in (arg, os.environ.get("TINY_INFRA_REF")):
+        if cand:
+            return cand
+    return _CHECKOUT if os.path.isdir(os.path.join(_CHECKOUT, "src")) else None
 MODULES = {
     "custom_paged_attn": ("src/attention.cu", "src/attention_binding.cpp"),
     "custom_rope": ("src/fused_rope.cu", "src/rope_binding.cpp"),
@@ -62,10 +74,13 @@ def load_ref(name: str):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TINY_INFRA_REF", "/root/reference"))
+    ap.add_argument("--ref", default=None, help="reference checkout (default: $TINY_INFRA_REF)")
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
-    for p in build(a.ref, a.verbose):
+    ref = reference_root(a.ref)
+    if ref is None:
+        ap.error("no reference checkout: pass --ref or set TINY_INFRA_REF")
+    for p in build(ref, a.verbose):
         print("built", p)
 
 

@@ -70,7 +70,7 @@ def init_weights(cfg: OracleConfig, seed: int = 0, std: float = 0.02, tied: bool
 def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np.ndarray,
             cache: OracleKVCache, cos: np.ndarray, sin: np.ndarray, *,
             device_rounding: str | None = None, last_only: bool = False,
-            chunked_prefill: bool = False) -> np.ndarray:
+            chunked_prefill: bool = False, layer_hook=None) -> np.ndarray:
     """``Qwen2ForCausalLM.forward`` (models/qwen_25.py:239-251, :205-230, :161-192, :51-151).
 
     input_ids [B, S] -> logits [B, S, V] (or [B, 1, V] with ``last_only``).  The cache is
@@ -85,6 +85,9 @@ def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np
     ``chunked_prefill`` makes S>1 calls attend over the paged pool (earlier tokens of the
     sequence included) instead of the reference's self-only SDPA; both agree when the call
     starts at seq_len 0.
+
+    ``layer_hook(layer_index, h)`` (optional) sees the float32 residual stream ``h`` [B, S, H]
+    after every decoder layer (models/qwen_25.py:226-228).
     """
     rd = (lambda x: round_to(x, device_rounding))
     B, S = input_ids.shape
@@ -135,6 +138,8 @@ def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np
         u = x @ W[f"{p}.mlp.up_proj.weight"].T
         a = rd(kernels.swiglu(np.concatenate([g, u], axis=-1)))                # :146-148
         h = a @ W[f"{p}.mlp.down_proj.weight"].T + res                        # :151, :191
+        if layer_hook is not None:
+            layer_hook(li, h)
     if last_only:
         h = h[:, -1:]
     h = kernels.rmsnorm(h, W["model.norm.weight"], eps)                        # :230

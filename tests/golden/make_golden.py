@@ -2,7 +2,7 @@
 
 Run where the reference checkout is available (a CUDA machine need not have it):
 
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 The reference's ``models/qwen_25.py`` imports three native modules (``engine.ops.custom_*``)
 whose prebuilt binaries are absent from the reference checkout.  This script registers a
@@ -331,10 +331,15 @@ def scheduler_trace(out_dir: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TINY_INFRA_REF", "/root/reference"))
+    ap.add_argument("--ref", default=None, help="reference checkout (default: $TINY_INFRA_REF)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
-    sys.path.insert(0, a.ref)
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle.build_ref import reference_root
+    ref = reference_root(a.ref)
+    if ref is None:
+        ap.error("no reference checkout: pass --ref or set TINY_INFRA_REF")
+    sys.path.insert(0, ref)
     torch.manual_seed(0)
     install_ops_shim()
     import builtins

@@ -139,6 +139,28 @@ def test_residual_split_k(cuda_device, split, bn):
     assert (diff <= split * 2.0 ** -23 * (np.abs(got) + rms)).all(), float(diff.max())
 
 
+@pytest.mark.parametrize("M,N,K,split,bn", [(256, 896, 4864, 16, 128), (256, 896, 896, 7, 64),
+                                            (32, 896, 4864, 16, 128), (37, 896, 896, 2, 64),
+                                            (300, 896, 4864, 8, 128)])
+def test_residual_deterministic(cuda_device, M, N, K, split, bn):
+    """TI_EPI_RESIDUAL_DET: the K slices are summed in a fixed order on a cluster before one
+    add per element, so two runs give bit-identical x, within the residual tolerance of the
+    float32 reference."""
+    from tiny_infra_b200 import _native as N_
+    a, b = _operands(M + K, M, N, K, wstd=0.02)
+    x0 = np.random.default_rng(6).standard_normal((M, N)).astype(np.float32)
+    outs = []
+    for _ in range(2):
+        x = torch.from_numpy(x0).cuda()
+        _gemm(N_.TI_EPI_RESIDUAL_DET, _dev(a), _dev(b), M, N, K, out=x, ldo=N, block_n=bn,
+              split_k=split)
+        outs.append(x.cpu().numpy())
+    ref = x0 + a @ b.T
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    assert np.abs(outs[0] - ref).max() <= 1e-4 * rms + 1e-6
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("bn,split", [(64, 2), (64, 4), (64, 8), (128, 2), (128, 4), (128, 8)])
 def test_cluster_split_k_store_and_swiglu(cuda_device, bn, split):
     """STORE (+bias) and SwiGLU epilogues on split-K tiles reduced through distributed shared

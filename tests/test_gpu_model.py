@@ -31,6 +31,7 @@ def _setup(num_layers, vocab=151936, seed=0, max_batch=4, max_seq=256, tied=True
     cfg = QwenConfig(num_layers=num_layers, vocab_size=vocab)
     sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=seed, tied=tied)
     model = Qwen2ForCausalLM(cfg).load_reference_state_dict(sd)
+    model.deterministic = True          # parity runs: bit-reproducible residual reductions
     kv = KVCacheManager(max_batch, max_seq, num_layers, cfg.num_key_value_heads, cfg.head_dim)
     W = {k: v.float().cpu().numpy() for k, v in sd.items()}
     if tied:
@@ -183,7 +184,8 @@ def test_engine_greedy_64_tokens(cuda_device):
     graph-captured DecodeEngine, teacher-forced: the oracle is fed the engine's tokens, so all
     4 x 64 greedy decisions are compared.  A decision may differ only where the oracle's own
     top-2 margin is below twice its logit noise floor (a near-tie that bf16 storage cannot
-    resolve); block tables and seq_len must match exactly throughout."""
+    resolve), and at most 2 of the 256 may; block tables and seq_len must match exactly
+    throughout."""
     from tiny_infra_b200.engine import DecodeEngine
     model, kv, W, ocfg, ocache = _setup(24, max_batch=4, max_seq=160)
     eng = DecodeEngine(model, kv)
@@ -222,6 +224,7 @@ def test_engine_greedy_64_tokens(cuda_device):
     print(f"greedy decisions {decisions}, identical {decisions - len(near_tie_mismatch)}, "
           f"near-tie differences {near_tie_mismatch} (tau {tau:.3g})")
     assert decisions == 256
+    assert len(near_tie_mismatch) <= 2, near_tie_mismatch
 
 
 def test_load_qwen_reference_checkpoint(cuda_device, tmp_path):

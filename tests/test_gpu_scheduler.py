@@ -3,7 +3,8 @@ packed prefill, graph-captured decode, device sampling.
 
 * greedy requests: every generated token is checked against the oracle (oracle.model, fp32 with
   bf16 storage points), teacher-forced per request; a token may differ only where the oracle's
-  own top-2 margin is below 0.05 (a near-tie bf16 storage cannot resolve);
+  own top-2 margin is below 0.05 (a near-tie bf16 storage cannot resolve), and at most one of
+  the 18 tokens may;
 * top-p 1e-6 with temperature 0.8 keeps only the first token of the descending order (ties:
   lowest index), i.e. the argmax, so it reproduces the greedy tokens (top_k = 1 would not: it
   keeps every value tied with the maximum, as the reference does);
@@ -30,7 +31,9 @@ def _model():
     from tiny_infra_b200.qwen2 import Qwen2ForCausalLM
     cfg = QwenConfig(num_layers=LAYERS, vocab_size=VOCAB)
     sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=3, tied=True)
-    return cfg, sd, Qwen2ForCausalLM(cfg).load_reference_state_dict(sd)
+    model = Qwen2ForCausalLM(cfg).load_reference_state_dict(sd)
+    model.deterministic = True          # parity runs: bit-reproducible residual reductions
+    return cfg, sd, model
 
 
 def _run(model, cfg, prompts, chunk=None, **kw):
@@ -81,6 +84,7 @@ def test_batcher_greedy_matches_oracle(cuda_device, chunk):
                 near.append(i)
             inp = np.array([[tok]])
     print("near-tie differences:", near)
+    assert len(near) <= 1, near
 
 
 def test_batcher_tiny_top_p_is_greedy(cuda_device):

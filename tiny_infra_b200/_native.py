@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
 
 TI_EPI_STORE, TI_EPI_SWIGLU, TI_EPI_RESIDUAL, TI_EPI_ARGMAX = 0, 1, 2, 3
 TI_EPI_SWIGLU16 = 5
+TI_EPI_RESIDUAL_DET = 6
 # device status bits (ti_device_status)
 TI_DEVERR_ATTN_WAIT, TI_DEVERR_GEMM_WAIT, TI_DEVERR_PREFILL_WAIT, TI_DEVERR_ATTN_PLAN = 1, 2, 4, 8
 
@@ -111,16 +112,22 @@ def device_status(clear: bool = True, device: torch.device | None = None) -> int
 
 
 class Workspace:
-    """Per-device, zero-initialised scratch buffer that grows on demand (kernels that use
-    arrival counters leave them at zero, so the buffer is reusable across launches)."""
+    """Zero-initialised scratch buffer per device -- and per stream when ``get`` is given one --
+    that grows on demand (kernels that use arrival counters leave them at zero, so a buffer is
+    reusable by every later launch on its stream).  Launches on different streams get different
+    buffers, so they may overlap on the GPU; a buffer is created on its own stream, so its
+    zero fill is ordered before that stream's first launch."""
 
     def __init__(self) -> None:
-        self._buf: dict[int, torch.Tensor] = {}
+        self._buf: dict[tuple, torch.Tensor] = {}
+        self._lock = threading.Lock()
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+    def get(self, device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
         idx = device.index if device.index is not None else torch.cuda.current_device()
-        buf = self._buf.get(idx)
-        if buf is None or buf.numel() < nbytes:
-            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            self._buf[idx] = buf
+        key = (idx, stream)
+        with self._lock:
+            buf = self._buf.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self._buf[key] = buf
         return buf

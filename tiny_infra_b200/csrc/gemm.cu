@@ -12,7 +12,9 @@
 //                    width that is a multiple of 16 pairs them: decode batches take 80- or
 //                    144-wide tiles that fill the SMs in one wave
 //   TI_EPI_RESIDUAL  x_f32 += D                              o_proj / down_proj + residual add
-//                    (models/qwen_25.py:182,191), one red.add per element
+//                    (models/qwen_25.py:182,191), one red.add per element and K slice
+//   TI_EPI_RESIDUAL_DET  the same with the K slices summed in a fixed order on a cluster
+//                    first (one add per element: x is bit-reproducible)
 //   TI_EPI_ARGMAX    per-row (max, first argmax) of each N tile, logits optionally stored
 //                    (greedy decoding without writing [M, vocab] logits)
 //   TI_EPI_QKV_ROPE  bias + RoPE on q and k, q stored, k and v written into the paged pool
@@ -28,7 +30,8 @@
 //             previous kernel.  Then the epilogue: tcgen05.ld from the TMEM lanes of their
 //             quadrant (warp w reads rows
 //             32*(w%4)..+31).  Split-K: for the residual every K slice red.adds its partial
-//             tile into x; for the other epilogues (nonlinear in the sum) the slices run on a
+//             tile into x (or, deterministic, runs on a cluster as below); for the other
+//             epilogues (nonlinear in the sum) the slices run on a
 //             cluster of CL CTAs, each parks its partial tile in shared memory and finishes
 //             128/CL rows by summing the cluster's partials through distributed shared memory
 //             in a fixed order.  The finished tile is staged in shared memory (swizzled rows) and
@@ -548,7 +551,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     }
   }
   if constexpr (CL > 1) {
-    static_assert(KIND != TI_EPI_RESIDUAL, "the residual splits K without a cluster");
     cluster_sync();   // every partial tile of the cluster is in shared memory
     if (warp >= 2) {
       float lo[C::kW], hi[C::kW];
@@ -891,12 +893,14 @@ constexpr int kMaxResidualSplit = 16;
 // Launch with the largest cluster size <= `cl` whose clusters for all `tiles` output tiles are
 // resident at once (a second wave would double the time) and that leaves at least two K blocks
 // per split.
-template <typename T, int BN, int STAGES, int KIND>
+// DET (residual only): split K over a cluster and sum the slices in a fixed order instead of
+// letting every slice red.add on its own, so that `x` is bit-reproducible.
+template <typename T, int BN, int STAGES, int KIND, bool DET = false>
 static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                        const EpiArgs& e, cudaStream_t s) {
   if constexpr (KIND == TI_EPI_ARGMAX) {   // argmax tiles are never split
     return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
-  } else if constexpr (KIND == TI_EPI_RESIDUAL) {
+  } else if constexpr (KIND == TI_EPI_RESIDUAL && !DET) {
     // The residual is linear: every K slice adds its partial tile into x on its own (red.add),
     // no cluster needed.  At most `cl` slices, at least two K blocks each, one wave.
     const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
@@ -930,17 +934,17 @@ static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int
 // so two CTAs share an SM and one's epilogue runs under the other's main loop (measured at 4096
 // tokens: gate/up 780 -> 933 TFLOP/s; at 256 tokens the deep rings are 5 % faster per step).
 constexpr int kDeepRingMaxM = 256;
-template <typename T, int KIND>
+template <typename T, int KIND, bool DET = false>
 static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
                        int K, const EpiArgs& e, cudaStream_t s) {
   const bool deep = M <= kDeepRingMaxM;
   switch (bn) {
     case 64:
-      return deep ? dispatch_cl<T, 64, TI_GEMM_STAGES_64, KIND>(cl, am, bm, M, N, K, e, s)
-                  : dispatch_cl<T, 64, 4, KIND>(cl, am, bm, M, N, K, e, s);
+      return deep ? dispatch_cl<T, 64, TI_GEMM_STAGES_64, KIND, DET>(cl, am, bm, M, N, K, e, s)
+                  : dispatch_cl<T, 64, 4, KIND, DET>(cl, am, bm, M, N, K, e, s);
     case 128:
-      return deep ? dispatch_cl<T, 128, TI_GEMM_STAGES_128, KIND>(cl, am, bm, M, N, K, e, s)
-                  : dispatch_cl<T, 128, 3, KIND>(cl, am, bm, M, N, K, e, s);
+      return deep ? dispatch_cl<T, 128, TI_GEMM_STAGES_128, KIND, DET>(cl, am, bm, M, N, K, e, s)
+                  : dispatch_cl<T, 128, 3, KIND, DET>(cl, am, bm, M, N, K, e, s);
     case 256:   // never split
       return deep ? launch_t<T, 256, TI_GEMM_STAGES_256, KIND, 1>(am, bm, M, N, K, e, s)
                   : launch_t<T, 256, 2, KIND, 1>(am, bm, M, N, K, e, s);
@@ -1070,6 +1074,8 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
     case TI_EPI_STORE: return gemm::dispatch_bn<T, TI_EPI_STORE>(block_n, cl, am, bm, M, N, K, e, s); \
     case TI_EPI_SWIGLU: return gemm::dispatch_bn<T, TI_EPI_SWIGLU>(block_n, cl, am, bm, M, N, K, e, s); \
     case TI_EPI_RESIDUAL: return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, cl, am, bm, M, N, K, e, s); \
+    case TI_EPI_RESIDUAL_DET:                                                                 \
+      return gemm::dispatch_bn<T, TI_EPI_RESIDUAL, true>(block_n, cl, am, bm, M, N, K, e, s);   \
     case TI_EPI_ARGMAX: return gemm::dispatch_bn<T, TI_EPI_ARGMAX>(block_n, 1, am, bm, M, N, K, e, s); \
     case TI_EPI_SWIGLU16: return gemm::launch_swiglu16<T>(block_n, am, bm, M, N, K, e, s);   \
     default: return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue");             \

@@ -5,6 +5,9 @@
 writes ``out`` in place, like the reference; it runs the sm_100a split-K kernel of
 ``csrc/paged_attention.cu`` on the current CUDA stream and accepts fp16 (the reference's
 dtype) and bf16.  Argument errors raise ``RuntimeError`` as the reference's TORCH_CHECKs do.
+
+Its split-K scratch is kept per (device, stream): calls on different streams may run at the
+same time, as calls of the reference op (which keeps no state) may.
 """
 from __future__ import annotations
 
@@ -55,10 +58,11 @@ def launch_paged_attention(out: torch.Tensor, q: torch.Tensor, k_cache: torch.Te
     max_blocks = block_tables.shape[1]
     lib = N.lib()
     need = lib.ti_paged_attention_workspace_bytes(B, NH, KVH, D, max_blocks, partition_blocks)
-    ws = _ws.get(q.device, need)
+    stream = N.stream_of(q)
+    ws = _ws.get(q.device, need, stream)       # one split-K scratch per (device, stream)
     N.check(lib.ti_paged_attention_decode(
         out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), k_cache.data_ptr(),
         v_cache.data_ptr(), NB, block_tables.data_ptr(), block_tables.stride(0),
         row_index.data_ptr() if row_index is not None else None, context_lens.data_ptr(), B, NH,
         KVH, D, block_size, max_blocks, N.dtype_code(q.dtype), partition_blocks, ws.data_ptr(),
-        ws.numel(), N.stream_of(q)))
+        ws.numel(), stream))

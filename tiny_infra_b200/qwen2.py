@@ -69,6 +69,10 @@ class Qwen2ForCausalLM:
         self._plan_ws = N.Workspace()
         self._bufs: dict[str, torch.Tensor] = {}
         self.tied = False
+        # True: the residual projections sum their K slices in a fixed order (bit-reproducible
+        # hidden states and greedy streams, ~13 % slower decode steps); False: every K slice
+        # adds into the residual stream on its own (fastest; the last bits vary between runs).
+        self.deterministic = False
 
     # ---- weights -------------------------------------------------------------------------
     def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
@@ -231,7 +235,8 @@ class Qwen2ForCausalLM:
     def _layers(self, pb: PackedBatch, kv_cache, cos: torch.Tensor, sin: torch.Tensor,
                 hidden: torch.Tensor, stream: int, num_layers: int | None = None,
                 bufs: dict | None = None, ws: torch.Tensor | None = None,
-                plan: torch.Tensor | None = None) -> None:
+                plan: torch.Tensor | None = None,
+                layer_out: list | None = None) -> None:
         c, W, lib = self.config, self.weights, N.lib()
         dt = N.dtype_code(self.dtype)
         T, H, D = pb.num_tokens, c.hidden_size, c.head_dim
@@ -255,6 +260,7 @@ class Qwen2ForCausalLM:
                 pb.num_seqs, NH, KVH, D, maxb, nb, plan.data_ptr(), plan.numel(), stream))
         split_o = self._splits(NH * D)
         split_d = self._splits(I)
+        residual = N.TI_EPI_RESIDUAL_DET if self.deterministic else N.TI_EPI_RESIDUAL
         for li in range(c.num_layers if num_layers is None else num_layers):
             kc, vc = kv_cache.key_cache[li], kv_cache.value_cache[li]
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
@@ -276,7 +282,7 @@ class Qwen2ForCausalLM:
                     bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.start_pos.data_ptr(),
                     pb.cu_seqlens.data_ptr(), pb.tile_seq.data_ptr(), pb.tile_q0.data_ptr(),
                     pb.tile_seq.numel(), NH, KVH, D, kv_cache.block_size, dt, stream))
-            N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
+            N.check(lib.ti_gemm(residual, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
                                 NH * D, T, H, NH * D, hidden.data_ptr(), H, None, None, None, dt,
                                 O_TILE, split_o, stream))
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
@@ -284,9 +290,11 @@ class Qwen2ForCausalLM:
             N.check(lib.ti_gemm(N.TI_EPI_SWIGLU16, xn.data_ptr(), H,
                                 W[f"{li}.gate_up"].data_ptr(), H, T, 2 * I, H, act.data_ptr(), I,
                                 None, None, None, dt, 0, 1, stream))
-            N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
+            N.check(lib.ti_gemm(residual, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
                                 I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
                                 DOWN_TILE, split_d, stream))
+            if layer_out is not None:       # the residual stream after this layer (a copy)
+                layer_out.append(hidden.clone())
 
     def _final_norm(self, hidden_rows: torch.Tensor, stream: int) -> torch.Tensor:
         c = self.config
@@ -308,16 +316,18 @@ class Qwen2ForCausalLM:
         return logits
 
     def forward_packed(self, pb: PackedBatch, kv_cache, cos, sin, *, rows: str = "all",
-                       num_layers: int | None = None, return_hidden: bool = False):
+                       num_layers: int | None = None, return_hidden: bool = False,
+                       layer_out: list | None = None):
         """Run the layers over a packed batch; returns logits of every token (rows='all') or of
-        each sequence's last token (rows='last')."""
+        each sequence's last token (rows='last').  ``layer_out`` (a list) receives a copy of the
+        float32 residual stream after every layer."""
         c = self.config
         stream = torch.cuda.current_stream(self.device).cuda_stream
         hidden = torch.empty(pb.num_tokens, c.hidden_size, dtype=torch.float32, device=self.device)
         N.check(N.lib().ti_embedding(hidden.data_ptr(), self.weights["embed"].data_ptr(),
                                      pb.input_ids.data_ptr(), pb.num_tokens, c.hidden_size,
                                      c.vocab_size, N.dtype_code(self.dtype), stream))
-        self._layers(pb, kv_cache, cos, sin, hidden, stream, num_layers)
+        self._layers(pb, kv_cache, cos, sin, hidden, stream, num_layers, layer_out=layer_out)
         if return_hidden:
             return hidden
         h = hidden if rows == "all" else hidden.index_select(0, pb.last_rows).contiguous()
