@@ -167,9 +167,15 @@ def swiglu(x: np.ndarray) -> np.ndarray:
 # ---------------------------------------------------------------------------------------------
 # RMSNorm -- models/qwen_25.py:24-36
 # ---------------------------------------------------------------------------------------------
-def rmsnorm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-6) -> np.ndarray:
-    """w * (x * rsqrt(mean(x^2) + eps)) computed in float32 (models/qwen_25.py:30-36)."""
+def rmsnorm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-6, round_fn=None) -> np.ndarray:
+    """w * (x * rsqrt(mean(x^2) + eps)) computed in float32 (models/qwen_25.py:30-36).
+
+    ``round_fn`` (optional) rounds the normalised row to the model dtype before the weight
+    multiply, as the reference's ``weight * hidden_states.to(input_dtype)`` does (:36)."""
     xf = x.astype(np.float32)
     var = np.mean(xf * xf, axis=-1, keepdims=True)
     rstd = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
-    return weight.astype(np.float32) * (xf * rstd)
+    xhat = xf * rstd
+    if round_fn is not None:
+        xhat = round_fn(xhat)
+    return weight.astype(np.float32) * xhat

@@ -67,6 +67,93 @@ def init_weights(cfg: OracleConfig, seed: int = 0, std: float = 0.02, tied: bool
     return W
 
 
+STAGES = ("xn1", "q", "k", "v", "attn", "h_mid", "xn2", "act", "h_out")
+
+
+def decoder_layer(W: dict, cfg: OracleConfig, li: int, h: np.ndarray, pos: np.ndarray,
+                  batch_indices: np.ndarray, cache: OracleKVCache, cos: np.ndarray,
+                  sin: np.ndarray, *, device_rounding: str | None = None,
+                  chunked_prefill: bool = False, record: dict | None = None,
+                  given: dict | None = None) -> np.ndarray:
+    """One ``Qwen2DecoderLayer`` (models/qwen_25.py:161-192 with Qwen2Attention :51-131 and
+    Qwen2MLP :140-151) on the float32 residual stream h [B, S, H]; returns the new stream.
+
+    The stages, named as in :data:`STAGES`: ``xn1`` (input RMSNorm), ``q`` / ``k`` / ``v``
+    (projections + bias, RoPE on q and k, [B, S, heads, D]), ``attn`` ([B, S, H]), ``h_mid``
+    (stream after the attention residual), ``xn2`` (post-attention RMSNorm), ``act`` (SwiGLU
+    output [B, S, I]) and ``h_out``.  ``record`` (a dict) receives every stage's value as
+    computed here; ``given`` (a dict) then replaces the named stages by the caller's values, so
+    that each later stage is computed from them -- with another implementation's stored tensors,
+    ``record`` holds what each of its stages should have produced from its own inputs.
+    """
+    rd = (lambda x: round_to(x, device_rounding))
+    given = given or {}
+    B, S = h.shape[:2]
+    D = cfg.head_dim
+    NH, KVH = cfg.num_attention_heads, cfg.num_key_value_heads
+    eps = cfg.rms_norm_eps
+    p = f"model.layers.{li}"
+
+    def stage(name, value):
+        if record is not None:
+            record[name] = np.array(value, np.float32, copy=True)
+        if name in given:
+            value = np.asarray(given[name], np.float32).reshape(np.shape(value))
+        return value
+
+    res = h
+    x = stage("xn1", rd(kernels.rmsnorm(h, W[f"{p}.input_layernorm.weight"], eps,
+                                        round_fn=rd if device_rounding else None)))
+    q = x @ W[f"{p}.self_attn.q_proj.weight"].T + W[f"{p}.self_attn.q_proj.bias"]
+    k = x @ W[f"{p}.self_attn.k_proj.weight"].T + W[f"{p}.self_attn.k_proj.bias"]
+    v = x @ W[f"{p}.self_attn.v_proj.weight"].T + W[f"{p}.self_attn.v_proj.bias"]
+    q = q.reshape(B, S, NH, D).astype(np.float32)
+    k = k.reshape(B, S, KVH, D).astype(np.float32)
+    v = v.reshape(B, S, KVH, D).astype(np.float32)
+    q3 = q.reshape(B * S, NH, D)
+    k3 = k.reshape(B * S, KVH, D)
+    kernels.rope_inplace(q3, k3, cos, sin, pos.reshape(-1))              # :79
+    q = stage("q", rd(q3.reshape(B, S, NH, D)))
+    k = stage("k", rd(k3.reshape(B, S, KVH, D)))
+    v = stage("v", rd(v))
+    cache.allocate_and_insert(li, batch_indices, k.transpose(0, 2, 1, 3),   # :82-87
+                              v.transpose(0, 2, 1, 3))
+    if S > 1 and not chunked_prefill:
+        attn = kernels.causal_self_attention(q, k, v)                       # :89-104
+    elif S > 1:
+        attn = np.stack([kernels.paged_prefill_attention(
+            q[i], cache.key_cache[li], cache.value_cache[li],
+            cache.block_tables[b], int(cache.seq_len[b]), cache.block_size)
+            for i, b in enumerate(batch_indices.tolist())])
+    else:
+        bt = cache.block_tables[batch_indices]                              # :114
+        ctx = cache.seq_len[batch_indices] + S                              # :115
+        out = np.zeros((B, NH, D), np.float32)
+        kernels.paged_attention(out, q[:, 0], cache.key_cache[li], cache.value_cache[li],
+                                bt, ctx, cache.block_size)                  # :117-125
+        attn = out[:, None]
+    attn = stage("attn", rd(attn.reshape(B, S, NH * D)))
+    h = stage("h_mid", attn @ W[f"{p}.self_attn.o_proj.weight"].T + res)  # :130, :182
+    res = h
+    x = stage("xn2", rd(kernels.rmsnorm(h, W[f"{p}.post_attention_layernorm.weight"], eps,
+                                        round_fn=rd if device_rounding else None)))
+    g = x @ W[f"{p}.mlp.gate_proj.weight"].T
+    u = x @ W[f"{p}.mlp.up_proj.weight"].T
+    a = stage("act", rd(kernels.swiglu(np.concatenate([g, u], axis=-1))))  # :146-148
+    return stage("h_out", a @ W[f"{p}.mlp.down_proj.weight"].T + res)     # :151, :191
+
+
+def embed(W: dict, input_ids: np.ndarray) -> np.ndarray:
+    """models/qwen_25.py:224: the float32 residual stream's starting value."""
+    return W["model.embed_tokens.weight"][input_ids].astype(np.float32)
+
+
+def positions(cache: OracleKVCache, batch_indices: np.ndarray, S: int) -> np.ndarray:
+    """models/qwen_25.py:218-222: positions of the call's tokens, from seq_len."""
+    start = cache.seq_len[np.asarray(batch_indices).reshape(-1)].astype(np.int64)
+    return np.arange(S)[None, :] + start[:, None]
+
+
 def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np.ndarray,
             cache: OracleKVCache, cos: np.ndarray, sin: np.ndarray, *,
             device_rounding: str | None = None, last_only: bool = False,
@@ -79,8 +166,9 @@ def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np
     forward, engine/scheduler.py:234,266).
 
     ``device_rounding='bf16'`` rounds to bf16 at the points where the CUDA path stores bf16
-    (normed activations, q/k/v after RoPE and the KV pool, attention output, SwiGLU output);
-    the residual stream and the logits stay float32 as on the device.  ``None`` is pure fp32.
+    (normed activations -- also before the RMSNorm weight multiply, as the reference rounds
+    them -- q/k/v after RoPE and the KV pool, attention output, SwiGLU output); the residual
+    stream and the logits stay float32 as on the device.  ``None`` is pure fp32.
 
     ``chunked_prefill`` makes S>1 calls attend over the paged pool (earlier tokens of the
     sequence included) instead of the reference's self-only SDPA; both agree when the call
@@ -91,57 +179,18 @@ def forward(W: dict, cfg: OracleConfig, input_ids: np.ndarray, batch_indices: np
     """
     rd = (lambda x: round_to(x, device_rounding))
     B, S = input_ids.shape
-    H, D = cfg.hidden_size, cfg.head_dim
-    NH, KVH = cfg.num_attention_heads, cfg.num_key_value_heads
     eps = cfg.rms_norm_eps
     batch_indices = np.asarray(batch_indices).reshape(-1)
-    start = cache.seq_len[batch_indices].astype(np.int64)                    # :218
-    pos = np.arange(S)[None, :] + start[:, None]                               # :221-222
-    h = W["model.embed_tokens.weight"][input_ids].astype(np.float32)          # :224
+    pos = positions(cache, batch_indices, S)
+    h = embed(W, input_ids)
     for li in range(cfg.num_layers):
-        p = f"model.layers.{li}"
-        res = h
-        x = rd(kernels.rmsnorm(h, W[f"{p}.input_layernorm.weight"], eps))
-        q = x @ W[f"{p}.self_attn.q_proj.weight"].T + W[f"{p}.self_attn.q_proj.bias"]
-        k = x @ W[f"{p}.self_attn.k_proj.weight"].T + W[f"{p}.self_attn.k_proj.bias"]
-        v = x @ W[f"{p}.self_attn.v_proj.weight"].T + W[f"{p}.self_attn.v_proj.bias"]
-        q = q.reshape(B, S, NH, D).astype(np.float32)
-        k = k.reshape(B, S, KVH, D).astype(np.float32)
-        v = v.reshape(B, S, KVH, D).astype(np.float32)
-        q3 = q.reshape(B * S, NH, D)
-        k3 = k.reshape(B * S, KVH, D)
-        kernels.rope_inplace(q3, k3, cos, sin, pos.reshape(-1))              # :79
-        q = rd(q3.reshape(B, S, NH, D))
-        k = rd(k3.reshape(B, S, KVH, D))
-        v = rd(v)
-        cache.allocate_and_insert(li, batch_indices, k.transpose(0, 2, 1, 3),   # :82-87
-                                  v.transpose(0, 2, 1, 3))
-        if S > 1 and not chunked_prefill:
-            attn = kernels.causal_self_attention(q, k, v)                       # :89-104
-        elif S > 1:
-            attn = np.stack([kernels.paged_prefill_attention(
-                q[i], cache.key_cache[li], cache.value_cache[li],
-                cache.block_tables[b], int(cache.seq_len[b]), cache.block_size)
-                for i, b in enumerate(batch_indices.tolist())])
-        else:
-            bt = cache.block_tables[batch_indices]                              # :114
-            ctx = cache.seq_len[batch_indices] + S                              # :115
-            out = np.zeros((B, NH, D), np.float32)
-            kernels.paged_attention(out, q[:, 0], cache.key_cache[li], cache.value_cache[li],
-                                    bt, ctx, cache.block_size)                  # :117-125
-            attn = out[:, None]
-        attn = rd(attn.reshape(B, S, H))
-        h = attn @ W[f"{p}.self_attn.o_proj.weight"].T + res                  # :130, :182
-        res = h
-        x = rd(kernels.rmsnorm(h, W[f"{p}.post_attention_layernorm.weight"], eps))
-        g = x @ W[f"{p}.mlp.gate_proj.weight"].T
-        u = x @ W[f"{p}.mlp.up_proj.weight"].T
-        a = rd(kernels.swiglu(np.concatenate([g, u], axis=-1)))                # :146-148
-        h = a @ W[f"{p}.mlp.down_proj.weight"].T + res                        # :151, :191
+        h = decoder_layer(W, cfg, li, h, pos, batch_indices, cache, cos, sin,
+                          device_rounding=device_rounding, chunked_prefill=chunked_prefill)
         if layer_hook is not None:
             layer_hook(li, h)
     if last_only:
         h = h[:, -1:]
-    h = kernels.rmsnorm(h, W["model.norm.weight"], eps)                        # :230
+    h = kernels.rmsnorm(h, W["model.norm.weight"], eps,                       # :230
+                        round_fn=rd if device_rounding else None)
     h = rd(h)
     return (h @ W["lm_head.weight"].T).astype(np.float32)                     # :250

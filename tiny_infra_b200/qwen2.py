@@ -235,8 +235,12 @@ class Qwen2ForCausalLM:
     def _layers(self, pb: PackedBatch, kv_cache, cos: torch.Tensor, sin: torch.Tensor,
                 hidden: torch.Tensor, stream: int, num_layers: int | None = None,
                 bufs: dict | None = None, ws: torch.Tensor | None = None,
-                plan: torch.Tensor | None = None,
-                layer_out: list | None = None) -> None:
+                plan: torch.Tensor | None = None, first_layer: int = 0,
+                trace=None) -> None:
+        """Layers first_layer .. num_layers-1 over the packed batch, in place on ``hidden``.
+        ``trace(layer, stage, bufs)`` (optional) is called after each stage's kernel is issued
+        (stages xn1, qkv, attn, h_mid, xn2, act, h_out; ``bufs`` holds xn / qkv / attn / act
+        and the stream ``hidden``), e.g. to copy intermediate tensors for a parity check."""
         c, W, lib = self.config, self.weights, N.lib()
         dt = N.dtype_code(self.dtype)
         T, H, D = pb.num_tokens, c.hidden_size, c.head_dim
@@ -261,15 +265,23 @@ class Qwen2ForCausalLM:
         split_o = self._splits(NH * D)
         split_d = self._splits(I)
         residual = N.TI_EPI_RESIDUAL_DET if self.deterministic else N.TI_EPI_RESIDUAL
-        for li in range(c.num_layers if num_layers is None else num_layers):
+        tb = dict(bufs, hidden=hidden)
+
+        def mark(li, stage):
+            if trace is not None:
+                trace(li, stage, tb)
+
+        for li in range(first_layer, c.num_layers if num_layers is None else num_layers):
             kc, vc = kv_cache.key_cache[li], kv_cache.value_cache[li]
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
                                    W[f"{li}.ln1"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
+            mark(li, "xn1")
             N.check(lib.ti_gemm_qkv_rope(
                 xn.data_ptr(), H, W[f"{li}.qkv"].data_ptr(), H, W[f"{li}.qkv_bias"].data_ptr(),
                 T, H, NH, KVH, D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(),
                 pb.slot_mapping.data_ptr(), cos.data_ptr(), sin.data_ptr(),
                 pb.positions.data_ptr(), kv_cache.block_size, dt, stream))
+            mark(li, "qkv")
             if pb.decode:
                 N.check(lib.ti_paged_attention_decode_planned(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
@@ -282,19 +294,22 @@ class Qwen2ForCausalLM:
                     bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.start_pos.data_ptr(),
                     pb.cu_seqlens.data_ptr(), pb.tile_seq.data_ptr(), pb.tile_q0.data_ptr(),
                     pb.tile_seq.numel(), NH, KVH, D, kv_cache.block_size, dt, stream))
+            mark(li, "attn")
             N.check(lib.ti_gemm(residual, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
                                 NH * D, T, H, NH * D, hidden.data_ptr(), H, None, None, None, dt,
                                 O_TILE, split_o, stream))
+            mark(li, "h_mid")
             N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
                                    W[f"{li}.ln2"].data_ptr(), c.rms_norm_eps, T, H, dt, stream))
+            mark(li, "xn2")
             N.check(lib.ti_gemm(N.TI_EPI_SWIGLU16, xn.data_ptr(), H,
                                 W[f"{li}.gate_up"].data_ptr(), H, T, 2 * I, H, act.data_ptr(), I,
                                 None, None, None, dt, 0, 1, stream))
+            mark(li, "act")
             N.check(lib.ti_gemm(residual, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
                                 I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
                                 DOWN_TILE, split_d, stream))
-            if layer_out is not None:       # the residual stream after this layer (a copy)
-                layer_out.append(hidden.clone())
+            mark(li, "h_out")
 
     def _final_norm(self, hidden_rows: torch.Tensor, stream: int) -> torch.Tensor:
         c = self.config
@@ -317,17 +332,23 @@ class Qwen2ForCausalLM:
 
     def forward_packed(self, pb: PackedBatch, kv_cache, cos, sin, *, rows: str = "all",
                        num_layers: int | None = None, return_hidden: bool = False,
-                       layer_out: list | None = None):
+                       first_layer: int = 0, hidden_in: torch.Tensor | None = None, trace=None):
         """Run the layers over a packed batch; returns logits of every token (rows='all') or of
-        each sequence's last token (rows='last').  ``layer_out`` (a list) receives a copy of the
-        float32 residual stream after every layer."""
+        each sequence's last token (rows='last').  ``hidden_in`` (float32 [T, H]) starts the
+        residual stream at layer ``first_layer`` instead of the embedding at layer 0; ``trace``
+        is passed to every layer (see ``_layers``)."""
         c = self.config
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        hidden = torch.empty(pb.num_tokens, c.hidden_size, dtype=torch.float32, device=self.device)
-        N.check(N.lib().ti_embedding(hidden.data_ptr(), self.weights["embed"].data_ptr(),
-                                     pb.input_ids.data_ptr(), pb.num_tokens, c.hidden_size,
-                                     c.vocab_size, N.dtype_code(self.dtype), stream))
-        self._layers(pb, kv_cache, cos, sin, hidden, stream, num_layers, layer_out=layer_out)
+        if hidden_in is not None:
+            hidden = hidden_in.to(self.device, torch.float32).contiguous().clone()
+        else:
+            hidden = torch.empty(pb.num_tokens, c.hidden_size, dtype=torch.float32,
+                                 device=self.device)
+            N.check(N.lib().ti_embedding(hidden.data_ptr(), self.weights["embed"].data_ptr(),
+                                         pb.input_ids.data_ptr(), pb.num_tokens, c.hidden_size,
+                                         c.vocab_size, N.dtype_code(self.dtype), stream))
+        self._layers(pb, kv_cache, cos, sin, hidden, stream, num_layers, first_layer=first_layer,
+                     trace=trace)
         if return_hidden:
             return hidden
         h = hidden if rows == "all" else hidden.index_select(0, pb.last_rows).contiguous()
