@@ -103,9 +103,9 @@ def _oracle_hidden(W, cfg, ids, slots, cache, cos, sin):
     hid = {}
     orig = OK.rmsnorm
 
-    def capture(x, w, eps=1e-6):
+    def capture(x, w, eps=1e-6, round_fn=None):
         hid["h"] = np.array(x, copy=True)
-        return orig(x, w, eps)
+        return orig(x, w, eps, round_fn=round_fn)
 
     OK.rmsnorm = capture
     try:

@@ -163,7 +163,12 @@ def test_layer_outputs_config3(full_model, cuda_device):
         for st in BF16_STAGES:
             g, r = got[st].reshape(-1), sub[st].reshape(-1)
             d = np.abs(g - r)
-            assert np.all(d <= _bf16_ulp(r) * 1.0001), (li, st, float(d.max()))
+            # one bf16 step at the larger of the two values, plus the float32 error of a value
+            # that a sum produced by cancellation (relative to the stage's rms)
+            rms = float(np.sqrt(np.mean(r.astype(np.float64) ** 2)))
+            tol = _bf16_ulp(np.maximum(np.abs(g), np.abs(r))) * 1.0001 + 1e-5 * rms
+            bad = np.nonzero(d > tol)[0]
+            assert len(bad) == 0, (li, st, [(int(i), float(g[i]), float(r[i])) for i in bad[:8]])
             row[f"{st}_flips"] = int((d > 0).sum())
             assert row[f"{st}_flips"] <= MAX_FLIP_FRAC * d.size, (li, st, row[f"{st}_flips"])
         for st in F32_STAGES:
