@@ -86,10 +86,7 @@ class DecodeEngine:
             self.ctx_lens.data_ptr(), self.hidden.data_ptr(), m.weights["embed"].data_ptr(),
             c.hidden_size, c.vocab_size, rows, dt, s))
         m._layers(self._batch(rows), kv, self.cos, self.sin, self.hidden[:rows], s,
-                  bufs=self.bufs, ws=self.ws, plan=self.plan)
-        N.check(lib.ti_rmsnorm(self.xf.data_ptr(), self.hidden.data_ptr(), N.TI_DTYPE_FP32,
-                               m.weights["norm"].data_ptr(), c.rms_norm_eps, rows,
-                               c.hidden_size, dt, s))
+                  bufs=self.bufs, ws=self.ws, plan=self.plan, final_norm_out=self.xf[:rows])
         if sampled:
             N.check(lib.ti_gemm(N.TI_EPI_STORE, self.xf.data_ptr(), c.hidden_size,
                                 m.weights["lm_head"].data_ptr(), c.hidden_size, rows,
