@@ -215,19 +215,6 @@ int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb
             int K, void* out, int64_t ldo, const void* bias, float* aux_val, int32_t* aux_idx,
             int dtype, int block_n, int split_k, void* stream);
 
-/* ---- residual projection fused with the RMSNorm that follows it ----------------------------
- * x (float32 [M, N], leading dim ldx) += A[M, K] . B[N, K]^T as ti_gemm's TI_EPI_RESIDUAL
- * (deterministic != 0: TI_EPI_RESIDUAL_DET), then norm_out[M, N] (dtype, leading dim ld_norm)
- * = norm_weight * rmsnorm(x) with the arithmetic of ti_rmsnorm -- the o_proj -> post-attention
- * norm and down_proj -> next input norm pairs of models/qwen_25.py:182-191,24-36 in one launch.
- * The launch's last CTAs to finish normalise the rows once every CTA's additions are in x.
- * `sync`: two zeroed unsigned ints of device memory (4-byte aligned) that every call leaves
- * zero; calls that share them must not overlap on the GPU.  N % 8 == 0, N <= 1024. */
-int ti_gemm_residual_rmsnorm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
-                             int K, float* x, int64_t ldx, int deterministic, int block_n,
-                             int split_k, const void* norm_weight, float eps, void* norm_out,
-                             int64_t ld_norm, unsigned int* sync, int dtype, void* stream);
-
 /* ---- QKV projection fused with RoPE and the KV-append write ----------------------
  * [q | k | v] = A[M, hidden] . W^T + bias, W = the fused [(NH+2*KVH)*64, hidden] q/k/v weight
  * (models/qwen_25.py:46-48,66-68).  RoPE (src/fused_rope.cu:37-50, tables cos/sin float32

@@ -161,42 +161,6 @@ def test_residual_deterministic(cuda_device, M, N, K, split, bn):
     np.testing.assert_array_equal(outs[0], outs[1])
 
 
-@pytest.mark.parametrize("M,K,split,bn,det", [(256, 896, 7, 64, 0), (256, 4864, 16, 128, 0),
-                                              (256, 4864, 16, 128, 1), (32, 896, 7, 64, 1),
-                                              (37, 4864, 16, 128, 0), (300, 896, 7, 64, 1),
-                                              (4096, 4864, 16, 128, 0)])
-def test_residual_rmsnorm(cuda_device, M, K, split, bn, det):
-    """ti_gemm_residual_rmsnorm: x += A W^T as the residual epilogue, then norm_out =
-    w * rmsnorm(x) in the same launch -- bit-identical to ti_rmsnorm of the finished x; two
-    calls in a row on the same counters, which are left at zero."""
-    from tiny_infra_b200 import _native as N_
-    N, lib = 896, N_.lib()
-    a, b = _operands(M * 3 + K, M, N, K, wstd=0.02)
-    x0 = np.random.default_rng(7).standard_normal((M, N)).astype(np.float32)
-    w = _dev(1 + 0.1 * np.random.default_rng(8).standard_normal(N))
-    x = torch.from_numpy(x0).cuda()
-    out = torch.full((M, N), 3.0, dtype=torch.bfloat16, device="cuda")
-    sync = torch.zeros(4, dtype=torch.int32, device="cuda")
-    A, B = _dev(a), _dev(b)
-    s = torch.cuda.current_stream().cuda_stream
-    for call in range(2):
-        N_.check(lib.ti_gemm_residual_rmsnorm(A.data_ptr(), K, B.data_ptr(), K, M, N, K,
-                                              x.data_ptr(), N, det, bn, split, w.data_ptr(), 1e-6,
-                                              out.data_ptr(), N, sync.data_ptr(),
-                                              N_.TI_DTYPE_BF16, s))
-        torch.cuda.synchronize()
-        assert N_.device_status() == 0
-        assert int(sync.abs().sum()) == 0
-        ref = x0 + (call + 1) * (a @ b.T)
-        rms = float(np.sqrt(np.mean(ref ** 2)))
-        assert np.abs(x.cpu().numpy() - ref).max() <= 2e-4 * rms + 1e-6
-        want = torch.empty_like(out)
-        N_.check(lib.ti_rmsnorm(want.data_ptr(), x.data_ptr(), N_.TI_DTYPE_FP32, w.data_ptr(),
-                                1e-6, M, N, N_.TI_DTYPE_BF16, s))
-        torch.cuda.synchronize()
-        assert torch.equal(out, want)
-
-
 @pytest.mark.parametrize("bn,split", [(64, 2), (64, 4), (64, 8), (128, 2), (128, 4), (128, 8)])
 def test_cluster_split_k_store_and_swiglu(cuda_device, bn, split):
     """STORE (+bias) and SwiGLU epilogues on split-K tiles reduced through distributed shared

@@ -42,8 +42,6 @@ SIGNATURES: dict[str, tuple] = {
     "ti_decode_prepare": (I32, [P, P, P, P, P, I64, I32, P, P, P, P, P, I32, I64, I32, I32, P]),
     "ti_argmax_finish": (I32, [P, P, I32, I32, P, P, P, I32, P]),
     "ti_kv_scatter": (I32, [P, P, P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P]),
-    "ti_gemm_residual_rmsnorm": (I32, [P, I64, P, I64, I32, I32, I32, P, I64, I32, I32, I32, P,
-                                       F32, P, I64, P, I32, P]),
     "ti_gemm_qkv_rope": (I32, [P, I64, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P,
                                P, I32, I32, P]),
     "ti_sample": (I32, [P, I64, I32, I32, I32, P, P, P, P, P, P, P, I32, P]),

@@ -81,19 +81,7 @@ struct EpiArgs {
   void* k_cache;
   void* v_cache;
   int num_heads, num_kv_heads, block_size;
-  // residual epilogue + RMSNorm of the finished stream (ti_gemm_residual_rmsnorm): norm_out
-  // (leading dim ld_norm) = norm_w * rmsnorm(x); sync = two zeroed arrival counters
-  const void* norm_w;
-  void* norm_out;
-  int64_t ld_norm;
-  float norm_eps;
-  unsigned int* sync;
 };
-
-// CTAs of a residual launch that normalise the finished rows (the last to arrive): at most this
-// many wait for the others, so the launch's other CTAs always find SMs to run on.
-constexpr int kNormCtas = 64;
-constexpr int kNormMaxChunks = 4;     // row in registers: hidden <= 4 x 256
 
 struct Best {
   float v;
@@ -371,93 +359,6 @@ __device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int
   }
 }
 
-// RMSNorm of one row by one warp, the arithmetic of ti_rmsnorm's row-in-registers kernel
-// (models/qwen_25.py:24-36): lane i holds elements 8i + 256k, sum of squares in that order, a
-// butterfly warp sum, rstd = rsqrt(mean + eps), out = w * dtype(x * rstd) rounded to dtype.
-// x is read from L2 (ld.global.cg): it was just written by other CTAs' red.adds.
-template <typename T>
-__device__ __forceinline__ void norm_row(T* __restrict__ out, const float* x, const T* w, float eps,
-                                         int H, int lane) {
-  float f[kNormMaxChunks][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < kNormMaxChunks; ++k) {
-    const int c = lane * 8 + k * 256;
-    if (c < H) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(x + c));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(x + c + 4));
-      f[k][0] = a.x; f[k][1] = a.y; f[k][2] = a.z; f[k][3] = a.w;
-      f[k][4] = b.x; f[k][5] = b.y; f[k][6] = b.z; f[k][7] = b.w;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += f[k][j] * f[k][j];
-    }
-  }
-  ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / (float)H + eps);
-#pragma unroll
-  for (int k = 0; k < kNormMaxChunks; ++k) {
-    const int c = lane * 8 + k * 256;
-    if (c < H) {
-      const uint4 wr = *reinterpret_cast<const uint4*>(w + c);
-      const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wr);
-      uint32_t o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 wf = Elem<T>::unpack2(wu[i]);
-        o[i] = Elem<T>::pack2(wf.x * Elem<T>::to_f(Elem<T>::from_f(f[k][2 * i] * rstd)),
-                              wf.y * Elem<T>::to_f(Elem<T>::from_f(f[k][2 * i + 1] * rstd)));
-      }
-      *reinterpret_cast<uint4*>(out + c) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
-}
-
-// Residual launches with a norm: run by the 4 epilogue warps of every CTA once its red.adds
-// are issued.  Each CTA fences its adds and takes an arrival ticket; the last kNormCtas to
-// arrive wait (bounded) until all CTAs have arrived, i.e. until x is final, and normalise an
-// equal share of its rows into norm_out.  The last of them to finish clears both counters for
-// the next launch (no CTA reads them after that).
-template <typename T>
-__device__ __forceinline__ void residual_norm_tail(const EpiArgs& e) {
-  __shared__ unsigned int s_ticket;
-  const int t = (int)threadIdx.x - 64;
-  const int lane = t & 31, w = t >> 5;
-  __threadfence();                      // this thread's red.adds before the arrival
-  epilogue_bar();
-  const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-  const unsigned nn = min(total, (unsigned)kNormCtas);
-  if (t == 0) s_ticket = atomicAdd(&e.sync[0], 1u);
-  epilogue_bar();
-  const unsigned ticket = s_ticket;
-  if (ticket + nn < total) return;      // x is finished by others
-  const unsigned slot = ticket - (total - nn);
-  if (t == 0) {
-    const long long t0 = clock64();
-    while (true) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(e.sync) : "memory");
-      if (v >= total) break;
-      if (clock64() - t0 > kWaitCycles) { raise_device_error(TI_DEVERR_GEMM_WAIT); break; }
-      __nanosleep(64);
-    }
-  }
-  epilogue_bar();
-  __threadfence();
-  const int per = (e.M + (int)nn - 1) / (int)nn;
-  const int r0 = (int)slot * per, r1 = min(e.M, r0 + per);
-  const float* x = reinterpret_cast<const float*>(e.out);
-  for (int r = r0 + w; r < r1; r += 4)
-    norm_row<T>(reinterpret_cast<T*>(e.norm_out) + (int64_t)r * e.ld_norm, x + (int64_t)r * e.ldo,
-                reinterpret_cast<const T*>(e.norm_w), e.norm_eps, e.N, lane);
-  epilogue_bar();
-  if (t == 0) {
-    if (atomicAdd(&e.sync[1], 1u) == nn - 1) {   // every normalising CTA is past its wait
-      e.sync[0] = 0u;
-      e.sync[1] = 0u;
-    }
-  }
-}
-
 template <int BN, int STAGES, int CL>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
@@ -687,9 +588,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       store_tile<T, BN, KIND>(e, stage, C::kRows, n0, m0 + (int)rank * C::kRows, ok);
     }
     cluster_sync();   // peers have finished reading this CTA's partial tile
-  }
-  if constexpr (KIND == TI_EPI_RESIDUAL) {
-    if (e.norm_out != nullptr && warp >= 2) residual_norm_tail<T>(e);
   }
   tc_fence_before();
   __syncthreads();
@@ -1113,20 +1011,10 @@ static int launch_swiglu16(int bn, const CUtensorMap& am, const CUtensorMap& bm,
 
 using namespace ti;
 
-namespace {
-struct NormSpec {          // the RMSNorm that follows a residual GEMM (null norm_out: none)
-  const void* w = nullptr;
-  void* out = nullptr;
-  int64_t ld = 0;
-  float eps = 0.f;
-  unsigned int* sync = nullptr;
-};
-}  // namespace
-
-static int gemm_entry(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb, int M,
-                      int N, int K, void* out, int64_t ldo, const void* bias, float* aux_val,
-                      int32_t* aux_idx, int dtype, int block_n, int split_k, void* stream,
-                      const NormSpec& norm) {
+extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
+                       int M, int N, int K, void* out, int64_t ldo, const void* bias,
+                       float* aux_val, int32_t* aux_idx, int dtype, int block_n, int split_k,
+                       void* stream) {
   clear_error();
   if (M == 0) return TI_OK;
   if (!A || !B || M < 0 || N <= 0 || K <= 0)
@@ -1180,8 +1068,6 @@ static int gemm_entry(int epilogue, const void* A, int64_t lda, const void* B, i
   gemm::EpiArgs e{};
   e.out = out; e.ldo = ldo; e.bias = bias; e.aux_val = aux_val; e.aux_idx = aux_idx;
   e.M = M; e.N = N; e.ntiles = N / block_n;
-  e.norm_w = norm.w; e.norm_out = norm.out; e.ld_norm = norm.ld; e.norm_eps = norm.eps;
-  e.sync = norm.sync;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 #define TI_GEMM_KIND(T)                                                                       \
   switch (epilogue) {                                                                         \
@@ -1197,35 +1083,6 @@ static int gemm_entry(int epilogue, const void* A, int64_t lda, const void* B, i
   if (dtype == TI_DTYPE_BF16) { TI_GEMM_KIND(__nv_bfloat16) }
   TI_GEMM_KIND(__half)
 #undef TI_GEMM_KIND
-}
-
-extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
-                       int M, int N, int K, void* out, int64_t ldo, const void* bias,
-                       float* aux_val, int32_t* aux_idx, int dtype, int block_n, int split_k,
-                       void* stream) {
-  return gemm_entry(epilogue, A, lda, B, ldb, M, N, K, out, ldo, bias, aux_val, aux_idx, dtype,
-                    block_n, split_k, stream, NormSpec{});
-}
-
-extern "C" int ti_gemm_residual_rmsnorm(const void* A, int64_t lda, const void* B, int64_t ldb,
-                                        int M, int N, int K, float* x, int64_t ldx,
-                                        int deterministic, int block_n, int split_k,
-                                        const void* norm_weight, float eps, void* norm_out,
-                                        int64_t ld_norm, unsigned int* sync, int dtype,
-                                        void* stream) {
-  clear_error();
-  if (M == 0) return TI_OK;
-  if (!norm_weight || !norm_out || !sync)
-    return set_error(TI_ERR_INVALID_ARGUMENT, "gemm_residual_rmsnorm: null norm weight, output or sync");
-  if (N % 8 || N > gemm::kNormMaxChunks * 256)
-    return set_error(TI_ERR_UNSUPPORTED, "gemm_residual_rmsnorm: hidden must be a multiple of 8, at most 1024");
-  if ((reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(norm_out)) & 15 ||
-      (ld_norm % 8) || (reinterpret_cast<uintptr_t>(sync) & 3))
-    return set_error(TI_ERR_INVALID_ARGUMENT, "gemm_residual_rmsnorm: norm operands must be 16-byte aligned");
-  NormSpec n;
-  n.w = norm_weight; n.out = norm_out; n.ld = ld_norm; n.eps = eps; n.sync = sync;
-  return gemm_entry(deterministic ? TI_EPI_RESIDUAL_DET : TI_EPI_RESIDUAL, A, lda, B, ldb, M, N,
-                    K, x, ldx, nullptr, nullptr, nullptr, dtype, block_n, split_k, stream, n);
 }
 
 extern "C" int ti_gemm_qkv_rope(const void* A, int64_t lda, const void* W, int64_t ldw,

@@ -1380,8 +1380,10 @@ merge_pieces_kernel(Params p, int units, int nheads) {
 // v5: one producer warp and pairs of consumer warps (head_dim 64, units of two kv heads,
 // GQA groups <= 8)
 //
-// Same block stream, chunking (one chunk per warp PAIR), pieces, split-K workspace and merge
-// as v4.  Warp 0 (lane 0) issues every TMA load of the CTA: per pair a kV5Stages-deep ring,
+// Same block stream, chunking (one chunk per warp PAIR), pieces and split-K workspace as v4;
+// the merge runs inside the kernel: each consumer warp announces its split pieces (per kv head)
+// once its chunk is done, and the last piece of a (sequence, kv head) to arrive merges them
+// (v2_merge), so no merge launch follows.  Warp 0 (lane 0) issues every TMA load of the CTA: per pair a kV5Stages-deep ring,
 // each stage the K and V tiles of one block for both kv heads of the unit (two 4 KB boxes).
 // The two warps of a pair read the same stage, warp 2i+1 computing the first kv head and warp
 // 2i+2 the second (swapped_block), and release it through an empty barrier of count 2.  With
@@ -1591,6 +1593,30 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   uint32_t phase = 0;
   uint32_t qb[4][2];
   float m[2], l[2], o[4][4];
+  T* const out_base = reinterpret_cast<T*>(p.out);
+  // Split pieces of this warp's chunk whose partials are written but not yet announced (at
+  // most two: a chunk cuts at most the unit it starts in and the unit it ends in).  They arrive
+  // together once the chunk is done -- one fence for both, and the warp never waits on an
+  // arrival in the middle of its chunk; the last piece of a (sequence, kv head) to arrive merges
+  // all of its pieces (v2_merge) and clears the counter for the next launch.
+  int npend = 0, pend_row[2], pend_kvh[2], pend_pieces[2];
+  auto arrive_pending = [&]() {
+    __threadfence();
+    __syncwarp();
+    for (int i = 0; i < npend; ++i) {
+      const int64_t kp = (int64_t)pend_row[i] * p.num_kv_heads + pend_kvh[i];
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.ws_count[kp], 1) == pend_pieces[i] - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        v2_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
+                    out_base + (int64_t)pend_row[i] * p.out_stride);
+        if (lane == 0) p.ws_count[kp] = 0;
+      }
+    }
+    npend = 0;
+  };
 
   while (pos < end) {
     // ---- a piece: positions of one unit inside [pos, end)
@@ -1643,8 +1669,6 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) l[j] += __shfl_xor_sync(0xffffffffu, l[j], off);
-    const int64_t pair = (int64_t)row * KVU + unit;
-    if (piece == 0 && sub == 0 && lane == 0) p.ws_pieces[pair] = pieces;   // merge_pieces_kernel
     if (pieces == 1) {
       T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
 #pragma unroll
@@ -1673,9 +1697,16 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
         }
         if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[j], l[j]);
       }
-      if (sub == 0 && lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
+      const int kvh = unit * 2 + sub;
+      if (lane == 0) p.ws_stop[((int64_t)row * p.num_kv_heads + kvh) * p.max_parts + piece] = stop;
+      if (npend == 2) arrive_pending();   // not reached for chunks cut as the plan cuts them
+      pend_row[npend] = row;
+      pend_kvh[npend] = kvh;
+      pend_pieces[npend] = pieces;
+      ++npend;
     }
   }
+  if (npend) arrive_pending();
 }
 
 template <typename T, bool PLANNED>
@@ -1693,13 +1724,9 @@ static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& 
     set_dev = dev;
   }
   if (batch > C::kMaxBatch) return set_error(TI_ERR_UNSUPPORTED, "paged attention v5: batch too large");
-  int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
-                         dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm,
-                         p, batch);
-  if (rc) return rc;
-  const int units = p.num_kv_heads / 2;
-  return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
-                       dim3(batch * units), dim3(256), 0, stream, 1, p, units, 2 * p.group);
+  return launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
+                       dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm, p,
+                       batch);
 }
 
 template <typename T, int HP>

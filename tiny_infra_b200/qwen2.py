@@ -7,11 +7,10 @@ for every layer, ``seq_len`` is NOT advanced -- the caller does that, engine/sch
 decode attends over seq_len + 1 tokens, models/qwen_25.py:115), and weights load from the
 reference's state-dict names (``load_reference_state_dict``).
 
-Per layer the forward is 5 kernel launches (decode: 6, the attention's split-K merge):
-  QKV GEMM (+bias, RoPE, KV append) -> paged attention (decode or prefill)
-  -> O GEMM (+residual, split-K, then the post-attention RMSNorm) -> gate/up GEMM (+SwiGLU)
-  -> down GEMM (+residual, then the next layer's input RMSNorm)
-plus the first layer's input RMSNorm
+Per layer the forward is 7 kernel launches:
+  rmsnorm -> QKV GEMM (+bias, RoPE, KV append) -> paged attention (decode or prefill, split-K
+  merged inside the decode kernel) -> O GEMM (+residual, split-K) -> rmsnorm
+  -> gate/up GEMM (+SwiGLU) -> down GEMM (+residual)
 with the residual stream kept in float32 (the reference keeps it in the model dtype; float32
 is closer to the float32 oracle).  The lm_head runs only on the rows whose logits are needed
 and, for greedy decoding, reduces to one token per row inside the GEMM epilogue.
@@ -75,8 +74,6 @@ class Qwen2ForCausalLM:
         # hidden states and greedy streams, ~13 % slower decode steps); False: every K slice
         # adds into the residual stream on its own (fastest; the last bits vary between runs).
         self.deterministic = False
-        # arrival counters of the residual projections' fused RMSNorm (zero between launches)
-        self._sync = torch.zeros(16, dtype=torch.int32, device=self.device)
 
     # ---- weights -------------------------------------------------------------------------
     def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
@@ -243,10 +240,8 @@ class Qwen2ForCausalLM:
                 trace=None, final_norm_out: torch.Tensor | None = None) -> None:
         """Layers first_layer .. num_layers-1 over the packed batch, in place on ``hidden``.
 
-        The input RMSNorm of the first layer is its own launch; every later RMSNorm runs in the
-        tail of the residual projection before it (o_proj -> post-attention norm, down_proj ->
-        the next layer's input norm, and with ``final_norm_out`` the last down_proj -> the
-        model's final norm into that buffer).
+        With ``final_norm_out`` (and the last layer run) the model's final RMSNorm of every row
+        is written there.
         ``trace(layer, stage, bufs)`` (optional) is called after each stage's kernel is issued
         (stages xn1, qkv, attn, h_mid, xn2, act, h_out; ``bufs`` holds xn / qkv / attn / act
         and the stream ``hidden``), e.g. to copy intermediate tensors for a parity check."""
@@ -273,8 +268,7 @@ class Qwen2ForCausalLM:
                 pb.num_seqs, NH, KVH, D, maxb, nb, plan.data_ptr(), plan.numel(), stream))
         split_o = self._splits(NH * D)
         split_d = self._splits(I)
-        det = int(self.deterministic)
-        sync = self._sync
+        residual = N.TI_EPI_RESIDUAL_DET if self.deterministic else N.TI_EPI_RESIDUAL
         tb = dict(bufs, hidden=hidden)
         end = c.num_layers if num_layers is None else num_layers
 
@@ -282,19 +276,13 @@ class Qwen2ForCausalLM:
             if trace is not None:
                 trace(li, stage, tb)
 
-        def residual_norm(a, lda, w, k, bn, split, norm_w, norm_out):
-            """hidden += a . w^T, then norm_out = norm_w * rmsnorm(hidden) (one launch)."""
-            N.check(lib.ti_gemm_residual_rmsnorm(
-                a.data_ptr(), lda, w.data_ptr(), k, T, H, k, hidden.data_ptr(), H, det, bn, split,
-                norm_w.data_ptr(), c.rms_norm_eps, norm_out.data_ptr(), norm_out.stride(0),
-                sync.data_ptr(), dt, stream))
+        def rmsnorm(out, weight, rows):
+            N.check(lib.ti_rmsnorm(out.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
+                                   weight.data_ptr(), c.rms_norm_eps, rows, H, dt, stream))
 
-        if first_layer < end:
-            N.check(lib.ti_rmsnorm(xn.data_ptr(), hidden.data_ptr(), N.TI_DTYPE_FP32,
-                                   W[f"{first_layer}.ln1"].data_ptr(), c.rms_norm_eps, T, H, dt,
-                                   stream))
         for li in range(first_layer, end):
             kc, vc = kv_cache.key_cache[li], kv_cache.value_cache[li]
+            rmsnorm(xn, W[f"{li}.ln1"], T)
             mark(li, "xn1")
             N.check(lib.ti_gemm_qkv_rope(
                 xn.data_ptr(), H, W[f"{li}.qkv"].data_ptr(), H, W[f"{li}.qkv_bias"].data_ptr(),
@@ -315,25 +303,22 @@ class Qwen2ForCausalLM:
                     pb.cu_seqlens.data_ptr(), pb.tile_seq.data_ptr(), pb.tile_q0.data_ptr(),
                     pb.tile_seq.numel(), NH, KVH, D, kv_cache.block_size, dt, stream))
             mark(li, "attn")
-            residual_norm(attn, NH * D, W[f"{li}.o"], NH * D, O_TILE, split_o, W[f"{li}.ln2"], xn)
+            N.check(lib.ti_gemm(residual, attn.data_ptr(), NH * D, W[f"{li}.o"].data_ptr(),
+                                NH * D, T, H, NH * D, hidden.data_ptr(), H, None, None, None, dt,
+                                O_TILE, split_o, stream))
             mark(li, "h_mid")
+            rmsnorm(xn, W[f"{li}.ln2"], T)
             mark(li, "xn2")
             N.check(lib.ti_gemm(N.TI_EPI_SWIGLU16, xn.data_ptr(), H,
                                 W[f"{li}.gate_up"].data_ptr(), H, T, 2 * I, H, act.data_ptr(), I,
                                 None, None, None, dt, 0, 1, stream))
             mark(li, "act")
-            if li + 1 < end:
-                residual_norm(act, I, W[f"{li}.down"], I, DOWN_TILE, split_d,
-                              W[f"{li + 1}.ln1"], xn)
-            elif final_norm_out is not None:
-                residual_norm(act, I, W[f"{li}.down"], I, DOWN_TILE, split_d, W["norm"],
-                              final_norm_out)
-            else:
-                epi = N.TI_EPI_RESIDUAL_DET if det else N.TI_EPI_RESIDUAL
-                N.check(lib.ti_gemm(epi, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
-                                    I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
-                                    DOWN_TILE, split_d, stream))
+            N.check(lib.ti_gemm(residual, act.data_ptr(), I, W[f"{li}.down"].data_ptr(),
+                                I, T, H, I, hidden.data_ptr(), H, None, None, None, dt,
+                                DOWN_TILE, split_d, stream))
             mark(li, "h_out")
+        if final_norm_out is not None and end == c.num_layers:
+            rmsnorm(final_norm_out, W["norm"], final_norm_out.shape[0])
 
     def _final_norm(self, hidden_rows: torch.Tensor, stream: int) -> torch.Tensor:
         c = self.config
