@@ -1458,10 +1458,35 @@ plan_kernel(Params p, int batch, int32_t* plan) {
   }
 }
 
+// Split-K arrivals of a v5 consumer warp's pending pieces (their partials are written): one
+// fence, one arrival per piece, and the last piece of a (sequence, kv head) merges them all and
+// clears the counter for the next launch.  Not inlined: the merge's registers stay out of the
+// kernel's main loop (inlined, they made the loop spill).
+template <typename T>
+__device__ __noinline__ void v5_arrive(const Params& p, int npend, const int* pend_row,
+                                       const int* pend_kvh, const int* pend_pieces, int G,
+                                       int lane, T* out_base) {
+  __threadfence();
+  __syncwarp();
+  for (int i = 0; i < npend; ++i) {
+    const int64_t kp = (int64_t)pend_row[i] * p.num_kv_heads + pend_kvh[i];
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.ws_count[kp], 1) == pend_pieces[i] - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      v2_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
+                  out_base + (int64_t)pend_row[i] * p.out_stride);
+      if (lane == 0) p.ws_count[kp] = 0;
+    }
+  }
+}
+
 template <typename T, bool PLANNED>
 __global__ void __launch_bounds__(kV5Threads, 1)
 decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
-                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
+                 const __grid_constant__ CUtensorMap vmap,
+                 const __grid_constant__ Params p, int batch) {
   if (threadIdx.x == 0) {   // descriptors are kernel parameters: independent of earlier kernels
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
@@ -1601,20 +1626,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   // all of its pieces (v2_merge) and clears the counter for the next launch.
   int npend = 0, pend_row[2], pend_kvh[2], pend_pieces[2];
   auto arrive_pending = [&]() {
-    __threadfence();
-    __syncwarp();
-    for (int i = 0; i < npend; ++i) {
-      const int64_t kp = (int64_t)pend_row[i] * p.num_kv_heads + pend_kvh[i];
-      int last = 0;
-      if (lane == 0) last = atomicAdd(&p.ws_count[kp], 1) == pend_pieces[i] - 1;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        v2_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
-                    out_base + (int64_t)pend_row[i] * p.out_stride);
-        if (lane == 0) p.ws_count[kp] = 0;
-      }
-    }
+    v5_arrive<T>(p, npend, pend_row, pend_kvh, pend_pieces, G, lane, out_base);
     npend = 0;
   };
 
