@@ -69,8 +69,12 @@ def _args():
                          "a Poisson request stream through the continuous batcher")
     ap.add_argument("--requests", type=int, default=1024, help="serving: number of requests")
     ap.add_argument("--rate", type=float, default=64.0, help="serving: arrivals per second")
+    ap.add_argument("--lm-head", choices=["bf16", "int8"], default="bf16",
+                    help="decode workload: the greedy lm_head's weights (int8: weight-only "
+                         "int8 copy with per-row scales)")
     ap.add_argument("--kernel", choices=["attention", "gate_up", "rmsnorm", "sampler",
-                                         "prefill_gemm", "prefill_attention"], default=None,
+                                         "prefill_gemm", "prefill_attention", "lm_head",
+                                         "lm_head_int8"], default=None,
                     help="time one kernel alone instead of the decode step")
     ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
@@ -178,7 +182,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------
-def build_workload(device, seed, steps_total):
+def build_workload(device, seed, steps_total, lm_head="bf16"):
     """Engine replica with SEQS sequences at their sampled context lengths, KV pre-filled."""
     import torch
     from tiny_infra_b200.cache_manager import KVCacheManager
@@ -193,6 +197,8 @@ def build_workload(device, seed, steps_total):
     blocks = int(sum((int(c) + steps_total + 15) // 16 for c in ctx)) + 64
     sd = Qwen2ForCausalLM.random_state_dict(cfg, seed=seed, tied=True, device=device)
     model = Qwen2ForCausalLM(cfg, device=device).load_reference_state_dict(sd)
+    if lm_head == "int8":
+        model.quantize_lm_head_int8()
     kv = KVCacheManager(SEQS, max_seq, cfg.num_layers, cfg.num_key_value_heads, cfg.head_dim,
                         device=device, num_blocks=blocks)
     slots = list(range(SEQS))
@@ -394,7 +400,7 @@ def run_ours(a, rank, world, local):
     steps_total = a.warmup + a.steps
     # the engine is built for warm-up + timed + e2e steps, and at least one context window
     cfg, sd, model, kv, engine, slots, ctx, first = build_workload(
-        device, a.seed + rank, max(2 * steps_total + 4, WINDOW + 4))
+        device, a.seed + rank, max(2 * steps_total + 4, WINDOW + 4), a.lm_head)
     peak, peak_kind = _peaks()
 
     # ---- device-resident decode (value) ----
@@ -518,7 +524,9 @@ def run_ours(a, rank, world, local):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights, random token ids, N(0,1) KV)",
-        "config": _config(world, {"global_batch": SEQS * world}),
+        "config": _config(world, {"global_batch": SEQS * world,
+                                  **({"lm_head": "weight-only int8 (per-row scales), greedy"}
+                                     if a.lm_head == "int8" else {})}),
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 3 * SEQS * 4,
                 "d2h_bytes_per_step": SEQS * 4,
                 "api": "tiny_infra_b200.engine.DecodeEngine.step (host lists in/out)"},
@@ -659,6 +667,56 @@ def run_gate_up_kernel(a):
     _kernel_line(a, "gate_up GEMM HBM GB/s", t, algo,
                  f"gate/up projection + SwiGLU (rows interleaved in groups of 8, 144-wide "
                  f"tiles), M={M}, N={2 * I}, K={H}, {L} layers' weights cycled", "synthetic (N(0,1) activations, N(0,0.02) weights)")
+    return 0
+
+
+def run_lm_head_kernel(a, int8):
+    """The greedy lm_head alone at 256 decode rows: 151936 x 896 weights (bf16, or the int8 copy
+    with per-row scales) times the final normed hidden rows, per-tile argmax in the epilogue;
+    two weight copies cycled (2 x 272 MB or 2 x 136 MB > L2).  GB/s of the weight bytes (+ the
+    activations and the argmax partials)."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    dev = torch.device("cuda:0")
+    M, H, V, L = SEQS, 896, 151936, 2
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    x = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    ws = [(torch.randn(V, H, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(L)]
+    nt = V // 128
+    val = torch.empty(M, nt, device=dev, dtype=torch.float32)
+    idx = torch.empty(M, nt, device=dev, dtype=torch.int32)
+    lib = N.lib()
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    if int8:
+        qs, ss = [], []
+        for w in ws:
+            q = torch.empty(V, H, dtype=torch.int8, device=dev)
+            sc = torch.empty(V, dtype=torch.float32, device=dev)
+            N.check(lib.ti_quantize_rows_int8(w.data_ptr(), H, V, H, q.data_ptr(), H,
+                                              sc.data_ptr(), N.TI_DTYPE_BF16, st()))
+            qs.append(q)
+            ss.append(sc)
+        del ws
+
+        def launch(i):
+            N.check(lib.ti_lm_head_argmax_int8(x.data_ptr(), H, qs[i].data_ptr(), H,
+                                               ss[i].data_ptr(), M, V, H, val.data_ptr(),
+                                               idx.data_ptr(), N.TI_DTYPE_BF16, st()))
+        wbytes = V * H + V * 4
+    else:
+        def launch(i):
+            N.check(lib.ti_gemm(N.TI_EPI_ARGMAX, x.data_ptr(), H, ws[i].data_ptr(), H, M, V, H,
+                                None, 0, None, val.data_ptr(), idx.data_ptr(), N.TI_DTYPE_BF16,
+                                128, 1, st()))
+        wbytes = V * H * 2
+    t = _time_launches(launch, L, a.steps, a.warmup)
+    algo = wbytes + M * H * 2 + M * nt * 8
+    kind = "weight-only int8 (per-row scales)" if int8 else "bf16"
+    _kernel_line(a, f"lm_head ({kind}) HBM GB/s", t, algo,
+                 f"greedy lm_head, {M} rows x {H} -> {V} vocab, {kind} weights, per-tile argmax "
+                 f"epilogue, {L} weight copies cycled",
+                 "synthetic (N(0,1) hidden rows, N(0,0.02) weights)")
     return 0
 
 
@@ -1015,6 +1073,8 @@ def main():
         return run_attention_kernel(a) if rank == 0 else 0
     if a.kernel == "rmsnorm":
         return run_rmsnorm_kernel(a) if rank == 0 else 0
+    if a.kernel in ("lm_head", "lm_head_int8"):
+        return run_lm_head_kernel(a, a.kernel == "lm_head_int8") if rank == 0 else 0
     if a.kernel == "sampler":
         return run_sampler_kernel(a) if rank == 0 else 0
     if a.kernel == "prefill_gemm":

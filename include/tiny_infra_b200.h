@@ -215,6 +215,24 @@ int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb
             int K, void* out, int64_t ldo, const void* bias, float* aux_val, int32_t* aux_idx,
             int dtype, int block_n, int split_k, void* stream);
 
+/* ---- weight-only INT8 lm_head (greedy decoding) --------------------------------------------
+ * The reference names weight-only INT8/INT4 quantised projections as its next step
+ * (README.md:156-157) and has no implementation; these two calls apply it to the tied lm_head
+ * (models/qwen_25.py:237,250).
+ * ti_quantize_rows_int8: per row r of w [rows, cols] (dtype, leading dim ldw):
+ *   scale[r] = max_c |w[r, c]| / 127 (1 for an all-zero row), q[r, c] = rint(w[r, c] / scale[r])
+ *   clamped to [-127, 127] (int8, leading dim ldq).  cols, ldw, ldq multiples of 8.
+ * ti_lm_head_argmax_int8: logits[m, n] = scale[n] * sum_k A[m, k] q[n, k] (A: M <= 256 rows of
+ *   dtype, fp32 accumulation of the exact products) reduced, like TI_EPI_ARGMAX with block_n 128,
+ *   to aux_val / aux_idx [M, N / 128] = (max, first argmax) of each row in each 128-column tile
+ *   (finish with ti_argmax_finish).  N % 128 == 0, K % 64 == 0, ldb (bytes) % 16 == 0, 16-byte
+ *   aligned operands.  The int8 weights are half the bytes of bf16 ones. */
+int ti_quantize_rows_int8(const void* w, int64_t ldw, int rows, int cols, int8_t* q, int64_t ldq,
+                          float* scale, int dtype, void* stream);
+int ti_lm_head_argmax_int8(const void* A, int64_t lda, const int8_t* Bq, int64_t ldb,
+                           const float* scale, int M, int N, int K, float* aux_val,
+                           int32_t* aux_idx, int dtype, void* stream);
+
 /* ---- QKV projection fused with RoPE and the KV-append write ----------------------
  * [q | k | v] = A[M, hidden] . W^T + bias, W = the fused [(NH+2*KVH)*64, hidden] q/k/v weight
  * (models/qwen_25.py:46-48,66-68).  RoPE (src/fused_rope.cu:37-50, tables cos/sin float32

@@ -42,6 +42,8 @@ SIGNATURES: dict[str, tuple] = {
     "ti_decode_prepare": (I32, [P, P, P, P, P, I64, I32, P, P, P, P, P, I32, I64, I32, I32, P]),
     "ti_argmax_finish": (I32, [P, P, I32, I32, P, P, P, I32, P]),
     "ti_kv_scatter": (I32, [P, P, P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P]),
+    "ti_quantize_rows_int8": (I32, [P, I64, I32, I32, P, I64, P, I32, P]),
+    "ti_lm_head_argmax_int8": (I32, [P, I64, P, I64, P, I32, I32, I32, P, P, I32, P]),
     "ti_gemm_qkv_rope": (I32, [P, I64, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P,
                                P, I32, I32, P]),
     "ti_sample": (I32, [P, I64, I32, I32, I32, P, P, P, P, P, P, P, I32, P]),

@@ -1458,12 +1458,63 @@ plan_kernel(Params p, int batch, int32_t* plan) {
   }
 }
 
+// Merge the pieces of one (sequence, kv head) and write its G output rows: lane l owns head
+// l / 4, dims 16 (l % 4) .. +15; pieces up to and including the first that stopped at a
+// negative block-table entry (their number from a ballot over the stop flags), combined with
+// weights 2^(m_piece - max m) in piece order; L == 0 gives NaN as attention.cu:150.
+template <typename T>
+__device__ __forceinline__ void v5_merge(const Params& p, int row, int kvh, int G, int pieces,
+                                         int lane, T* outp) {
+  const int64_t kp = (int64_t)row * p.num_kv_heads + kvh;
+  const int32_t* stops = p.ws_stop + kp * p.max_parts;
+  int use = pieces;
+  {
+    const int st = lane < pieces ? __ldcg(stops + lane) : 0;   // pieces <= 17 < 32
+    const unsigned b = __ballot_sync(0xffffffffu, st != 0);
+    if (b) use = __ffs(b);
+  }
+  const int hl = lane >> 2, dq = lane & 3;
+  if (hl >= G) return;
+  const int64_t base = ((int64_t)row * p.num_heads + (int64_t)kvh * G + hl) * p.max_parts;
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + base;
+  float M = -INFINITY;
+#pragma unroll 4
+  for (int q = 0; q < use; ++q) M = fmaxf(M, __ldcg(ml + q).x);
+  float L = 0.f, acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll 2
+  for (int q = 0; q < use; ++q) {
+    const float2 mq = __ldcg(ml + q);
+    const float f = mq.x == -INFINITY ? 0.f : fast_exp2(mq.x - M);
+    L += mq.y * f;
+    const float4* src = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64 + dq * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = __ldcg(src + i);
+      acc[4 * i] += f * v.x; acc[4 * i + 1] += f * v.y;
+      acc[4 * i + 2] += f * v.z; acc[4 * i + 3] += f * v.w;
+    }
+  }
+  const float inv = 1.f / L;
+  T* dst = outp + ((int64_t)kvh * G + hl) * 64 + dq * 16;
+#pragma unroll
+  for (int i = 0; i < 16; i += 8) {
+    uint4 u;
+    u.x = Elem<T>::pack2(acc[i] * inv, acc[i + 1] * inv);
+    u.y = Elem<T>::pack2(acc[i + 2] * inv, acc[i + 3] * inv);
+    u.z = Elem<T>::pack2(acc[i + 4] * inv, acc[i + 5] * inv);
+    u.w = Elem<T>::pack2(acc[i + 6] * inv, acc[i + 7] * inv);
+    *reinterpret_cast<uint4*>(dst + i) = u;
+  }
+}
+
 // Split-K arrivals of a v5 consumer warp's pending pieces (their partials are written): one
 // fence, one arrival per piece, and the last piece of a (sequence, kv head) merges them all and
-// clears the counter for the next launch.  Not inlined: the merge's registers stay out of the
-// kernel's main loop (inlined, they made the loop spill).
+// clears the counter for the next launch.  The merge holds 16 accumulators per lane: with a
+// merge of 32 per lane and all pieces' (m, l) in registers the kernel's main loop spilled.
 template <typename T>
-__device__ __noinline__ void v5_arrive(const Params& p, int npend, const int* pend_row,
+__device__ __forceinline__ void v5_arrive(const Params& p, int npend, const int* pend_row,
                                        const int* pend_kvh, const int* pend_pieces, int G,
                                        int lane, T* out_base) {
   __threadfence();
@@ -1475,7 +1526,7 @@ __device__ __noinline__ void v5_arrive(const Params& p, int npend, const int* pe
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence();
-      v2_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
+      v5_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
                   out_base + (int64_t)pend_row[i] * p.out_stride);
       if (lane == 0) p.ws_count[kp] = 0;
     }

@@ -98,10 +98,20 @@ class DecodeEngine:
                                   dp[3].data_ptr(), self.next_tok.data_ptr(),
                                   self.d_in[1].data_ptr(), kv.seq_len.data_ptr(), 1, s))
             return
-        N.check(lib.ti_gemm(N.TI_EPI_ARGMAX, self.xf.data_ptr(), c.hidden_size,
-                            m.weights["lm_head"].data_ptr(), c.hidden_size, rows, c.vocab_size,
-                            c.hidden_size, None, 0, None, self.part_val.data_ptr(),
-                            self.part_idx.data_ptr(), dt, LM_TILE, 1, s))
+        if "lm_head_q" in m.weights:        # weight-only int8 lm_head, 256 rows per launch
+            q, sc = m.weights["lm_head_q"], m.weights["lm_head_scale"]
+            for r0 in range(0, rows, 256):
+                n = min(256, rows - r0)
+                N.check(lib.ti_lm_head_argmax_int8(
+                    self.xf[r0].data_ptr(), c.hidden_size, q.data_ptr(), q.stride(0),
+                    sc.data_ptr(), n, c.vocab_size, c.hidden_size, self.part_val[r0].data_ptr(),
+                    self.part_idx[r0].data_ptr(), dt, s))
+        else:
+            N.check(lib.ti_gemm(N.TI_EPI_ARGMAX, self.xf.data_ptr(), c.hidden_size,
+                                m.weights["lm_head"].data_ptr(), c.hidden_size, rows,
+                                c.vocab_size, c.hidden_size, None, 0, None,
+                                self.part_val.data_ptr(), self.part_idx.data_ptr(), dt, LM_TILE,
+                                1, s))
         N.check(lib.ti_argmax_finish(self.part_val.data_ptr(), self.part_idx.data_ptr(),
                                      self.ntiles, rows, self.next_tok.data_ptr(),
                                      self.d_in[1].data_ptr(), kv.seq_len.data_ptr(), 1, s))

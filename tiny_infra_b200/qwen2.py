@@ -150,13 +150,35 @@ class Qwen2ForCausalLM:
         sd["lm_head.weight"] = sd["model.embed_tokens.weight"] if tied else rnd(V, H)
         return sd
 
+    def quantize_lm_head_int8(self) -> "Qwen2ForCausalLM":
+        """Add a weight-only int8 copy of the lm_head (one float32 scale per vocab row,
+        ``ti_quantize_rows_int8``) that greedy decode steps of ``DecodeEngine`` then read instead
+        of the bf16 matrix: 136 MB instead of 272 MB per step.  This changes the model's logits
+        by the int8 rounding of the weights (the reference lists weight-only INT8 as its next
+        step, README.md:156-157); sampled steps and ``forward`` keep the bf16 lm_head."""
+        W = self.weights["lm_head"]
+        V, H = W.shape
+        q = torch.empty(V, H, dtype=torch.int8, device=self.device)
+        scale = torch.empty(V, dtype=torch.float32, device=self.device)
+        N.check(N.lib().ti_quantize_rows_int8(
+            W.data_ptr(), W.stride(0), V, H, q.data_ptr(), q.stride(0), scale.data_ptr(),
+            N.dtype_code(self.dtype), torch.cuda.current_stream(self.device).cuda_stream))
+        self.weights["lm_head_q"] = q
+        self.weights["lm_head_scale"] = scale
+        return self
+
     def weight_bytes(self) -> int:
-        """Bytes of weights one decode step streams (the tied lm_head counted once)."""
+        """Bytes of weights one greedy decode step streams: every layer's weights and the
+        lm_head once (the tied embedding is the same matrix; with the int8 lm_head its int8
+        copy and scales instead of the bf16 matrix, of which the step reads only its tokens'
+        embedding rows)."""
+        skip = {"lm_head", "embed"} if "lm_head_q" in self.weights else set()
         seen, total = set(), 0
-        for t in self.weights.values():
-            if t.data_ptr() not in seen:
-                seen.add(t.data_ptr())
-                total += t.numel() * t.element_size()
+        for k, t in self.weights.items():
+            if k in skip or t.data_ptr() in seen:
+                continue
+            seen.add(t.data_ptr())
+            total += t.numel() * t.element_size()
         return total
 
     # ---- scratch buffers ---------------------------------------------------------------------
