@@ -74,7 +74,7 @@ def _args():
                          "int8 copy with per-row scales)")
     ap.add_argument("--kernel", choices=["attention", "gate_up", "rmsnorm", "sampler",
                                          "prefill_gemm", "prefill_attention", "lm_head",
-                                         "lm_head_int8"], default=None,
+                                         "lm_head_int8", "qkv", "o_proj", "down"], default=None,
                     help="time one kernel alone instead of the decode step")
     ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
@@ -720,6 +720,63 @@ def run_lm_head_kernel(a, int8):
     return 0
 
 
+def run_projection_kernel(a):
+    """One decode-step projection alone at 256 tokens, weight copies cycled (> L2): qkv
+    (896 -> 1152 with bias, RoPE and the KV-append write into a paged pool), o_proj (896 -> 896)
+    or down (4864 -> 896), both adding into the float32 residual stream (split-K red.add, as in
+    the decode step).  GB/s of the algorithmic bytes: weights, activations in, output."""
+    import torch
+    from tiny_infra_b200 import _native as N
+    dev = torch.device("cuda:0")
+    M, H, I, NH, KVH, D = SEQS, 896, 4864, 14, 2, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed)
+    lib = N.lib()
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    K, Nout = {"qkv": (H, (NH + 2 * KVH) * D), "o_proj": (NH * D, H), "down": (I, H)}[a.kernel]
+    L = -(-320 * 2 ** 20 // (Nout * K * 2))      # weight copies: > 2.5 x L2 in every cycle
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    ws = [(torch.randn(Nout, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+          for _ in range(L)]
+    if a.kernel == "qkv":
+        bias = (torch.randn(Nout, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        nb = M + 16
+        kc = torch.zeros(nb, KVH, 16, D, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        slot = torch.arange(M, device=dev, dtype=torch.int64) * 16     # one block per token
+        pos = torch.randint(0, 2048, (M,), device=dev, dtype=torch.int32, generator=g)
+        inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=dev).float() / D))
+        fr = torch.outer(torch.arange(4096, device=dev, dtype=torch.float32), inv)
+        cos, sin = fr.cos().contiguous(), fr.sin().contiguous()
+        q = torch.empty(M, NH * D, device=dev, dtype=torch.bfloat16)
+
+        def launch(i):
+            N.check(lib.ti_gemm_qkv_rope(x.data_ptr(), K, ws[i].data_ptr(), K, bias.data_ptr(), M,
+                                         H, NH, KVH, D, q.data_ptr(), NH * D, kc.data_ptr(),
+                                         vc.data_ptr(), slot.data_ptr(), cos.data_ptr(),
+                                         sin.data_ptr(), pos.data_ptr(), 16, N.TI_DTYPE_BF16,
+                                         st()))
+        out_bytes = M * Nout * 2
+        what = "QKV projection + bias + RoPE + KV append (cluster split-K)"
+    else:
+        hidden = torch.zeros(M, Nout, device=dev, dtype=torch.float32)
+        bn, split = (64, 7) if a.kernel == "o_proj" else (128, 16)
+
+        def launch(i):
+            N.check(lib.ti_gemm(N.TI_EPI_RESIDUAL, x.data_ptr(), K, ws[i].data_ptr(), K, M, Nout,
+                                K, hidden.data_ptr(), Nout, None, None, None, N.TI_DTYPE_BF16,
+                                bn, split, st()))
+        out_bytes = M * Nout * 4 * 2                  # residual read-modify-write (float32)
+        what = f"{a.kernel} projection + residual add (block_n {bn}, split-K red.add)"
+    t = _time_launches(launch, L, max(a.steps, L), a.warmup)
+    algo = Nout * K * 2 + M * K * 2 + out_bytes
+    _kernel_line(a, f"{a.kernel} GEMM HBM GB/s", t, algo,
+                 f"{what}, M={M}, N={Nout}, K={K}, {L} weight copies cycled (> L2), "
+                 f"{max(a.steps, L)} launches timed",
+                 "synthetic (N(0,1) activations, N(0,0.02) weights)")
+    return 0
+
+
 def run_rmsnorm_kernel(a):
     """RMSNorm of the fused-elementwise workload: 4096 tokens x hidden 896, float32 residual
     stream in, bf16 out, eps 1e-6, cycling over 12 inputs (176 MB > L2); GB/s of its
@@ -1073,6 +1130,8 @@ def main():
         return run_attention_kernel(a) if rank == 0 else 0
     if a.kernel == "rmsnorm":
         return run_rmsnorm_kernel(a) if rank == 0 else 0
+    if a.kernel in ("qkv", "o_proj", "down"):
+        return run_projection_kernel(a) if rank == 0 else 0
     if a.kernel in ("lm_head", "lm_head_int8"):
         return run_lm_head_kernel(a, a.kernel == "lm_head_int8") if rank == 0 else 0
     if a.kernel == "sampler":

@@ -38,6 +38,7 @@ extern "C" {
 #define TI_DEVERR_GEMM_WAIT 0x2u
 #define TI_DEVERR_PREFILL_WAIT 0x4u
 #define TI_DEVERR_ATTN_PLAN 0x8u   /* a planned attention call got a plan of another batch */
+#define TI_DEVERR_BAD_INPUT 0x10u  /* a slot / position / block id outside the table or pool */
 
 /* ---- library ---------------------------------------------------------------------------- */
 
@@ -128,7 +129,9 @@ int ti_paged_attention_decode_planned(void* out, int64_t out_seq_stride, const v
  * call on each device looks the array's device address up (cudaGetSymbolAddress) and loads
  * the library's device code there: make that first call before any stream capture.  All calls
  * share the array; each clears its arrival counters on `stream` before launching, and calls
- * that overlap on the GPU race on the array. */
+ * that overlap on the GPU race on the array.  A call that splits no sequence (head_dim 128 with
+ * at most 16 blocks per sequence) uses no scratch and is never refused.  The looked-up address
+ * belongs to the device's context: do not call this again after cudaDeviceReset of the device. */
 #define TI_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int ti_paged_attention_decode_noalloc(void* out, int64_t out_seq_stride, const void* q,
                                       int64_t q_seq_stride, const void* k_cache,
@@ -287,9 +290,14 @@ int ti_sample(const void* logits, int64_t ld, int dtype, int rows, int vocab,
  * host allocator decided it, FIFO order of engine/cache_manager.py:86-92), then sets
  * positions[r] = seq_len[slot] (models/qwen_25.py:218-222), slot_mapping[r] (pool slot of the
  * new token), ctx_lens[r] = seq_len[slot] + 1 (models/qwen_25.py:115) and hidden[r] (float32)
- * = embed[tokens[r]].  Padding rows get slot_mapping -1, ctx 0 and a zero hidden row. */
+ * = embed[tokens[r]].  Padding rows get slot_mapping -1, ctx 0 and a zero hidden row.
+ * block_tables has num_slots rows of max_blocks_per_seq entries (row stride bt_stride); the pool
+ * has num_blocks blocks.  A slot >= num_slots or a position beyond the row's last block makes
+ * the row padding, a new_block >= num_blocks is not written, a table entry >= num_blocks gets
+ * no pool slot (-1); each raises TI_DEVERR_BAD_INPUT. */
 int ti_decode_prepare(const int32_t* tokens, const int32_t* slots, const int32_t* new_block,
                       const int32_t* seq_len, int32_t* block_tables, int64_t bt_stride,
+                      int num_slots, int max_blocks_per_seq, int64_t num_blocks,
                       int block_size, int32_t* positions, int64_t* slot_mapping,
                       int32_t* ctx_lens, float* hidden, const void* embed, int hidden_size,
                       int64_t vocab, int rows, int dtype, void* stream);
@@ -304,11 +312,13 @@ int ti_argmax_finish(const float* part_val, const int32_t* part_idx, int ntiles,
 
 /* Write K/V rows of num_tokens tokens into the pool at slot_mapping[t] (-1 = skip):
  * k/v element (t, h, d) at t*tok_stride + h*head_stride + d.  The write of
- * engine/cache_manager.py:95-99. */
+ * engine/cache_manager.py:95-99.  Slots at or beyond num_blocks * block_size (outside the pool
+ * of num_blocks blocks) are not written and raise TI_DEVERR_BAD_INPUT. */
 int ti_kv_scatter(void* k_cache, void* v_cache, const void* k, int64_t k_tok_stride,
                   int64_t k_head_stride, const void* v, int64_t v_tok_stride,
                   int64_t v_head_stride, const int64_t* slot_mapping, int num_tokens,
-                  int num_kv_heads, int head_dim, int block_size, int dtype, void* stream);
+                  int64_t num_blocks, int num_kv_heads, int head_dim, int block_size, int dtype,
+                  void* stream);
 
 #ifdef __cplusplus
 }

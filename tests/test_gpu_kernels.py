@@ -299,3 +299,49 @@ def test_qkv_rope_append_gemm(cuda_device, T):
     written = np.zeros((NB, bs), bool)
     written[blk, off] = True
     assert (_f32(kc).transpose(0, 2, 1, 3)[~written] == 0).all()
+
+
+def test_step_kernels_bound_their_indices(cuda_device):
+    """ti_decode_prepare and ti_kv_scatter check slots, positions and block ids against the
+    block table and the pool they are given: a row whose position lies past its table row, or
+    whose slot is outside the table, becomes padding; a new block or a pool slot outside the pool
+    is not written; each raises TI_DEVERR_BAD_INPUT and leaves the valid rows' results intact."""
+    from tiny_infra_b200 import _native as N
+    lib, dev = N.lib(), cuda_device
+    s = torch.cuda.current_stream().cuda_stream
+    slots_n, mb, nb, bs, H, V = 4, 3, 10, 16, 64, 32
+    bt = torch.full((slots_n, mb), -1, dtype=torch.int32, device=dev)
+    bt[0, 0] = 2
+    seq = torch.tensor([5, 0, mb * bs, 0], dtype=torch.int32, device=dev)   # slot 2: past its row
+    tokens = torch.tensor([1, 2, 3, 4], dtype=torch.int32, device=dev)
+    rows_slots = torch.tensor([0, 1, 2, 9], dtype=torch.int32, device=dev)  # 9: outside the table
+    new_block = torch.tensor([-1, nb + 5, 4, 6], dtype=torch.int32, device=dev)  # row 1: outside
+    pos = torch.full((4,), -7, dtype=torch.int32, device=dev)
+    smap = torch.full((4,), -7, dtype=torch.int64, device=dev)
+    ctx = torch.full((4,), -7, dtype=torch.int32, device=dev)
+    hid = torch.full((4, H), 3.0, dtype=torch.float32, device=dev)
+    emb = torch.randn(V, H, device=dev).to(torch.bfloat16)
+    N.device_status()
+    N.check(lib.ti_decode_prepare(tokens.data_ptr(), rows_slots.data_ptr(), new_block.data_ptr(),
+                                  seq.data_ptr(), bt.data_ptr(), bt.stride(0), slots_n, mb, nb, bs,
+                                  pos.data_ptr(), smap.data_ptr(), ctx.data_ptr(), hid.data_ptr(),
+                                  emb.data_ptr(), H, V, 4, N.TI_DTYPE_BF16, s))
+    torch.cuda.synchronize()
+    assert N.device_status() & N.TI_DEVERR_BAD_INPUT
+    assert smap.tolist() == [2 * bs + 5, -1, -1, -1]
+    assert ctx.tolist() == [6, 1, 0, 0] and pos.tolist()[:2] == [5, 0]
+    assert bt[1].tolist() == [-1, -1, -1] and bt[2].tolist() == [-1, -1, -1]
+    assert torch.equal(hid[0], emb[1].float()) and (hid[2:] == 0).all()
+    kc = torch.zeros(nb, 2, bs, 64, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    k = torch.randn(3, 2, 64, device=dev).to(torch.bfloat16)
+    v = torch.randn(3, 2, 64, device=dev).to(torch.bfloat16)
+    sm = torch.tensor([3, nb * bs, -1], dtype=torch.int64, device=dev)     # second: outside
+    N.check(lib.ti_kv_scatter(kc.data_ptr(), vc.data_ptr(), k.data_ptr(), k.stride(0), k.stride(1),
+                              v.data_ptr(), v.stride(0), v.stride(1), sm.data_ptr(), 3, nb, 2, 64,
+                              bs, N.TI_DTYPE_BF16, s))
+    torch.cuda.synchronize()
+    assert N.device_status() & N.TI_DEVERR_BAD_INPUT
+    assert torch.equal(kc[0, :, 3], k[0]) and torch.equal(vc[0, :, 3], v[0])
+    assert int((kc != 0).sum()) == int((k[0] != 0).sum())
+    assert N.device_status() == 0

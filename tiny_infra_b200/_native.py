@@ -39,9 +39,10 @@ SIGNATURES: dict[str, tuple] = {
     "ti_gemm": (I32, [I32, P, I64, P, I64, I32, I32, I32, P, I64, P, P, P, I32, I32, I32, P]),
     "ti_paged_prefill_attention": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, P, P, P, I32,
                                          I32, I32, I32, I32, I32, P]),
-    "ti_decode_prepare": (I32, [P, P, P, P, P, I64, I32, P, P, P, P, P, I32, I64, I32, I32, P]),
+    "ti_decode_prepare": (I32, [P, P, P, P, P, I64, I32, I32, I64, I32, P, P, P, P, P, I32, I64,
+                                I32, I32, P]),
     "ti_argmax_finish": (I32, [P, P, I32, I32, P, P, P, I32, P]),
-    "ti_kv_scatter": (I32, [P, P, P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P]),
+    "ti_kv_scatter": (I32, [P, P, P, I64, I64, P, I64, I64, P, I32, I64, I32, I32, I32, I32, P]),
     "ti_quantize_rows_int8": (I32, [P, I64, I32, I32, P, I64, P, I32, P]),
     "ti_lm_head_argmax_int8": (I32, [P, I64, P, I64, P, I32, I32, I32, P, P, I32, P]),
     "ti_gemm_qkv_rope": (I32, [P, I64, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P,
@@ -58,6 +59,7 @@ TI_EPI_SWIGLU16 = 5
 TI_EPI_RESIDUAL_DET = 6
 # device status bits (ti_device_status)
 TI_DEVERR_ATTN_WAIT, TI_DEVERR_GEMM_WAIT, TI_DEVERR_PREFILL_WAIT, TI_DEVERR_ATTN_PLAN = 1, 2, 4, 8
+TI_DEVERR_BAD_INPUT = 16
 
 _lib = None
 _lock = threading.Lock()

@@ -259,8 +259,8 @@ class KVCacheManager:
             N.check(N.lib().ti_kv_scatter(
                 self.key_cache[layer_idx].data_ptr(), self.value_cache[layer_idx].data_ptr(),
                 k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0), v.stride(1),
-                m.data_ptr(), n, self.num_kv_heads, self.head_dim, self.block_size,
-                N.dtype_code(self.dtype), N.stream_of(k)))
+                m.data_ptr(), n, self.total_physical_blocks, self.num_kv_heads, self.head_dim,
+                self.block_size, N.dtype_code(self.dtype), N.stream_of(k)))
             torch.cuda.current_stream(self.device).synchronize()
         if err is not None:
             raise err

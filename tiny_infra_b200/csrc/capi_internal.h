@@ -57,6 +57,10 @@ int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
   return 0;
 }
 
+// Split-K slots per (sequence, query head) that ti_paged_attention_decode uses with the default
+// partitioning (1: the call needs no workspace).
+int64_t attn_split_parts(int batch, int head_dim, int max_blocks);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 int encode_tensor_map_2d(CUtensorMap* out, CUtensorMapDataType type, void* base,
                          const cuuint64_t* dims, const cuuint64_t* strides_bytes,

@@ -20,6 +20,7 @@
 //             and tile into aux_val / aux_idx, overlapping the next tile's MMAs.
 // Every wait is bounded (TI_DEVERR_GEMM_WAIT on expiry, then the kernel winds down).
 #include <algorithm>
+#include <type_traits>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -42,20 +43,34 @@ constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 static_assert(kStage % 1024 == 0, "stage alignment");
 
-// 8 int8 values (two 32-bit words) -> 8 elements of T packed as four 32-bit words (exact: every
-// integer in [-128, 127] is a bf16 / fp16 value).
+// 8 int8 values (two 32-bit words) -> 8 elements of T packed as four 32-bit words, exactly and
+// with full-rate integer / float ops only (a per-element int -> float conversion instruction runs
+// on the slow conversion unit and made the converters the bottleneck).  u = byte ^ 0x80 is the
+// value + 128; bf16: the float32 with bits 0x4B000000 | u is 2^23 + u, minus 2^23 + 128 it is the
+// value, and a small integer's float32 has zero low 16 bits, so its high half is the bf16;
+// fp16: the half with bits 0x6400 | u is 1024 + u, minus 1152 (one packed subtraction).
 template <typename T>
 __device__ __forceinline__ uint4 convert8(uint32_t lo, uint32_t hi) {
   uint32_t o[4];
-  const uint32_t w[2] = {lo, hi};
+  const uint32_t w[2] = {lo ^ 0x80808080u, hi ^ 0x80808080u};
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const float a = (float)(int8_t)(w[i] & 0xffu);
-    const float b = (float)(int8_t)((w[i] >> 8) & 0xffu);
-    const float c = (float)(int8_t)((w[i] >> 16) & 0xffu);
-    const float d = (float)(int8_t)(w[i] >> 24);
-    o[2 * i] = Elem<T>::pack2(a, b);
-    o[2 * i + 1] = Elem<T>::pack2(c, d);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      float f[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        f[j] = __uint_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540u | j)) - 8388736.0f;
+      o[2 * i] = __byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632u);
+      o[2 * i + 1] = __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632u);
+    } else {
+      const __half2 bias = __halves2half2(__float2half(1152.f), __float2half(1152.f));
+      const uint32_t a = __byte_perm(w[i], 0x64646464u, 0x5140u);
+      const uint32_t b = __byte_perm(w[i], 0x64646464u, 0x5342u);
+      __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+      __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+      o[2 * i] = *reinterpret_cast<uint32_t*>(&ha);
+      o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hb);
+    }
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }

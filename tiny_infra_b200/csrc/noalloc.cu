@@ -8,7 +8,9 @@
 // loads this library's device code on the device and should happen before any stream capture.
 // Every call shares the one array, whose contents persist between calls: the split-K arrival
 // counters at its start are cleared on the call's stream before each launch, and calls that
-// overlap on the GPU (other streams, other threads) race on the array.
+// overlap on the GPU (other streams, other threads) race on the array.  The cached address
+// belongs to the device's current context: after cudaDeviceReset (or any teardown of that
+// context) the entry point must not be called again in the same process.
 #include <cstdio>
 #include <mutex>
 
@@ -60,6 +62,13 @@ extern "C" int ti_paged_attention_decode_noalloc(
   if (batch == 0) return TI_OK;
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_blocks_per_seq <= 0)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention (no-alloc): bad sizes");
+  // a call whose sequences are never split (head_dim 128 with at most one partition of
+  // blocks) needs no scratch at all, whatever its batch size
+  if (attn_split_parts(batch, head_dim, max_blocks_per_seq) <= 1)
+    return ti_paged_attention_decode(out, out_seq_stride, q, q_seq_stride, k_cache, v_cache,
+                                     num_blocks, block_tables, bt_stride, row_index, context_lens,
+                                     batch, num_heads, num_kv_heads, head_dim, block_size,
+                                     max_blocks_per_seq, dtype, 0, nullptr, 0, stream);
   const size_t need = ti_paged_attention_workspace_bytes(batch, num_heads, num_kv_heads, head_dim,
                                                           max_blocks_per_seq, 0);
   if (need > noalloc::kScratchBytes) {

@@ -1380,10 +1380,8 @@ merge_pieces_kernel(Params p, int units, int nheads) {
 // v5: one producer warp and pairs of consumer warps (head_dim 64, units of two kv heads,
 // GQA groups <= 8)
 //
-// Same block stream, chunking (one chunk per warp PAIR), pieces and split-K workspace as v4;
-// the merge runs inside the kernel: each consumer warp announces its split pieces (per kv head)
-// once its chunk is done, and the last piece of a (sequence, kv head) to arrive merges them
-// (v2_merge), so no merge launch follows.  Warp 0 (lane 0) issues every TMA load of the CTA: per pair a kV5Stages-deep ring,
+// Same block stream, chunking (one chunk per warp PAIR), pieces, split-K workspace and merge
+// as v4.  Warp 0 (lane 0) issues every TMA load of the CTA: per pair a kV5Stages-deep ring,
 // each stage the K and V tiles of one block for both kv heads of the unit (two 4 KB boxes).
 // The two warps of a pair read the same stage, warp 2i+1 computing the first kv head and warp
 // 2i+2 the second (swapped_block), and release it through an empty barrier of count 2.  With
@@ -1458,86 +1456,10 @@ plan_kernel(Params p, int batch, int32_t* plan) {
   }
 }
 
-// Merge the pieces of one (sequence, kv head) and write its G output rows: lane l owns head
-// l / 4, dims 16 (l % 4) .. +15; pieces up to and including the first that stopped at a
-// negative block-table entry (their number from a ballot over the stop flags), combined with
-// weights 2^(m_piece - max m) in piece order; L == 0 gives NaN as attention.cu:150.
-template <typename T>
-__device__ __forceinline__ void v5_merge(const Params& p, int row, int kvh, int G, int pieces,
-                                         int lane, T* outp) {
-  const int64_t kp = (int64_t)row * p.num_kv_heads + kvh;
-  const int32_t* stops = p.ws_stop + kp * p.max_parts;
-  int use = pieces;
-  {
-    const int st = lane < pieces ? __ldcg(stops + lane) : 0;   // pieces <= 17 < 32
-    const unsigned b = __ballot_sync(0xffffffffu, st != 0);
-    if (b) use = __ffs(b);
-  }
-  const int hl = lane >> 2, dq = lane & 3;
-  if (hl >= G) return;
-  const int64_t base = ((int64_t)row * p.num_heads + (int64_t)kvh * G + hl) * p.max_parts;
-  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + base;
-  float M = -INFINITY;
-#pragma unroll 4
-  for (int q = 0; q < use; ++q) M = fmaxf(M, __ldcg(ml + q).x);
-  float L = 0.f, acc[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-#pragma unroll 2
-  for (int q = 0; q < use; ++q) {
-    const float2 mq = __ldcg(ml + q);
-    const float f = mq.x == -INFINITY ? 0.f : fast_exp2(mq.x - M);
-    L += mq.y * f;
-    const float4* src = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64 + dq * 16);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = __ldcg(src + i);
-      acc[4 * i] += f * v.x; acc[4 * i + 1] += f * v.y;
-      acc[4 * i + 2] += f * v.z; acc[4 * i + 3] += f * v.w;
-    }
-  }
-  const float inv = 1.f / L;
-  T* dst = outp + ((int64_t)kvh * G + hl) * 64 + dq * 16;
-#pragma unroll
-  for (int i = 0; i < 16; i += 8) {
-    uint4 u;
-    u.x = Elem<T>::pack2(acc[i] * inv, acc[i + 1] * inv);
-    u.y = Elem<T>::pack2(acc[i + 2] * inv, acc[i + 3] * inv);
-    u.z = Elem<T>::pack2(acc[i + 4] * inv, acc[i + 5] * inv);
-    u.w = Elem<T>::pack2(acc[i + 6] * inv, acc[i + 7] * inv);
-    *reinterpret_cast<uint4*>(dst + i) = u;
-  }
-}
-
-// Split-K arrivals of a v5 consumer warp's pending pieces (their partials are written): one
-// fence, one arrival per piece, and the last piece of a (sequence, kv head) merges them all and
-// clears the counter for the next launch.  The merge holds 16 accumulators per lane: with a
-// merge of 32 per lane and all pieces' (m, l) in registers the kernel's main loop spilled.
-template <typename T>
-__device__ __forceinline__ void v5_arrive(const Params& p, int npend, const int* pend_row,
-                                       const int* pend_kvh, const int* pend_pieces, int G,
-                                       int lane, T* out_base) {
-  __threadfence();
-  __syncwarp();
-  for (int i = 0; i < npend; ++i) {
-    const int64_t kp = (int64_t)pend_row[i] * p.num_kv_heads + pend_kvh[i];
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&p.ws_count[kp], 1) == pend_pieces[i] - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence();
-      v5_merge<T>(p, pend_row[i], pend_kvh[i], G, pend_pieces[i], lane,
-                  out_base + (int64_t)pend_row[i] * p.out_stride);
-      if (lane == 0) p.ws_count[kp] = 0;
-    }
-  }
-}
-
 template <typename T, bool PLANNED>
 __global__ void __launch_bounds__(kV5Threads, 1)
 decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
-                 const __grid_constant__ CUtensorMap vmap,
-                 const __grid_constant__ Params p, int batch) {
+                 const __grid_constant__ CUtensorMap vmap, Params p, int batch) {
   if (threadIdx.x == 0) {   // descriptors are kernel parameters: independent of earlier kernels
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
@@ -1669,17 +1591,6 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   uint32_t phase = 0;
   uint32_t qb[4][2];
   float m[2], l[2], o[4][4];
-  T* const out_base = reinterpret_cast<T*>(p.out);
-  // Split pieces of this warp's chunk whose partials are written but not yet announced (at
-  // most two: a chunk cuts at most the unit it starts in and the unit it ends in).  They arrive
-  // together once the chunk is done -- one fence for both, and the warp never waits on an
-  // arrival in the middle of its chunk; the last piece of a (sequence, kv head) to arrive merges
-  // all of its pieces (v2_merge) and clears the counter for the next launch.
-  int npend = 0, pend_row[2], pend_kvh[2], pend_pieces[2];
-  auto arrive_pending = [&]() {
-    v5_arrive<T>(p, npend, pend_row, pend_kvh, pend_pieces, G, lane, out_base);
-    npend = 0;
-  };
 
   while (pos < end) {
     // ---- a piece: positions of one unit inside [pos, end)
@@ -1732,6 +1643,8 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) l[j] += __shfl_xor_sync(0xffffffffu, l[j], off);
+    const int64_t pair = (int64_t)row * KVU + unit;
+    if (piece == 0 && sub == 0 && lane == 0) p.ws_pieces[pair] = pieces;   // merge_pieces_kernel
     if (pieces == 1) {
       T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
 #pragma unroll
@@ -1760,16 +1673,9 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
         }
         if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + sl * 2) = make_float2(m[j], l[j]);
       }
-      const int kvh = unit * 2 + sub;
-      if (lane == 0) p.ws_stop[((int64_t)row * p.num_kv_heads + kvh) * p.max_parts + piece] = stop;
-      if (npend == 2) arrive_pending();   // not reached for chunks cut as the plan cuts them
-      pend_row[npend] = row;
-      pend_kvh[npend] = kvh;
-      pend_pieces[npend] = pieces;
-      ++npend;
+      if (sub == 0 && lane == 0) p.ws_stop[pair * p.max_parts + piece] = stop;
     }
   }
-  if (npend) arrive_pending();
 }
 
 template <typename T, bool PLANNED>
@@ -1787,9 +1693,13 @@ static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& 
     set_dev = dev;
   }
   if (batch > C::kMaxBatch) return set_error(TI_ERR_UNSUPPORTED, "paged attention v5: batch too large");
-  return launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
-                       dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm, p,
-                       batch);
+  int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
+                         dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm,
+                         p, batch);
+  if (rc) return rc;
+  const int units = p.num_kv_heads / 2;
+  return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
+                       dim3(batch * units), dim3(256), 0, stream, 1, p, units, 2 * p.group);
 }
 
 template <typename T, int HP>
@@ -1860,6 +1770,12 @@ static int64_t attn_parts(int batch, int head_dim, int max_blocks, int partition
   if (partition_blocks <= 0) partition_blocks = attn::default_partition(max_blocks);
   return (max_blocks + partition_blocks - 1) / partition_blocks;
 }
+
+namespace ti {
+int64_t attn_split_parts(int batch, int head_dim, int max_blocks) {
+  return attn_parts(batch, head_dim, max_blocks, 0);
+}
+}  // namespace ti
 
 extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, int num_kv_heads,
                                                       int head_dim, int max_blocks_per_seq,

@@ -22,7 +22,8 @@ __global__ void decode_prepare_kernel(const int32_t* __restrict__ tokens,
                                       const int32_t* __restrict__ slots,
                                       const int32_t* __restrict__ new_block,
                                       const int32_t* __restrict__ seq_len, int32_t* block_tables,
-                                      int64_t bt_stride, int bs, int32_t* __restrict__ positions,
+                                      int64_t bt_stride, int num_slots, int max_blocks,
+                                      int64_t num_blocks, int bs, int32_t* __restrict__ positions,
                                       int64_t* __restrict__ slot_mapping,
                                       int32_t* __restrict__ ctx_lens, float* __restrict__ hidden,
                                       const T* __restrict__ embed, int H, int64_t V, int rows) {
@@ -34,18 +35,25 @@ __global__ void decode_prepare_kernel(const int32_t* __restrict__ tokens,
   __shared__ int s_tok;
   if (threadIdx.x == 0) {
     int tok = tokens[r];
-    if (slot < 0) {
+    // a slot outside the table, or a position past its last block column, is an input error
+    // the host planner rules out: flagged, and the row is treated as padding (no writes)
+    const int pos = (slot >= 0 && slot < num_slots) ? seq_len[slot] : -1;
+    if (slot >= num_slots || (slot >= 0 && (pos < 0 || pos / bs >= max_blocks)))
+      raise_device_error(TI_DEVERR_BAD_INPUT);
+    if (slot < 0 || slot >= num_slots || pos < 0 || pos / bs >= max_blocks) {
       positions[r] = 0;
       slot_mapping[r] = -1;
       ctx_lens[r] = 0;
       tok = -1;
     } else {
-      const int pos = seq_len[slot];
       int32_t* row = block_tables + (int64_t)slot * bt_stride;
-      if (new_block[r] >= 0) row[pos / bs] = new_block[r];
+      const int nb = new_block[r];
+      if (nb >= num_blocks) raise_device_error(TI_DEVERR_BAD_INPUT);
+      else if (nb >= 0) row[pos / bs] = nb;
       const int blk = row[pos / bs];
       positions[r] = pos;
-      slot_mapping[r] = blk >= 0 ? (int64_t)blk * bs + pos % bs : -1;
+      // a block id outside the pool gets no KV write (attention treats it as absent too)
+      slot_mapping[r] = (blk >= 0 && blk < num_blocks) ? (int64_t)blk * bs + pos % bs : -1;
       ctx_lens[r] = pos + 1;
     }
     s_tok = tok;
@@ -109,7 +117,7 @@ __global__ void kv_scatter_kernel(T* k_cache, T* v_cache, const T* __restrict__ 
                                   int64_t k_tok_stride, int64_t k_head_stride,
                                   const T* __restrict__ v, int64_t v_tok_stride,
                                   int64_t v_head_stride, const int64_t* __restrict__ slots,
-                                  int tokens, int KVH, int HD, int bs) {
+                                  int64_t pool_slots, int tokens, int KVH, int HD, int bs) {
   pdl_wait();
   pdl_launch_dependents();
   const int per = KVH * (HD / 8);
@@ -121,6 +129,10 @@ __global__ void kv_scatter_kernel(T* k_cache, T* v_cache, const T* __restrict__ 
     const int h = r / (HD / 8), d = (r % (HD / 8)) * 8;
     const int64_t slot = slots[t];
     if (slot < 0) continue;
+    if (slot >= pool_slots) {          // outside the pool: flagged, not written
+      if (r == 0) raise_device_error(TI_DEVERR_BAD_INPUT);
+      continue;
+    }
     const int64_t dst = (((slot / bs) * KVH + h) * bs + slot % bs) * HD + d;
     *reinterpret_cast<uint4*>(k_cache + dst) =
         *reinterpret_cast<const uint4*>(k + t * k_tok_stride + h * k_head_stride + d);
@@ -136,7 +148,8 @@ using namespace ti;
 
 extern "C" int ti_decode_prepare(const int32_t* tokens, const int32_t* slots,
                                  const int32_t* new_block, const int32_t* seq_len,
-                                 int32_t* block_tables, int64_t bt_stride, int block_size,
+                                 int32_t* block_tables, int64_t bt_stride, int num_slots,
+                                 int max_blocks_per_seq, int64_t num_blocks, int block_size,
                                  int32_t* positions, int64_t* slot_mapping, int32_t* ctx_lens,
                                  float* hidden, const void* embed, int hidden_size, int64_t vocab,
                                  int rows, int dtype, void* stream) {
@@ -145,18 +158,23 @@ extern "C" int ti_decode_prepare(const int32_t* tokens, const int32_t* slots,
   if (!tokens || !slots || !new_block || !seq_len || !block_tables || !positions ||
       !slot_mapping || !ctx_lens || !hidden || !embed || rows < 0)
     return set_error(TI_ERR_INVALID_ARGUMENT, "decode_prepare: null pointer");
+  if (num_slots <= 0 || max_blocks_per_seq <= 0 || num_blocks <= 0 || block_size <= 0 ||
+      bt_stride < max_blocks_per_seq)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "decode_prepare: bad block-table or pool shape");
   if (hidden_size % 8) return set_error(TI_ERR_UNSUPPORTED, "decode_prepare: hidden % 8 != 0");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TI_DTYPE_BF16)
     return launch_kernel("decode_prepare launch", step::decode_prepare_kernel<__nv_bfloat16>,
                          dim3(rows), dim3(128), 0, s, 1,
-        tokens, slots, new_block, seq_len, block_tables, bt_stride, block_size, positions,
-        slot_mapping, ctx_lens, hidden, (const __nv_bfloat16*)embed, hidden_size, vocab, rows);
+        tokens, slots, new_block, seq_len, block_tables, bt_stride, num_slots, max_blocks_per_seq,
+        num_blocks, block_size, positions, slot_mapping, ctx_lens, hidden,
+        (const __nv_bfloat16*)embed, hidden_size, vocab, rows);
   else if (dtype == TI_DTYPE_FP16)
     return launch_kernel("decode_prepare launch", step::decode_prepare_kernel<__half>,
                          dim3(rows), dim3(128), 0, s, 1,
-        tokens, slots, new_block, seq_len, block_tables, bt_stride, block_size, positions,
-        slot_mapping, ctx_lens, hidden, (const __half*)embed, hidden_size, vocab, rows);
+        tokens, slots, new_block, seq_len, block_tables, bt_stride, num_slots, max_blocks_per_seq,
+        num_blocks, block_size, positions, slot_mapping, ctx_lens, hidden, (const __half*)embed,
+        hidden_size, vocab, rows);
   else
     return set_error(TI_ERR_UNSUPPORTED, "decode_prepare: dtype must be bf16 or fp16");
 }
@@ -178,12 +196,13 @@ extern "C" int ti_argmax_finish(const float* part_val, const int32_t* part_idx, 
 extern "C" int ti_kv_scatter(void* k_cache, void* v_cache, const void* k, int64_t k_tok_stride,
                              int64_t k_head_stride, const void* v, int64_t v_tok_stride,
                              int64_t v_head_stride, const int64_t* slot_mapping, int num_tokens,
-                             int num_kv_heads, int head_dim, int block_size, int dtype,
-                             void* stream) {
+                             int64_t num_blocks, int num_kv_heads, int head_dim, int block_size,
+                             int dtype, void* stream) {
   clear_error();
   if (num_tokens == 0) return TI_OK;
-  if (!k_cache || !v_cache || !k || !v || !slot_mapping || num_tokens < 0)
-    return set_error(TI_ERR_INVALID_ARGUMENT, "kv_scatter: null pointer");
+  if (!k_cache || !v_cache || !k || !v || !slot_mapping || num_tokens < 0 || num_blocks <= 0)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "kv_scatter: null pointer or empty pool");
+  const int64_t pool_slots = num_blocks * block_size;
   if (head_dim % 8 || (k_tok_stride | k_head_stride | v_tok_stride | v_head_stride) % 8 ||
       ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15))
     return set_error(TI_ERR_INVALID_ARGUMENT, "kv_scatter: rows must be 16-byte aligned");
@@ -195,13 +214,13 @@ extern "C" int ti_kv_scatter(void* k_cache, void* v_cache, const void* k, int64_
                          dim3(blocks), dim3(256), 0, s, 1,
         (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (const __nv_bfloat16*)k, k_tok_stride,
         k_head_stride, (const __nv_bfloat16*)v, v_tok_stride, v_head_stride, slot_mapping,
-        num_tokens, num_kv_heads, head_dim, block_size);
+        pool_slots, num_tokens, num_kv_heads, head_dim, block_size);
   else if (dtype == TI_DTYPE_FP16)
     return launch_kernel("kv_scatter launch", step::kv_scatter_kernel<__half>,
                          dim3(blocks), dim3(256), 0, s, 1,
         (__half*)k_cache, (__half*)v_cache, (const __half*)k, k_tok_stride, k_head_stride,
-        (const __half*)v, v_tok_stride, v_head_stride, slot_mapping, num_tokens, num_kv_heads,
-        head_dim, block_size);
+        (const __half*)v, v_tok_stride, v_head_stride, slot_mapping, pool_slots, num_tokens,
+        num_kv_heads, head_dim, block_size);
   else
     return set_error(TI_ERR_UNSUPPORTED, "kv_scatter: dtype must be bf16 or fp16");
 }

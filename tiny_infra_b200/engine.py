@@ -82,6 +82,7 @@ class DecodeEngine:
         N.check(lib.ti_decode_prepare(
             self.d_in[0].data_ptr(), self.d_in[1].data_ptr(), self.d_in[2].data_ptr(),
             kv.seq_len.data_ptr(), kv.block_tables.data_ptr(), kv.block_tables.stride(0),
+            kv.block_tables.shape[0], kv.block_tables.shape[1], kv.total_physical_blocks,
             kv.block_size, self.positions.data_ptr(), self.slot_mapping.data_ptr(),
             self.ctx_lens.data_ptr(), self.hidden.data_ptr(), m.weights["embed"].data_ptr(),
             c.hidden_size, c.vocab_size, rows, dt, s))
