@@ -213,15 +213,17 @@ def test_argmax_epilogue(cuda_device):
     assert (ix >= 0).all() and (ix < N).all()
 
 
-@pytest.mark.parametrize("M", [37, 130, 256])
+@pytest.mark.parametrize("M", [1, 16, 32, 37, 64, 130, 256])
 def test_argmax_persistent_lm_head(cuda_device, M):
-    """Greedy lm_head without logits (the persistent kernel: both 128-row halves per CTA, two
-    TMEM buffers): per-tile (max, first argmax) equal to the float32 reference; ties planted
-    across tiles resolve to the lowest index."""
+    """Greedy lm_head without logits: up to 64 tokens the weight-streaming kernel (gemv.cu:
+    tokens resident, weights as the MMA's M), above the persistent GEMM (both 128-row halves per
+    CTA, two TMEM buffers): per-tile (max, first argmax) equal to the float32 reference; ties
+    planted within a tile and across tiles resolve to the lowest index."""
     from tiny_infra_b200 import _native as N_
     N, K, bn = 151936, 896, 128
     a, b = _operands(M + 3, M, N, K)
     b[140000] = b[77]
+    b[78] = b[77]
     a[M - 1] = bf16_round(b[77] * 64.0)
     nt = N // bn
     val = torch.empty((M, nt), dtype=torch.float32, device="cuda")

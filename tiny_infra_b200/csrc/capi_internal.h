@@ -61,6 +61,15 @@ int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 // partitioning (1: the call needs no workspace).
 int64_t attn_split_parts(int batch, int head_dim, int max_blocks);
 
+// The weight-streaming greedy lm_head for small token counts (gemv.cu): M <= 64 tokens of A
+// (dtype, leading dim lda) against N rows of B (dtype, or int8 with per-row `scale` when int8),
+// K <= 896, N % 128 == 0; writes the [M, N / 128] argmax partials.
+constexpr int kGemvMaxTokens = 64;
+constexpr int kGemvMaxK = 896;
+int gemv_argmax(const void* A, int64_t lda, const void* B, int64_t ldb, bool int8,
+                const float* scale, int M, int N, int K, float* aux_val, int32_t* aux_idx,
+                int dtype, cudaStream_t s);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 int encode_tensor_map_2d(CUtensorMap* out, CUtensorMapDataType type, void* base,
                          const cuuint64_t* dims, const cuuint64_t* strides_bytes,

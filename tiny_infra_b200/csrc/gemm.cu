@@ -1050,6 +1050,12 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
 
   CUtensorMap am, bm;
   int rc;
+  if (epilogue == TI_EPI_ARGMAX && !out && block_n == gemm::lmh::kBN && M <= kGemvMaxTokens &&
+      K <= kGemvMaxK) {
+    // few tokens: stream the weights through the swapped kernel, tokens resident (gemv.cu)
+    return gemv_argmax(A, lda, B, ldb, false, nullptr, M, N, K, aux_val, aux_idx, dtype,
+                       reinterpret_cast<cudaStream_t>(stream));
+  }
   if (epilogue == TI_EPI_ARGMAX && !out && M <= 256 && block_n == gemm::lmh::kBN) {
     // greedy lm_head: persistent kernel, both 128-row halves per CTA
     rc = gemm::operand_map(&am, A, M, K, lda, 256, dtype);

@@ -348,6 +348,9 @@ extern "C" int ti_lm_head_argmax_int8(const void* A, int64_t lda, const int8_t* 
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bq) |
        reinterpret_cast<uintptr_t>(scale)) & 15 || (lda % 8) || (ldb % 16))
     return set_error(TI_ERR_INVALID_ARGUMENT, "lm_head_argmax_int8: operands must be 16-byte aligned (lda % 8, ldb % 16)");
+  if (M <= kGemvMaxTokens && K <= kGemvMaxK)   // few tokens: the weight-streaming kernel
+    return gemv_argmax(A, lda, Bq, ldb, true, scale, M, N, K, aux_val, aux_idx, dtype,
+                       reinterpret_cast<cudaStream_t>(stream));
   CUtensorMap am, qm;
   {
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
