@@ -42,7 +42,8 @@ template <int NP, bool I8>
 struct Cfg {
   static constexpr int kMaxK = 896;                           // tokens held for K <= 896
   static constexpr int kXBytes = kMaxK / kBK * NP * 128;      // the resident token tiles
-  static constexpr int kStages = I8 ? 7 : 6;                  // weight tiles in flight
+  // weight tiles in flight (int8: 8 KB each, so more of them for the same bytes in flight)
+  static constexpr int kStages = I8 ? (NP <= 32 ? 14 : 7) : 6;
   static constexpr int kConv = I8 ? 3 : 0;                    // converted 16-bit tiles (int8)
   static constexpr int kRing = kStages * (I8 ? kQTile : kWTile) + kConv * kWTile;
   static constexpr int kRed = 4 * NP * 8;                     // (max, argmax) per warp, token
