@@ -90,6 +90,17 @@ def test_attention_split_k_long(cuda_device, pb):
     assert ok, err
 
 
+def test_attention_small_batch_many_pieces(cuda_device):
+    """Small decode batches cut each sequence into up to 65 pieces so that a few sequences still
+    spread over every SM; the merge reads them in rounds of 16: 3 sequences of 8192 tokens (64
+    pieces each), one with a -1 entry inside its third round of pieces."""
+    q, k, v, bt, ctx = _attn_case(7, 3, 14, 2, 64, 1600, 8000, 8192)
+    bt[1, 300] = -1
+    out, ref = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx)
+    ok, err = _attn_ok(out, ref)
+    assert ok, err
+
+
 def test_attention_edge_cases(cuda_device):
     """ctx 0 leaves the row untouched; a -1 entry truncates the context (in the first and in a
     later partition); a leading -1 gives NaN; block ids past the pool are treated as -1."""

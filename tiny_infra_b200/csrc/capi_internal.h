@@ -59,7 +59,8 @@ int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 
 // Split-K slots per (sequence, query head) that ti_paged_attention_decode uses with the default
 // partitioning (1: the call needs no workspace).
-int64_t attn_split_parts(int batch, int head_dim, int max_blocks);
+int64_t attn_split_parts(int batch, int num_heads, int num_kv_heads, int head_dim,
+                         int max_blocks);
 
 // The weight-streaming greedy lm_head for small token counts (gemv.cu): M <= 64 tokens of A
 // (dtype, leading dim lda) against N rows of B (dtype, or int8 with per-row `scale` when int8),

@@ -64,7 +64,7 @@ extern "C" int ti_paged_attention_decode_noalloc(
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention (no-alloc): bad sizes");
   // a call whose sequences are never split (head_dim 128 with at most one partition of
   // blocks) needs no scratch at all, whatever its batch size
-  if (attn_split_parts(batch, head_dim, max_blocks_per_seq) <= 1)
+  if (attn_split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq) <= 1)
     return ti_paged_attention_decode(out, out_seq_stride, q, q_seq_stride, k_cache, v_cache,
                                      num_blocks, block_tables, bt_stride, row_index, context_lens,
                                      batch, num_heads, num_kv_heads, head_dim, block_size,

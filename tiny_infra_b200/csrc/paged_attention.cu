@@ -452,6 +452,10 @@ static int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm,
 constexpr int kV2Meta = 4;
 constexpr int kV2MaxBatch = 4096;
 constexpr int kV2MaxPieces = 17;                           // pieces per unit (bounded by the chunk)
+// Small decode batches (the v5 kernel): units may be cut into up to this many pieces, so that a
+// few sequences still spread over every SM (the merge reads their partials in rounds of 16).
+constexpr int kV5MaxPiecesSmall = 65;
+constexpr int kV5SmallBatch = 64;
 
 struct PieceV2 {
   int row, unit, j0, len, ctx, piece, pieces;
@@ -476,12 +480,14 @@ struct CfgV2 {
   static_assert(kTotal <= 227 * 1024, "v2 shared memory");
 };
 
-// chunk of the block stream per warp: balanced, but at least max_blocks / 16 (so that a unit is
-// cut into at most kV2MaxPieces pieces, which bounds the split-K workspace) and at least 2 (small
-// batches: 8 sequences of up to 512 tokens take 9.7 us with 2, 11.2 us with 4, measured)
-__host__ __device__ inline int v2_chunk(int64_t total_blocks, int warps, int max_blocks) {
+// chunk of the block stream per warp: balanced, but at least max_blocks / (max_parts - 1) (so
+// that a unit is cut into at most max_parts pieces, which bounds the split-K workspace) and at
+// least 2 (small batches: 8 sequences of up to 512 tokens take 9.7 us with 2, 11.2 us with 4,
+// measured)
+__host__ __device__ inline int v2_chunk(int64_t total_blocks, int warps, int max_blocks,
+                                        int max_parts) {
   int64_t c = (total_blocks + warps - 1) / warps;
-  const int lo = max(2, (max_blocks + 15) / 16);
+  const int lo = max(2, (max_blocks + max_parts - 2) / (max_parts - 1));
   return (int)(c < lo ? lo : c);
 }
 
@@ -766,7 +772,7 @@ decode_kernel_v2(const __grid_constant__ CUtensorMap kmap,
   __syncthreads();
   const int total = s_off[batch];
   const int W = gridDim.x * C::kWarps;
-  const int chunk = v2_chunk(total, W, p.max_blocks);
+  const int chunk = v2_chunk(total, W, p.max_blocks, p.max_parts);
   const int wid = blockIdx.x * C::kWarps + warp;
   const int begin = wid * chunk;
   if (begin >= total) return;
@@ -1105,7 +1111,7 @@ __device__ __forceinline__ bool resolve_stream(const Params& p, int batch, int s
   }
   __syncthreads();
   const int total = s_off[batch];
-  chunk = v2_chunk(total, gridDim.x * streams, p.max_blocks);
+  chunk = v2_chunk(total, gridDim.x * streams, p.max_blocks, p.max_parts);
   cb = blockIdx.x * streams * chunk;
   if (cb >= total) return false;
   ce = min(total, cb + streams * chunk);
@@ -1334,38 +1340,52 @@ merge_pieces_kernel(Params p, int units, int nheads) {
   if (ctx <= 0 || pieces <= 1) return;   // no blocks (row left untouched) or not split
   const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
   const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
-  int st[kV2MaxPieces];
-  float2 ml[kV2MaxPieces];
-  float4 v[kV2MaxPieces];
-#pragma unroll
-  for (int q = 0; q < kV2MaxPieces; ++q) {   // all partials of the unit in one round
-    if (q < pieces) {
-      st[q] = stops[q];
-      ml[q] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
-      v[q] = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64)[d4];
-    } else {
-      st[q] = 0;
-      ml[q] = make_float2(-INFINITY, 0.f);
-      v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
-  int use = pieces;                       // up to and including the first piece that stopped
-#pragma unroll
-  for (int q = kV2MaxPieces - 1; q >= 0; --q)
-    if (q < pieces && st[q]) use = q + 1;
-  float M = -INFINITY;
-#pragma unroll
-  for (int q = 0; q < kV2MaxPieces; ++q)
-    if (q < use) M = fmaxf(M, ml[q].x);
-  float L = 0.f;
+  // Rounds of kRound pieces, all of a round's partials loaded together (one round for up to 16
+  // pieces, as many as the decode step's units have); pieces are used up to and including the
+  // first that stopped at a negative block-table entry, and each round's maximum rescales the
+  // running sums (online softmax over the pieces).
+  constexpr int kRound = 16;
+  int use = pieces;
+  float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int q0 = 0; q0 < use; q0 += kRound) {
+    int st[kRound];
+    float2 ml[kRound];
+    float4 v[kRound];
 #pragma unroll
-  for (int q = 0; q < kV2MaxPieces; ++q) {
-    if (q < use) {
-      const float f = ml[q].x == -INFINITY ? 0.f : fast_exp2(ml[q].x - M);
-      L += ml[q].y * f;
-      acc.x += f * v[q].x; acc.y += f * v[q].y; acc.z += f * v[q].z; acc.w += f * v[q].w;
+    for (int i = 0; i < kRound; ++i) {
+      const int q = q0 + i;
+      if (q < use) {
+        st[i] = stops[q];
+        ml[i] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
+        v[i] = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64)[d4];
+      } else {
+        st[i] = 0;
+        ml[i] = make_float2(-INFINITY, 0.f);
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
+    int n = min(kRound, use - q0);          // this round's pieces, up to the first stop
+#pragma unroll
+    for (int i = kRound - 1; i >= 0; --i)
+      if (i < n && st[i]) n = i + 1;
+    use = min(use, q0 + n);
+    float Mr = M;
+#pragma unroll
+    for (int i = 0; i < kRound; ++i)
+      if (i < n) Mr = fmaxf(Mr, ml[i].x);
+    const float fo = M == -INFINITY ? 0.f : fast_exp2(M - Mr);   // rescale the earlier rounds
+    L *= fo;
+    acc.x *= fo; acc.y *= fo; acc.z *= fo; acc.w *= fo;
+#pragma unroll
+    for (int i = 0; i < kRound; ++i) {
+      if (i < n) {
+        const float f = ml[i].x == -INFINITY ? 0.f : fast_exp2(ml[i].x - Mr);
+        L += ml[i].y * f;
+        acc.x += f * v[i].x; acc.y += f * v[i].y; acc.z += f * v[i].z; acc.w += f * v[i].w;
+      }
+    }
+    M = Mr;
   }
   const float inv = 1.f / L;               // L == 0 -> NaN (attention.cu:150)
   T* dst = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride +
@@ -1771,16 +1791,31 @@ static int64_t attn_parts(int batch, int head_dim, int max_blocks, int partition
   return (max_blocks + partition_blocks - 1) / partition_blocks;
 }
 
+static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks);
+
+// Split-K slots per (sequence, query head) of a call: the v5 kernel at <= kV5SmallBatch
+// sequences cuts units finer (kV5MaxPiecesSmall pieces at most), so a small batch's blocks
+// spread over every SM; otherwise as attn_parts.
+static int64_t split_parts(int batch, int num_heads, int num_kv_heads, int head_dim,
+                           int max_blocks, int partition_blocks) {
+  if (batch <= attn::kV5SmallBatch && partition_blocks <= 0 &&
+      v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks))
+    return attn::kV5MaxPiecesSmall;
+  return attn_parts(batch, head_dim, max_blocks, partition_blocks);
+}
+
 namespace ti {
-int64_t attn_split_parts(int batch, int head_dim, int max_blocks) {
-  return attn_parts(batch, head_dim, max_blocks, 0);
+int64_t attn_split_parts(int batch, int num_heads, int num_kv_heads, int head_dim,
+                         int max_blocks) {
+  return split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks, 0);
 }
 }  // namespace ti
 
 extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, int num_kv_heads,
                                                       int head_dim, int max_blocks_per_seq,
                                                       int partition_blocks) {
-  const int64_t parts = attn_parts(batch, head_dim, max_blocks_per_seq, partition_blocks);
+  const int64_t parts =
+      split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq, partition_blocks);
   const int64_t slots = (int64_t)batch * num_heads * parts;
   size_t bytes = attn::kCounterBytes;                           // arrival counters (kept zero)
   bytes += (size_t)slots * head_dim * 4;                        // ws_o
@@ -1797,9 +1832,11 @@ static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, in
   const int forced = attn::forced_kernel();
   if (forced != 0 && forced != 5) return false;
   if (batch > attn::CfgV5::kMaxBatch) return false;
+  // the largest chunk any batch of this shape can get (the piece floor at 17 pieces is the
+  // larger one) must fit a CTA's id window
   const int64_t worst = (int64_t)batch * (num_kv_heads / 2) * max_blocks;
-  return (int64_t)attn::v2_chunk(worst, attn::sm_count() * attn::kV5Pairs, max_blocks) *
-             attn::kV5Pairs <= attn::kV5IdCap;
+  return (int64_t)attn::v2_chunk(worst, attn::sm_count() * attn::kV5Pairs, max_blocks,
+                                 attn::kV2MaxPieces) * attn::kV5Pairs <= attn::kV5IdCap;
 }
 
 static int decode_impl(
@@ -1834,7 +1871,8 @@ static int decode_impl(
       (reinterpret_cast<uintptr_t>(out) & 3) || (out_seq_stride & 1))
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: q/out must be 4-byte aligned with even row strides");
   const bool v2 = attn::use_v2(head_dim, batch);
-  const int max_parts = (int)attn_parts(batch, head_dim, max_blocks_per_seq, partition_blocks);
+  const int max_parts = (int)split_parts(batch, num_heads, num_kv_heads, head_dim,
+                                         max_blocks_per_seq, partition_blocks);
   const size_t need = ti_paged_attention_workspace_bytes(batch, num_heads, num_kv_heads, head_dim,
                                                           max_blocks_per_seq, partition_blocks);
   if (max_parts > 1 && (!workspace || workspace_bytes < need))
@@ -1889,7 +1927,8 @@ static int decode_impl(
       return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, false>(p, km, vm, batch, s)
                                     : attn::launch_v5<__half, false>(p, km, vm, batch, s);
     }
-    const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq);
+    const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq,
+                                            max_parts);
     if (p.group <= 8 && forced != 2 && chunk_ub * attn::kV4Warps <= attn::kV4IdCap) {
       if (hp == 2)
         return dtype == TI_DTYPE_BF16 ? attn::launch_v4<__nv_bfloat16, 2>(p, km, vm, batch, s)
@@ -1954,6 +1993,7 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
   p.context_lens = context_lens;
   p.num_heads = num_heads; p.num_kv_heads = num_kv_heads; p.group = num_heads / num_kv_heads;
   p.max_blocks = max_blocks_per_seq; p.num_blocks = num_blocks;
+  p.max_parts = (int)split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq, 0);
   return launch_kernel("attention plan launch", attn::plan_kernel<512>, dim3(attn::sm_count()),
                        dim3(512), 0, reinterpret_cast<cudaStream_t>(stream), 1, p, batch,
                        reinterpret_cast<int32_t*>(plan));
