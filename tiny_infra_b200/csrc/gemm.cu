@@ -299,14 +299,34 @@ __device__ __forceinline__ void swiglu16_rows(uint32_t trow, int lr, uint32_t st
   }
 }
 
+// Pool slots of the rows one epilogue thread stores in a k / v tile of the QKV epilogue (rows
+// t / 8 + 16 j of the R staged rows, t = the thread's index among the 128), loaded before the
+// accumulator wait so that the stores do not wait on a dependent load; -1: no store.
+template <int KIND, int R>
+struct KvSlots {
+  static constexpr int kN = KIND == TI_EPI_QKV_ROPE ? R / 16 : 1;
+  int64_t s[kN];
+  __device__ __forceinline__ void load(const EpiArgs& e, int n0, int y0) {
+    if constexpr (KIND == TI_EPI_QKV_ROPE) {
+      const int t = (int)threadIdx.x - 64;
+      const bool kv = n0 / 64 >= e.num_heads;
+#pragma unroll
+      for (int j = 0; j < kN; ++j) {
+        const int row = y0 + (t >> 3) + 16 * j;
+        s[j] = kv && row < e.M ? e.slot_mapping[row] : -1;
+      }
+    }
+  }
+};
+
 // Write the staged tile (R rows starting at global row y0) to global memory: the 128 epilogue
 // threads walk it in 16-byte chunks, consecutive threads on consecutive chunks of a row, so
 // each warp store covers whole lines; the residual adds with red.global.add (one add per
 // element: deterministic).  The k / v heads of the QKV epilogue go to their pool slots, one
 // 128-byte row per token.  Fire-and-forget: the CTA does not wait for the writes.
-template <typename T, int BN, int KIND>
-__device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int R, int n0, int y0,
-                                           bool ok) {
+template <typename T, int BN, int KIND, int R>
+__device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int n0, int y0,
+                                           bool ok, const KvSlots<KIND, R>& kv) {
   using O = Out<T, BN, KIND>;
   constexpr int PB = O::kPanelBytes;
   constexpr int CPR = O::kBytes / 16;   // 16-byte chunks per staged row
@@ -319,11 +339,11 @@ __device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int
       const bool is_k = head < e.num_heads + e.num_kv_heads;
       const int kh = is_k ? head - e.num_heads : head - e.num_heads - e.num_kv_heads;
       T* pool = reinterpret_cast<T*>(is_k ? e.k_cache : e.v_cache);
-      for (int idx = t; idx < R * 8; idx += 128) {   // 8 threads per 128-byte row
-        const int r = idx >> 3, ch = idx & 7;
-        const int row = y0 + r;
-        if (row >= e.M) continue;
-        const int64_t slot = e.slot_mapping[row];
+      static_assert(R % 16 == 0, "whole rounds of 16 rows");
+#pragma unroll
+      for (int j = 0; j < R / 16; ++j) {   // 8 threads per 128-byte row
+        const int r = (t >> 3) + 16 * j, ch = t & 7;
+        const int64_t slot = kv.s[j];
         if (slot < 0) continue;
         const uint4 v = ld_shared_v4(stage + stage_off<PB>(r, ch * 16, R));
         T* dst = pool + (((slot / e.block_size) * e.num_kv_heads + kh) * e.block_size +
@@ -445,6 +465,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   const int red_row = m0 + (int)rank * C::kRows + red_lr;
   const bool red_live = red_t >= 0 && red_row < e.M;
   Pre<T, BN, KIND, (CL > 1 ? C::kW : 4)> pre;
+  KvSlots<KIND, C::kRows> kv;
   bool ok = true;
 
   if (warp == 1) {
@@ -504,6 +525,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     if constexpr (CL > 1) {
       if (red_live) pre.load(e, red_row, n0, red_c);
     }
+    kv.load(e, n0, m0 + (int)rank * C::kRows);
     // tcgen05.ld is warp-collective: the warp goes on only when all its lanes saw the phase
     ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, TI_DEVERR_GEMM_WAIT));
     tc_fence_after();
@@ -531,7 +553,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
           }
         }
       }
-      store_tile<T, BN, KIND>(e, sbase, BM, n0, m0, ok && nk > 0);
+      store_tile<T, BN, KIND, BM>(e, sbase, n0, m0, ok && nk > 0, kv);
     } else {
       // this CTA's fp32 partial tile -> shared memory (zeros for an empty split)
       float* red = reinterpret_cast<float*>(smem) + (quad * 32 + lane) * C::kRedStride;
@@ -585,7 +607,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
           e.aux_idx[(int64_t)red_row * e.ntiles + tile_n] = best.i;
         }
       }
-      store_tile<T, BN, KIND>(e, stage, C::kRows, n0, m0 + (int)rank * C::kRows, ok);
+      store_tile<T, BN, KIND, C::kRows>(e, stage, n0, m0 + (int)rank * C::kRows, ok, kv);
     }
     cluster_sync();   // peers have finished reading this CTA's partial tile
   }

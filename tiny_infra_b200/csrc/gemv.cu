@@ -28,6 +28,7 @@
 
 #include "capi_internal.h"
 #include "common.cuh"
+#include "int8_tile.cuh"
 #include "tcgen05.cuh"
 
 namespace ti {
@@ -54,33 +55,6 @@ struct Cfg {
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert((kXBytes + kRing) % 1024 == 0, "tile alignment");
 };
-
-// exact int8 -> 16-bit conversion of 8 values (see lmhead_i8.cu for the bit tricks)
-template <typename T>
-__device__ __forceinline__ uint4 cvt8(uint32_t lo, uint32_t hi) {
-  uint32_t o[4];
-  const uint32_t w[2] = {lo ^ 0x80808080u, hi ^ 0x80808080u};
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      float f[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        f[j] = __uint_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540u | j)) - 8388736.0f;
-      o[2 * i] = __byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632u);
-      o[2 * i + 1] = __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632u);
-    } else {
-      const __half2 bias = __halves2half2(__float2half(1152.f), __float2half(1152.f));
-      const uint32_t a = __byte_perm(w[i], 0x64646464u, 0x5140u);
-      const uint32_t b = __byte_perm(w[i], 0x64646464u, 0x5342u);
-      __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
-      __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
-      o[2 * i] = *reinterpret_cast<uint32_t*>(&ha);
-      o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hb);
-    }
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -169,33 +143,25 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
       }
     }
     __syncwarp();
-  } else if (I8 && warp >= 6) {
-    // converters: int8 stage g -> 16-bit tile g % CS in the canonical SWIZZLE_128B K-major layout
-    const int t = (int)threadIdx.x - 192;
-    for (int g = 0; g < total; ++g) {
-      const int s = g % S, c = g % CS;
-      if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (g / S) & 1, TI_DEVERR_GEMM_WAIT)))
-        break;
-      if (g >= CS && !__all_sync(0xffffffffu, mbar_wait(cempty0 + 8 * c, ((g / CS) & 1) ^ 1,
-                                                        TI_DEVERR_GEMM_WAIT)))
-        break;
-      const uint32_t qt = wbase + s * kW, ct = cbase + c * kWTile;
-#pragma unroll
-      for (int i = t; i < kBM * 8; i += 128) {
-        const int row = i >> 3, ch = i & 7;
-        uint32_t lo, hi;
-        asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi)
-                     : "r"(qt + row * kBK + ch * 8));
-        const uint4 v = cvt8<T>(lo, hi);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(ct + swz128(row, ch)),
-                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(empty0 + 8 * s);            // the int8 stage may be refilled
-        mbar_arrive(cfull0 + 8 * c);            // the converted tile is ready
+  } else if (warp >= 6) {   // int8 only (the 16-bit kernels have 6 warps)
+    if constexpr (I8) {
+      // converters: int8 stage g -> 16-bit tile g % CS in the canonical SWIZZLE_128B K-major layout
+      const int t = (int)threadIdx.x - 192;
+      for (int g = 0; g < total; ++g) {
+        const int s = g % S, c = g % CS;
+        if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (g / S) & 1, TI_DEVERR_GEMM_WAIT)))
+          break;
+        if (g >= CS && !__all_sync(0xffffffffu, mbar_wait(cempty0 + 8 * c, ((g / CS) & 1) ^ 1,
+                                                          TI_DEVERR_GEMM_WAIT)))
+          break;
+        const uint32_t qt = wbase + s * kW, ct = cbase + c * kWTile;
+        convert_int8_tile<T>(qt, ct, t);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(empty0 + 8 * s);            // the int8 stage may be refilled
+          mbar_arrive(cfull0 + 8 * c);            // the converted tile is ready
+        }
       }
     }
   } else if (warp == 1) {

@@ -12,8 +12,8 @@
 //   warp 0    TMA: per K block the activations (256 x 64 bf16, SWIZZLE_128B) and the int8 tile
 //             (128 rows x 64 bytes, row-major) into a 3-stage ring;
 //   warps 6-9 convert the int8 tile into the bf16 B tile in the canonical SWIZZLE_128B K-major
-//             layout (8 bytes -> one 16-byte chunk per item, conflict-free), fence the writes to
-//             the async proxy and arrive on the stage's "converted" barrier;
+//             layout (convert_int8_tile, int8_tile.cuh), fence the writes to the async proxy and
+//             arrive on the stage's "converted" barrier;
 //   warp 1    MMA: two tcgen05.mma M=128 N=128 (both 128-row halves of the tokens) per K step
 //             into one of two 256-column TMEM accumulator pairs, commits stages and buffers;
 //   warps 2-5 epilogue: tcgen05.ld, multiply by the tile's scales, (max, first argmax) per row
@@ -24,6 +24,7 @@
 
 #include "capi_internal.h"
 #include "common.cuh"
+#include "int8_tile.cuh"
 #include "tcgen05.cuh"
 
 namespace ti {
@@ -42,38 +43,6 @@ constexpr int kSmem = kRing + kBars + 1024;
 constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 static_assert(kStage % 1024 == 0, "stage alignment");
-
-// 8 int8 values (two 32-bit words) -> 8 elements of T packed as four 32-bit words, exactly and
-// with full-rate integer / float ops only (a per-element int -> float conversion instruction runs
-// on the slow conversion unit and made the converters the bottleneck).  u = byte ^ 0x80 is the
-// value + 128; bf16: the float32 with bits 0x4B000000 | u is 2^23 + u, minus 2^23 + 128 it is the
-// value, and a small integer's float32 has zero low 16 bits, so its high half is the bf16;
-// fp16: the half with bits 0x6400 | u is 1024 + u, minus 1152 (one packed subtraction).
-template <typename T>
-__device__ __forceinline__ uint4 convert8(uint32_t lo, uint32_t hi) {
-  uint32_t o[4];
-  const uint32_t w[2] = {lo ^ 0x80808080u, hi ^ 0x80808080u};
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      float f[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        f[j] = __uint_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540u | j)) - 8388736.0f;
-      o[2 * i] = __byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632u);
-      o[2 * i + 1] = __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632u);
-    } else {
-      const __half2 bias = __halves2half2(__float2half(1152.f), __float2half(1152.f));
-      const uint32_t a = __byte_perm(w[i], 0x64646464u, 0x5140u);
-      const uint32_t b = __byte_perm(w[i], 0x64646464u, 0x5342u);
-      __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
-      __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
-      o[2 * i] = *reinterpret_cast<uint32_t*>(&ha);
-      o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hb);
-    }
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
 
 __device__ __forceinline__ void fence_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -149,7 +118,7 @@ lmhead_argmax_i8_kernel(const __grid_constant__ CUtensorMap amap,
     }
     __syncwarp();
   } else if (warp >= 6) {
-    // converters: item i of a stage = (row i / 8, 8-byte chunk i % 8) of the int8 tile
+    // converters: the stage's int8 tile -> its bf16 / fp16 B tile
     const int t = (int)threadIdx.x - 192;
     int g = 0;
     bool ok = true;
@@ -163,17 +132,7 @@ lmhead_argmax_i8_kernel(const __grid_constant__ CUtensorMap amap,
         }
         const uint32_t bt = sbase + s * kStage + kABytes;
         const uint32_t qt = bt + kBBytes;
-#pragma unroll
-        for (int i = t; i < kBN * 8; i += 128) {
-          const int row = i >> 3, ch = i & 7;
-          uint32_t lo, hi;
-          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi)
-                       : "r"(qt + row * kBK + ch * 8));
-          const uint4 v = convert8<T>(lo, hi);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(bt + swz128(row, ch)),
-                       "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                       : "memory");
-        }
+        convert_int8_tile<T>(qt, bt, t);
         fence_async_shared();             // generic-proxy writes -> the tensor cores' reads
         __syncwarp();
         if (lane == 0) mbar_arrive(conv0 + 8 * s);
