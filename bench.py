@@ -539,6 +539,16 @@ def run_ours(a, rank, world, local):
         "device_status": status,
     }
     print(json.dumps(line), flush=True)
+    return _status_rc(status)
+
+
+def _status_rc(status: int) -> int:
+    """Exit code of a measured run: a kernel that raised a device status bit skipped work, so
+    its line is not a measurement."""
+    if status:
+        print(f"bench: device status 0x{status:x} raised during the run: the line above is "
+              "not a valid measurement", file=sys.stderr, flush=True)
+        return 1
     return 0
 
 
@@ -1112,7 +1122,7 @@ def run_long(a, rank, world, local):
                           "peak_gbs": peak, "peak_kind": peak_kind,
                           "frac": round(step_bytes / (tsecs / steps) / 1e9 / peak, 4)},
         "clocks": clocks, "device_status": status}), flush=True)
-    return 0
+    return _status_rc(status)
 
 
 def main():

@@ -116,6 +116,22 @@ int ti_paged_attention_decode_planned(void* out, int64_t out_seq_stride, const v
                                       int block_size, int max_blocks_per_seq, int dtype,
                                       void* workspace, size_t workspace_bytes, const void* plan,
                                       void* stream);
+/* The same with flags.  TI_ATTN_EARLY_KV: the caller guarantees that the plan, and every KV
+ * block of the batch except the last block of each sequence, were complete before the kernel
+ * that precedes this call on the stream started (in a decode step: the plan is written before
+ * layer 0 and only the new token's block changes); the kernel then loads the plan and starts
+ * streaming those blocks while that kernel still runs (programmatic dependent launch), and
+ * waits for it only before it reads q and the last blocks.  Results are identical to flags 0. */
+#define TI_ATTN_EARLY_KV 1
+int ti_paged_attention_decode_planned_ex(void* out, int64_t out_seq_stride, const void* q,
+                                         int64_t q_seq_stride, const void* k_cache,
+                                         const void* v_cache, int64_t num_blocks,
+                                         const int32_t* block_tables, int64_t bt_stride,
+                                         const int32_t* row_index, const int32_t* context_lens,
+                                         int batch, int num_heads, int num_kv_heads, int head_dim,
+                                         int block_size, int max_blocks_per_seq, int dtype,
+                                         void* workspace, size_t workspace_bytes,
+                                         const void* plan, int flags, void* stream);
 
 /* ---- paged decode attention without caller scratch ---------------------------------------------
  * No counterpart in the reference.  Same computation and arguments as

@@ -162,3 +162,126 @@ def test_v5_long_ranges(cuda_device, monkeypatch):
         want = (p @ vv).reshape(NH, D)
         err = (got5[b].float() - want).abs()
         assert (err <= 2e-3 + 2.0 ** -9 * want.abs()).all(), float(err.max())
+
+
+@pytest.mark.parametrize("case", [(11, 256, 128, 2048), (12, 32, 128, 2048), (13, 7, 1, 300)])
+def test_early_kv_after_qkv_append(cuda_device, case):
+    """TI_ATTN_EARLY_KV right behind the QKV GEMM that writes q and appends each sequence's new
+    token to its last block (the decode step's order): the attention streams the other blocks
+    while the GEMM runs and must still see the new q and the appended token.  Its output equals
+    the plain call's, run after a full synchronisation on the same q and pool, bit for bit."""
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    seed, B, lo, hi = case
+    NH, KVH, D, H = 14, 2, 64, 896
+    QKV = (NH + 2 * KVH) * D
+    rng = np.random.default_rng(seed)
+    ctx_np = rng.integers(lo, hi + 1, B).astype(np.int32)
+    nblk = (ctx_np + 15) // 16
+    NB = int(nblk.sum()) + 64
+    mb = (hi + 15) // 16
+    perm = rng.permutation(NB).astype(np.int32)
+    bt_np = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        bt_np[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += int(nblk[b])
+    last = ctx_np - 1
+    slots_np = bt_np[np.arange(B), last // 16].astype(np.int64) * 16 + last % 16
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(B, H, device=dev, generator=g).bfloat16()
+    w = (torch.randn(QKV, H, device=dev, generator=g) * 0.05).bfloat16()
+    bias = (torch.randn(QKV, device=dev, generator=g) * 0.1).bfloat16()
+    k = torch.randn(NB, KVH, 16, D, device=dev, generator=g).bfloat16()
+    v = torch.randn(NB, KVH, 16, D, device=dev, generator=g).bfloat16()
+    pos = torch.from_numpy(last).to(dev)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
+    ang = torch.arange(hi + 1, dtype=torch.float64)[:, None] * inv[None]
+    cos = ang.cos().float().to(dev).contiguous()
+    sin = ang.sin().float().to(dev).contiguous()
+    bt, ctx = torch.from_numpy(bt_np).to(dev), torch.from_numpy(ctx_np).to(dev)
+    slots = torch.from_numpy(slots_np).to(dev)
+    qkv = torch.zeros(B, QKV, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    need = lib.ti_paged_attention_workspace_bytes(B, NH, KVH, D, mb, 0)
+    ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    plan = torch.zeros(lib.ti_paged_attention_plan_bytes(B), dtype=torch.uint8, device=dev)
+    N.check(lib.ti_paged_attention_plan(bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), B, NH,
+                                        KVH, D, mb, NB, plan.data_ptr(), plan.numel(), s))
+    torch.cuda.synchronize()                 # the plan is final before the QKV GEMM starts
+
+    def args(out):
+        return [out.data_ptr(), NH * D, qkv.data_ptr(), QKV, k.data_ptr(), v.data_ptr(), NB,
+                bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), B, NH, KVH, D, 16, mb,
+                N.dtype_code(torch.bfloat16), ws.data_ptr(), need, plan.data_ptr()]
+
+    got = torch.full((B, NH * D), 3.0, dtype=torch.bfloat16, device=dev)
+    N.check(lib.ti_gemm_qkv_rope(x.data_ptr(), H, w.data_ptr(), H, bias.data_ptr(), B, H, NH, KVH,
+                                 D, qkv.data_ptr(), QKV, k.data_ptr(), v.data_ptr(),
+                                 slots.data_ptr(), cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
+                                 16, N.dtype_code(torch.bfloat16), s))
+    N.check(lib.ti_paged_attention_decode_planned_ex(*args(got), N.TI_ATTN_EARLY_KV, s))
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    ref = torch.full_like(got, 3.0)
+    N.check(lib.ti_paged_attention_decode(*args(ref)[:-3], 0, ws.data_ptr(), need, s))
+    torch.cuda.synchronize()
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    # a second, unsynchronised round (q and the appended token rewritten by a new GEMM input)
+    x2 = torch.randn(B, H, device=dev, generator=g).bfloat16()
+    got2 = torch.full_like(got, 3.0)
+    N.check(lib.ti_gemm_qkv_rope(x2.data_ptr(), H, w.data_ptr(), H, bias.data_ptr(), B, H, NH,
+                                 KVH, D, qkv.data_ptr(), QKV, k.data_ptr(), v.data_ptr(),
+                                 slots.data_ptr(), cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
+                                 16, N.dtype_code(torch.bfloat16), s))
+    N.check(lib.ti_paged_attention_decode_planned_ex(*args(got2), N.TI_ATTN_EARLY_KV, s))
+    ref2 = torch.full_like(got, 3.0)
+    torch.cuda.synchronize()
+    N.check(lib.ti_paged_attention_decode(*args(ref2)[:-3], 0, ws.data_ptr(), need, s))
+    torch.cuda.synchronize()
+    assert N.device_status() == 0
+    assert not torch.equal(got2.view(torch.int16), got.view(torch.int16))
+    assert torch.equal(ref2.view(torch.int16), got2.view(torch.int16))
+
+
+def test_small_batch_many_pieces(cuda_device):
+    """Four sequences of 20k-30k tokens: at small batches v5 cuts each (sequence, kv-head pair)
+    into up to 65 pieces so that the blocks spread over every SM, and the merge combines them in
+    rounds of 16.  Planned equals plain bit for bit, and every row agrees with an fp32 torch
+    reference (tolerance: 2e-3 + half a bf16 ulp of the reference); one row stops at a negative
+    block-table entry in its last round of pieces."""
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    B, NH, KVH, D = 4, 14, 2, 64
+    rng = np.random.default_rng(21)
+    ctx_np = rng.integers(20000, 30001, B).astype(np.int32)
+    nblk = (ctx_np + 15) // 16
+    NB = int(nblk.sum()) + 16
+    mb = int((30000 + 15) // 16)
+    perm = rng.permutation(NB).astype(np.int32)
+    bt_np = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        bt_np[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += int(nblk[b])
+    stop_at = int(nblk[2]) - 40                   # row 2 reads up to here (attention.cu:99)
+    bt_np[2, stop_at] = -1
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    q = torch.randn(B, NH, D, device=cuda_device, generator=g).bfloat16()
+    k = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    v = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    ref, got, _ = _plain_and_planned(lib, N, q, k, v, bt_np, ctx_np, mb)
+    assert N.device_status() == 0
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    for b in range(B):
+        n = int(ctx_np[b]) if b != 2 else stop_at * 16
+        nb = (n + 15) // 16
+        ids = torch.from_numpy(bt_np[b, :nb].astype(np.int64)).to(cuda_device)
+        kk = k[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        vv = v[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        qq = q[b].float().view(KVH, NH // KVH, D)
+        p = torch.softmax(qq @ kk.transpose(1, 2) / 8.0, dim=-1)
+        want = (p @ vv).reshape(NH, D)
+        err = (got[b].float() - want).abs()
+        assert (err <= 2e-3 + 2.0 ** -9 * want.abs()).all(), (b, float(err.max()))

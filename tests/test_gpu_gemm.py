@@ -93,12 +93,15 @@ def test_swiglu_epilogue(cuda_device, bn):
 @pytest.mark.parametrize("M,I,dt", [(256, 4864, "bf16"), (200, 4864, "bf16"),
                                     (100, 1032, "bf16"), (256, 1032, "bf16"),
                                     (4096, 4864, "bf16"), (300, 1032, "bf16"), (1, 4864, "bf16"),
-                                    (256, 4864, "fp16"), (4096, 1032, "fp16")])
+                                    (32, 4864, "bf16"), (37, 4864, "bf16"), (64, 4864, "fp16"),
+                                    (17, 1032, "bf16"), (256, 4864, "fp16"), (4096, 1032, "fp16")])
 def test_swiglu16_epilogue(cuda_device, M, I, dt):
     """gate/up + SwiGLU with gate/up rows interleaved in groups of 8 (TI_EPI_SWIGLU16), the
     model's layout: the library picks 80-, 144- or 256-wide tiles by M (80 at M <= 128 and
     2I = 2064: a ragged last tile of 64 columns; 144 at M = 200 / 256 and 2I = 9728: a last tile
-    of 80; 256 above 256 rows, ragged at 2I = 2064).  Output columns past I stay untouched."""
+    of 80; 256 above 256 rows, ragged at 2I = 2064).  At M <= 32 / 64 the activation box is 32 /
+    64 rows and the ring holds all 14 K blocks (the MMA's rows past M read the rest of the stage
+    and are dropped).  Output columns past I stay untouched."""
     from tiny_infra_b200 import _native as N_
     K = 896
     tdt = torch.bfloat16 if dt == "bf16" else torch.float16

@@ -269,5 +269,23 @@ __device__ __forceinline__ float4 ld_peer_f4(uint32_t addr) {
                : "memory");
   return v;
 }
+// Store to a CTA of this cluster (address from map_peer): fire-and-forget, made visible to the
+// owner by a release arrive / acquire wait on the cluster barrier.
+__device__ __forceinline__ void st_peer_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+// The two halves of the cluster barrier, for threads that have work between them.  Every thread
+// of every CTA of the cluster takes the same sequence of arrive / wait.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 }  // namespace ti

@@ -50,6 +50,10 @@
 #include "common.cuh"
 #include "tcgen05.cuh"
 
+#ifndef TI_RESIDUAL_TMA_REDUCE
+#define TI_RESIDUAL_TMA_REDUCE 1
+#endif
+
 namespace ti {
 namespace gemm {
 
@@ -326,10 +330,32 @@ struct KvSlots {
 // 128-byte row per token.  Fire-and-forget: the CTA does not wait for the writes.
 template <typename T, int BN, int KIND, int R>
 __device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int n0, int y0,
-                                           bool ok, const KvSlots<KIND, R>& kv) {
+                                           bool ok, const KvSlots<KIND, R>& kv,
+                                           const CUtensorMap* xmap) {
   using O = Out<T, BN, KIND>;
   constexpr int PB = O::kPanelBytes;
   constexpr int CPR = O::kBytes / 16;   // 16-byte chunks per staged row
+#if TI_RESIDUAL_TMA_REDUCE
+  if constexpr (KIND == TI_EPI_RESIDUAL) {
+    // The staged fp32 tile is R rows x 128-byte panels in the 128-byte swizzle: one bulk tensor
+    // reduce-add per panel (rows past M clipped by the tensor map) instead of a red.add per
+    // 16 bytes.  The staging writes are made visible to the async proxy first.
+    static_assert(PB == 128, "fp32 residual tiles stage 128-byte panels");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    epilogue_bar();
+    if (!ok || threadIdx.x != 64) return;
+#pragma unroll
+    for (int pnl = 0; pnl < O::kBytes / 128; ++pnl)
+      asm volatile(
+          "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+          " [%0, {%1, %2}], [%3];" ::"l"(reinterpret_cast<uint64_t>(xmap)),
+          "r"(n0 + pnl * 32), "r"(y0), "r"(stage + (uint32_t)(pnl * R * 128))
+          : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // shared memory read
+    return;
+  }
+#endif
   epilogue_bar();                       // the whole tile is staged
   if (!ok) return;
   const int t = (int)threadIdx.x - 64;
@@ -379,54 +405,78 @@ __device__ __forceinline__ void store_tile(const EpiArgs& e, uint32_t stage, int
   }
 }
 
-template <int BN, int STAGES, int CL>
+constexpr int kMaxSmem = 227 * 1024;
+
+// AR: activation rows loaded per stage.  Batches of at most 32 / 64 rows load 32 / 64 (the MMA
+// still reads 128 rows: the rows past AR come from the rest of the stage and are garbage that
+// only reaches accumulator rows >= M, which are never stored), so that a stage is small enough
+// for the ring to hold every K block of the tile at once.
+template <int BN, int STAGES, int CL, int AR = BM>
 struct Cfg {
-  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kABytes = AR * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
+  // the last stage's 128-row A read reaches this far past the ring
+  static constexpr int kAOver = (BM - AR) * BK * 2 > kBBytes ? (BM - AR) * BK * 2 - kBBytes : 0;
   static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  static constexpr int kRing = STAGES * kStage;
-  // split-K across a cluster of CL CTAs: each CTA leaves its fp32 partial tile in shared memory
-  // (over the drained stage ring, rows padded by 16 bytes against bank conflicts) and finishes
-  // BM / CL rows of the cluster's tile through distributed shared memory.
+  // mbarriers (full, empty per stage; accumulator) and the TMEM address slot (sized for STAGES,
+  // an upper bound of the ring depth)
+  static constexpr int kBarBytes = (2 * STAGES + 1) * 8 + 8;
+  // split-K across a cluster of CL CTAs: CTA r finishes rows r * BM / CL .. of the cluster's
+  // tile.  Every CTA pushes each row of its fp32 partial tile into the receive buffer of the
+  // CTA that finishes that row ([source rank][row][column], rows padded by 16 bytes against
+  // bank conflicts), so after one cluster barrier the owner sums the CL partials from its own
+  // shared memory.  The receive buffer lies beside the stage ring, because a peer may push
+  // while this CTA's MMAs still read the ring; the ring gives up stages to make room.
   static constexpr int kRedStride = BN + 4;
-  static constexpr int kRedBytes = CL > 1 ? BM * kRedStride * 4 : 0;
-  static constexpr int kStageOff = (kRedBytes + 1023) / 1024 * 1024;   // output staging
+  static constexpr int kRecvBytes = CL > 1 ? BM * kRedStride * 4 : 0;
+  static constexpr int kRecvOff = CL > 1 ? (kBarBytes + 127) / 128 * 128 : 0;   // after the ring
+  static constexpr int kStages =
+      CL > 1 ? (STAGES < (kMaxSmem - 1024 - kRecvOff - kRecvBytes) / kStage
+                    ? STAGES
+                    : (kMaxSmem - 1024 - kRecvOff - kRecvBytes) / kStage)
+             : STAGES;
+  static constexpr int kRing = kStages * kStage;
+  static constexpr int kStageOff = 0;              // output staging: the drained ring
   static constexpr int kRows = BM / CL;            // rows each CTA of the cluster finishes
   static constexpr int kW = BN / 2 / CL;           // chunk width per thread
-  // mbarriers (full, empty per stage; accumulator) and the TMEM address slot
-  static constexpr int kBarBytes = (2 * STAGES + 1) * 8 + 8;
   // The ring starts on a 1024-byte boundary (128-byte swizzle atoms); the barriers go into
-  // the alignment slack below it when that has room, else right after the ring.
-  static constexpr int kSmem = kRing + 1024;
+  // the alignment slack below it when that has room, else right after the ring (where the
+  // receive buffer leaves them kRecvOff bytes).
+  static constexpr int kSmem = kRing + 1024 + (CL > 1 ? kRecvOff + kRecvBytes : 0) + kAOver;
   static_assert(2 * kBarBytes <= 1024, "barriers fit beside the ring in the 1 KB slack");
   static_assert(CL == 1 || kW % 4 == 0, "cluster chunks must be multiples of 4 columns");
-  static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(kStages >= 2, "a ring of at least two stages");
+  static_assert(AR == BM || (CL == 1 && AR % 8 == 0 && kABytes % 1024 == 0),
+                "short activation boxes: unsplit tiles, 1024-byte aligned stages");
+  static_assert(kSmem <= kMaxSmem, "shared memory");
 };
 
-// Whether the cluster partials and the staged output tile fit the drained stage ring.
-template <typename T, int BN, int STAGES, int KIND, int CL>
+// Whether the staged output tile fits the drained stage ring.
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
 constexpr bool ring_fits() {
-  using C = Cfg<BN, STAGES, CL>;
+  using C = Cfg<BN, STAGES, CL, AR>;
   return C::kStageOff + C::kRows * Out<T, BN, KIND>::kBytes <= C::kRing;
 }
 
 // One 128 x BN output tile per cluster of CL CTAs (CL = split-K factor along grid z).
-template <typename T, int BN, int STAGES, int KIND, int CL>
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
-            int K, int kb_per_split, EpiArgs e) {
-  using C = Cfg<BN, STAGES, CL>;
-  static_assert(ring_fits<T, BN, STAGES, KIND, CL>(), "partials and staged tile fit the ring");
+            const __grid_constant__ CUtensorMap xmap, int K, int kb_per_split, EpiArgs e) {
+  using C = Cfg<BN, STAGES, CL, AR>;
+  constexpr int S = C::kStages;   // ring depth (a cluster kernel's receive buffer takes stages)
+  static_assert(ring_fits<T, BN, STAGES, KIND, CL, AR>(), "staged tile fits the ring");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* bars = (smem - smem_raw >= C::kBarBytes) ? smem_raw : smem + C::kRing;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t full0 = smem_u32(bars);
-  const uint32_t empty0 = full0 + STAGES * 8;
-  const uint32_t accum = empty0 + STAGES * 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + (2 * STAGES + 1) * 8);
+  const uint32_t empty0 = full0 + S * 8;
+  const uint32_t accum = empty0 + S * 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + (2 * S + 1) * 8);
+  const uint32_t recv = sbase + C::kRing + C::kRecvOff;   // cluster receive buffer (CL > 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_n = blockIdx.x;
@@ -438,7 +488,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int s = 0; s < STAGES; ++s) {
+      for (int s = 0; s < S; ++s) {
         mbar_init(full0 + 8 * s, 1);
         mbar_init(empty0 + 8 * s, 1);
       }
@@ -456,6 +506,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   const uint32_t tmem = *tmem_slot;
   // All on-chip resources are held: the next kernel may be scheduled.
   pdl_launch_dependents();
+  // Cluster barrier phase 1 (arrive now, wait before the first push): every CTA of the
+  // cluster has started, so its shared memory may be written.
+  if constexpr (CL > 1) cluster_arrive_relaxed();
 
   // split-K: the row / columns this thread finishes after the cluster reduction
   const int red_t = (int)threadIdx.x - 64;
@@ -472,8 +525,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(BN, std::is_same<T, __nv_bfloat16>::value);
       for (int it = 0; it < nk; ++it) {
-        const int s = it % STAGES;
-        if (!mbar_wait(full0 + 8 * s, (it / STAGES) & 1, TI_DEVERR_GEMM_WAIT)) break;
+        const int s = it % S;
+        if (!mbar_wait(full0 + 8 * s, (it / S) & 1, TI_DEVERR_GEMM_WAIT)) break;
         tc_fence_after();
         const uint32_t sa = sbase + s * C::kStage;
         const uint64_t da = smem_desc(sa), db = smem_desc(sa + C::kABytes);
@@ -490,16 +543,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     // (one issuing thread's loads complete one after another, the streams overlap).  The empty
     // barrier waits are parity waits: a producer about to refill a stage for its u-th use must
     // know that use u - 2 was consumed, which holds when its own previous K block (kProd
-    // earlier) waited for a consumption at least STAGES - kProd blocks later than that use,
-    // hence kProd <= STAGES.
-    constexpr int kProd = STAGES < 4 ? STAGES : 4;
+    // earlier) waited for a consumption at least S - kProd blocks later than that use,
+    // hence kProd <= S.
+    constexpr int kProd = S < 4 ? S : 4;
     if (lane == 0 && warp - 2 < kProd) {
       const int p = warp - 2;
       const uint64_t pol_a = l2_policy_evict_last();    // activations: re-read by many CTAs
       const uint64_t pol_b = l2_policy_evict_first();   // weights: streamed once
       // Weights do not depend on earlier kernels: fetch the first stages' B tiles before
       // waiting for the producer of the activations.
-      const int pre_n = min(nk, STAGES);
+      const int pre_n = min(nk, S);
       for (int it = p; it < pre_n; it += kProd) {
         mbar_arrive_expect_tx(full0 + 8 * it, C::kStage);
         tma_load_2d_hint(sbase + it * C::kStage + C::kABytes, &bmap, full0 + 8 * it,
@@ -510,8 +563,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
         tma_load_2d_hint(sbase + it * C::kStage, &amap, full0 + 8 * it, (kb0 + it) * BK, m0, pol_a);
       for (int it = p; it < nk; it += kProd) {
         if (it < pre_n) continue;
-        const int s = it % STAGES;
-        if (!mbar_wait(empty0 + 8 * s, ((it / STAGES) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
+        const int s = it % S;
+        if (!mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
         mbar_arrive_expect_tx(full0 + 8 * s, C::kStage);
         const uint32_t sa = sbase + s * C::kStage;
         const int kx = (kb0 + it) * BK;
@@ -553,12 +606,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
           }
         }
       }
-      store_tile<T, BN, KIND, BM>(e, sbase, n0, m0, ok && nk > 0, kv);
+      store_tile<T, BN, KIND, BM>(e, sbase, n0, m0, ok && nk > 0, kv, &xmap);
     } else {
-      // this CTA's fp32 partial tile -> shared memory (zeros for an empty split)
-      float* red = reinterpret_cast<float*>(smem) + (quad * 32 + lane) * C::kRedStride;
+      // this CTA's fp32 partial tile (zeros for an empty split), row by row, into the receive
+      // buffer of the CTA that finishes the row: slot [this rank][row % kRows]
+      cluster_wait_acquire();   // phase 1: every CTA of the cluster has started
+      const int lr = quad * 32 + lane;
+      const uint32_t dst = map_peer(
+          recv + (uint32_t)(((int)rank * C::kRows + lr % C::kRows) * C::kRedStride) * 4u,
+          (uint32_t)(lr / C::kRows));
+      // a warp whose 32 rows all lie past M pushes nothing (their sums are never stored)
+      const bool rows_live = m0 + quad * 32 < e.M;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < (rows_live ? BN : 0); c += 32) {
         float v[32];
         if (ok && nk > 0) {
           tmem_ld32(trow + c, v);
@@ -568,27 +628,31 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
         }
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(red + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          st_peer_f4(dst + 4u * (uint32_t)(c + i), v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
     }
   }
   if constexpr (CL > 1) {
-    cluster_sync();   // every partial tile of the cluster is in shared memory
+    if (warp < 2) cluster_wait_acquire();   // phase 1 (the epilogue warps took it above)
+    // phase 2: every partial of the rows this CTA finishes is in its receive buffer
+    cluster_arrive_release();
+    cluster_wait_acquire();
     if (warp >= 2) {
       float lo[C::kW], hi[C::kW];
 #pragma unroll
       for (int i = 0; i < C::kW; ++i) lo[i] = hi[i] = 0.f;
-      const uint32_t mine =
-          sbase + (uint32_t)(((int)rank * C::kRows + red_lr) * C::kRedStride + red_c) * 4u;
+      const uint32_t mine = recv + (uint32_t)(red_lr * C::kRedStride + red_c) * 4u;
 #pragma unroll
       for (int src = 0; src < CL; ++src) {   // fixed order: the sum is deterministic
-        const uint32_t a = map_peer(mine, (uint32_t)src);
+        const uint32_t a = mine + (uint32_t)(src * C::kRows * C::kRedStride) * 4u;
 #pragma unroll
         for (int i = 0; i < C::kW; i += 4) {
-          const float4 x = ld_peer_f4(a + 4u * i);
-          const float4 y = ld_peer_f4(a + 4u * (BN / 2 + i));
-          lo[i] += x.x; lo[i + 1] += x.y; lo[i + 2] += x.z; lo[i + 3] += x.w;
-          hi[i] += y.x; hi[i + 1] += y.y; hi[i + 2] += y.z; hi[i + 3] += y.w;
+          const uint4 x = ld_shared_v4(a + 4u * i);
+          const uint4 y = ld_shared_v4(a + 4u * (BN / 2 + i));
+          lo[i] += __uint_as_float(x.x); lo[i + 1] += __uint_as_float(x.y);
+          lo[i + 2] += __uint_as_float(x.z); lo[i + 3] += __uint_as_float(x.w);
+          hi[i] += __uint_as_float(y.x); hi[i + 1] += __uint_as_float(y.y);
+          hi[i + 2] += __uint_as_float(y.z); hi[i + 3] += __uint_as_float(y.w);
         }
       }
       Best best{-INFINITY, 0x7fffffff};
@@ -607,9 +671,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
           e.aux_idx[(int64_t)red_row * e.ntiles + tile_n] = best.i;
         }
       }
-      store_tile<T, BN, KIND, C::kRows>(e, stage, n0, m0 + (int)rank * C::kRows, ok, kv);
+      store_tile<T, BN, KIND, C::kRows>(e, stage, n0, m0 + (int)rank * C::kRows, ok, kv, &xmap);
     }
-    cluster_sync();   // peers have finished reading this CTA's partial tile
+    // no closing cluster barrier: after phase 2 no CTA touches another's shared memory
   }
   tc_fence_before();
   __syncthreads();
@@ -845,14 +909,16 @@ static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols
   return tile_map(m, p, tma_type(dtype), rows, cols, ld * 2, BK, box_rows);
 }
 
-template <typename T, int BN, int STAGES, int KIND, int CL>
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
 static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                     const EpiArgs& e, cudaStream_t s, int zsplits = 1) {
-  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL>()) {
+  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL, AR>()) {
     return set_error(TI_ERR_UNSUPPORTED, "gemm: this tile width and epilogue do not fit the stage ring");
   } else {
-    using C = Cfg<BN, STAGES, CL>;
-    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL>;
+    using C = Cfg<BN, STAGES, CL, AR>;
+    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL, AR>;
+    if (AR < BM && M > AR)
+      return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: short activation box for a taller batch");
     static int set_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -865,7 +931,15 @@ static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, 
     const int zs = CL > 1 ? CL : zsplits;
     const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
-    return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, K, per, e);
+    // residual: tensor map over x (fp32) for the bulk reduce-add of staged tiles
+    CUtensorMap xm = am;
+    if constexpr (KIND == TI_EPI_RESIDUAL && TI_RESIDUAL_TMA_REDUCE) {
+      const int rc = tile_map(&xm, e.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, M, N, e.ldo * 4, 32,
+                              C::kRows);
+      if (rc) return rc;
+    }
+    return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, xm,
+                         K, per, e);
   }
 }
 
@@ -1015,9 +1089,18 @@ static int swiglu16_bn(int M, int N) {
   }
   return 256;
 }
+// Rows of the activation box for an M-row SwiGLU16 GEMM: 32 / 64 when the batch fits and the
+// whole hidden size (K <= 896, 14 K blocks) then fits the deeper ring, else BM.
+static int swiglu16_box_rows(int M, int K, int bn) {
+  if (bn != 80 || K > 896) return BM;
+  return M <= 32 ? 32 : M <= 64 ? 64 : BM;
+}
 template <typename T>
 static int launch_swiglu16(int bn, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
                            int K, const EpiArgs& e, cudaStream_t s) {
+  const int ar = swiglu16_box_rows(M, K, bn);
+  if (ar == 32) return launch_t<T, 80, 14, TI_EPI_SWIGLU16, 1, 32>(am, bm, M, N, K, e, s);
+  if (ar == 64) return launch_t<T, 80, 12, TI_EPI_SWIGLU16, 1, 64>(am, bm, M, N, K, e, s);
   switch (bn) {
     case 80: return launch_t<T, 80, TI_GEMM_STAGES_80, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s);
     case 144: return launch_t<T, 144, TI_GEMM_STAGES_144, TI_EPI_SWIGLU16, 1>(am, bm, M, N, K, e, s);
@@ -1089,7 +1172,8 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
                ? gemm::launch_lmhead_argmax<__nv_bfloat16>(am, bm, M, N, K, aux_val, aux_idx, s)
                : gemm::launch_lmhead_argmax<__half>(am, bm, M, N, K, aux_val, aux_idx, s);
   }
-  rc = gemm::operand_map(&am, A, M, K, lda, gemm::BM, dtype);
+  const int a_rows = epilogue == TI_EPI_SWIGLU16 ? gemm::swiglu16_box_rows(M, K, block_n) : gemm::BM;
+  rc = gemm::operand_map(&am, A, M, K, lda, a_rows, dtype);
   if (rc) return rc;
   rc = gemm::operand_map(&bm, B, N, K, ldb, block_n, dtype);
   if (rc) return rc;

@@ -14,14 +14,16 @@
 // engine/scheduler.py:153): persistent over the vocab's 128-row tiles, per tile and token the
 // (max, first argmax) over the tile's rows, into the same [tokens, tiles] partials as the GEMM's
 // TI_EPI_ARGMAX (ti_argmax_finish reduces them).  bf16 / fp16 weights, or weight-only int8 with a
-// float32 scale per row (converted exactly to bf16 / fp16 in shared memory by four converter
-// warps, as in lmhead_i8.cu).
+// float32 scale per row: four converter warps turn each streamed int8 tile (TMA, 64-byte
+// swizzle) exactly into bf16 / fp16, one weight row per thread, and store it into tensor memory,
+// from where the MMA reads it as its A operand -- the 16-bit tile never passes through shared
+// memory, whose bandwidth the earlier shared-memory conversion exhausted.
 //   warp 0    TMA: the tokens (once, after the wait on the previous kernel) and the weight tiles
 //             (the first stages before that wait: weights are no earlier kernel's output);
 //   warp 1    MMA (M=128, N=NP, K=16 per instruction) into one of two TMEM accumulators;
 //   warps 2-5 epilogue: tcgen05.ld, scale (int8), per token a warp max / first argmax over its 32
 //             rows by shuffles and over the 4 warps through shared memory;
-//   warps 6-9 int8 only: converters.
+//   warps 6-9 int8 only: converters (shared-memory int8 stage -> tensor-memory A slot).
 // Every wait is bounded (TI_DEVERR_GEMM_WAIT on expiry, then the kernel winds down).
 #include <algorithm>
 #include <type_traits>
@@ -44,16 +46,22 @@ struct Cfg {
   static constexpr int kMaxK = 896;                           // tokens held for K <= 896
   static constexpr int kXBytes = kMaxK / kBK * NP * 128;      // the resident token tiles
   // weight tiles in flight (int8: 8 KB each, so more of them for the same bytes in flight)
-  static constexpr int kStages = I8 ? (NP <= 32 ? 14 : 7) : 6;
-  static constexpr int kConv = I8 ? 3 : 0;                    // converted 16-bit tiles (int8)
-  static constexpr int kRing = kStages * (I8 ? kQTile : kWTile) + kConv * kWTile;
+  static constexpr int kStages = I8 ? (NP <= 32 ? 20 : 13) : 6;
+  // int8: converted 16-bit weight tiles live in tensor memory (the MMA's A operand), kConv
+  // slots of 32 columns (64 K elements) after the two accumulators
+  static constexpr int kConv = I8 ? 4 : 0;
+  static constexpr int kRing = kStages * (I8 ? kQTile : kWTile);
   static constexpr int kRed = 4 * NP * 8;                     // (max, argmax) per warp, token
   static constexpr int kBars = (2 * kStages + 2 * kConv + 1 + 4) * 8 + 8;
   static constexpr int kSmem = kXBytes + kRing + kRed + kBars + 1024;
-  static constexpr int kTmemCols = NP <= 16 ? 32 : 2 * NP;    // two accumulators, power of 2
+  static constexpr int kAccCols = NP <= 16 ? 32 : 2 * NP;     // two accumulators
+  static constexpr int kUsedCols = kAccCols + kConv * (kBK / 2);
+  static constexpr int kTmemCols = kUsedCols <= 32 ? 32 : kUsedCols <= 64 ? 64
+                                 : kUsedCols <= 128 ? 128 : kUsedCols <= 256 ? 256 : 512;
   static constexpr int kThreads = I8 ? 320 : 192;
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert((kXBytes + kRing) % 1024 == 0, "tile alignment");
+  static_assert(kUsedCols <= 512, "tensor memory");
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -73,13 +81,13 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
                                              ~uintptr_t(1023));
   const uint32_t xbase = smem_u32(smem);
   const uint32_t wbase = xbase + C::kXBytes;                 // streamed stages
-  const uint32_t cbase = wbase + S * kW;                     // converted tiles (int8)
   float2* red = reinterpret_cast<float2*>(smem + C::kXBytes + C::kRing);
   uint8_t* bars = smem + C::kXBytes + C::kRing + C::kRed;
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + S * 8;
   const uint32_t cfull0 = empty0 + S * 8;                    // converted tile ready (int8)
   const uint32_t cempty0 = cfull0 + CS * 8;                  // converted tile consumed (int8)
+  // (int8) tensor-memory column of converted slot c: C::kAccCols + c * kBK / 2
   const uint32_t xfull = cempty0 + CS * 8;
   const uint32_t accf0 = xfull + 8;
   const uint32_t acce0 = accf0 + 2 * 8;
@@ -145,8 +153,10 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
     __syncwarp();
   } else if (warp >= 6) {   // int8 only (the 16-bit kernels have 6 warps)
     if constexpr (I8) {
-      // converters: int8 stage g -> 16-bit tile g % CS in the canonical SWIZZLE_128B K-major layout
-      const int t = (int)threadIdx.x - 192;
+      // converters: thread = weight row (the TMEM lane its warp may access: warp w reaches lanes
+      // 32 (w % 4) ..); its 64 int8 of stage g -> 32 columns of tensor-memory slot g % CS
+      const int r = (warp & 3) * 32 + lane;
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
       for (int g = 0; g < total; ++g) {
         const int s = g % S, c = g % CS;
         if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (g / S) & 1, TI_DEVERR_GEMM_WAIT)))
@@ -154,13 +164,16 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
         if (g >= CS && !__all_sync(0xffffffffu, mbar_wait(cempty0 + 8 * c, ((g / CS) & 1) ^ 1,
                                                           TI_DEVERR_GEMM_WAIT)))
           break;
-        const uint32_t qt = wbase + s * kW, ct = cbase + c * kWTile;
-        convert_int8_tile<T>(qt, ct, t);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_after();
+        uint32_t w[32];
+        convert_int8_row<T>(wbase + s * kW, r, w);
+        tmem_st32_u(tmem + lane_base + (uint32_t)(C::kAccCols + c * (kBK / 2)), w);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(empty0 + 8 * s);            // the int8 stage may be refilled
-          mbar_arrive(cfull0 + 8 * c);            // the converted tile is ready
+          mbar_arrive(cfull0 + 8 * c);            // the converted slot is ready
         }
       }
     }
@@ -177,23 +190,26 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * NP);
         for (int kb = 0; kb < nkb; ++kb, ++g) {
-          uint32_t wt;
+          const uint64_t db = smem_desc(xbase + kb * NP * 128);
           if constexpr (I8) {
             const int c = g % CS;
             if (!mbar_wait(cfull0 + 8 * c, (g / CS) & 1, TI_DEVERR_GEMM_WAIT)) { ok = false; break; }
-            wt = cbase + c * kWTile;
+            tc_fence_after();
+            const uint32_t ta = tmem + (uint32_t)(C::kAccCols + c * (kBK / 2));
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)   // 16 K elements = 8 columns of A
+              tc_mma_tmem_a(d, ta + 8 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_commit(cempty0 + 8 * c);
           } else {
             const int s = g % S;
             if (!mbar_wait(full0 + 8 * s, (g / S) & 1, TI_DEVERR_GEMM_WAIT)) { ok = false; break; }
-            wt = wbase + s * kWTile;
-          }
-          tc_fence_after();
-          const uint64_t da = smem_desc(wt), db = smem_desc(xbase + kb * NP * 128);
+            tc_fence_after();
+            const uint64_t da = smem_desc(wbase + s * kWTile);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            tc_mma(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          if constexpr (I8) tc_commit(cempty0 + 8 * (g % CS));
-          else tc_commit(empty0 + 8 * (g % S));
+            for (int k = 0; k < kBK / 16; ++k)
+              tc_mma(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_commit(empty0 + 8 * s);
+          }
         }
         tc_commit(accf0 + 8 * b);
       }
@@ -300,7 +316,7 @@ int gemv_argmax(const void* A, int64_t lda, const void* B, int64_t ldb, bool int
     cuuint32_t es[2] = {1, 1};
     int rc = encode_tensor_map_2d(&wm, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : ty,
                                   const_cast<void*>(B), dims, strides, box, es,
-                                  int8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                                  int8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (rc) return rc;
   }

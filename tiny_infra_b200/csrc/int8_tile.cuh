@@ -1,9 +1,11 @@
-// Exact int8 -> bf16 / fp16 conversion of a weight tile in shared memory, for the weight-only int8
-// lm_head kernels (lmhead_i8.cu, gemv.cu).
+// Exact int8 -> bf16 / fp16 conversion of weight tiles, for the weight-only int8 lm_head
+// kernels: a whole tile into a 16-bit shared-memory tile (lmhead_i8.cu), or one row per thread
+// into registers for tensor memory (gemv.cu).
 //
-// Input: a 128-row x 64-byte int8 tile as TMA writes it without swizzle (row pitch 64 bytes).
-// Output: the same 128 x 64 values as 16-bit elements in the canonical SWIZZLE_128B K-major
-// layout the tcgen05 shared-memory descriptors read (128-byte rows, 1024-byte aligned base).
+// convert_int8_tile -- input: a 128-row x 64-byte int8 tile as TMA writes it without swizzle
+// (row pitch 64 bytes); output: the same 128 x 64 values as 16-bit elements in the canonical
+// SWIZZLE_128B K-major layout the tcgen05 shared-memory descriptors read (128-byte rows,
+// 1024-byte aligned base).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -73,6 +75,27 @@ __device__ __forceinline__ void convert_int8_tile(uint32_t q, uint32_t c, int t)
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(c + swz128(row, 2 * p + 1)),
                  "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
                  : "memory");
+  }
+}
+
+// One row of a 128-row x 64-byte int8 tile that TMA wrote with the 64-byte swizzle (16-byte
+// chunk c of row r at chunk c ^ ((r >> 1) & 3)) -> its 64 values as 32 words of two 16-bit
+// elements, lower K index in the low half (the layout of a K-major A tile in tensor memory).
+// Eight consecutive rows read eight distinct 16-byte bank groups: conflict-free.
+template <typename T>
+__device__ __forceinline__ void convert_int8_row(uint32_t tile, int r, uint32_t (&out)[32]) {
+  uint32_t v[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[c][0]), "=r"(v[c][1]), "=r"(v[c][2]), "=r"(v[c][3])
+                 : "r"(tile + (uint32_t)r * 64u + ((uint32_t)(c ^ ((r >> 1) & 3)) << 4)));
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 a = convert8<T>(v[c][0], v[c][1]);
+    const uint4 b = convert8<T>(v[c][2], v[c][3]);
+    out[8 * c + 0] = a.x; out[8 * c + 1] = a.y; out[8 * c + 2] = a.z; out[8 * c + 3] = a.w;
+    out[8 * c + 4] = b.x; out[8 * c + 5] = b.y; out[8 * c + 6] = b.z; out[8 * c + 7] = b.w;
   }
 }
 

@@ -76,6 +76,8 @@ struct Params {
   int32_t* ws_count;        // [B, KVH]
   int32_t* ws_pieces;       // [B, KVH] v4: pieces of each unit (written by its first piece)
   const int32_t* plan;      // v5: the batch's stream resolved once (ti_paged_attention_plan)
+  int early;                // v5 planned: plan and all but each unit's last block are final
+                            // before the previous kernel (TI_ATTN_EARLY_KV)
 };
 
 // SM count of the current device (the persistent kernels' grid), cached per device.
@@ -1335,41 +1337,53 @@ merge_pieces_kernel(Params p, int units, int nheads) {
   const int row = pair / units, unit = pair % units;
   const int h = threadIdx.x >> 4, d4 = threadIdx.x & 15;
   if (h >= nheads) return;
-  const int ctx = p.context_lens[row];      // both loads in one round trip
-  const int pieces = p.ws_pieces[pair];
-  if (ctx <= 0 || pieces <= 1) return;   // no blocks (row left untouched) or not split
   const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
   const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
-  // Rounds of kRound pieces, all of a round's partials loaded together (one round for up to 16
-  // pieces, as many as the decode step's units have); pieces are used up to and including the
-  // first that stopped at a negative block-table entry, and each round's maximum rescales the
-  // running sums (online softmax over the pieces).
-  constexpr int kRound = 16;
+  // Rounds of kRound pieces, all of a round's partials loaded together (one round for the
+  // pieces a decode step's unit usually has); pieces are used up to and including the first
+  // that stopped at a negative block-table entry, and each round's maximum rescales the running
+  // sums (online softmax over the pieces).  The first round's slots (within the unit's
+  // max_parts slots, whatever the piece count) are loaded together with the context length and
+  // the piece count: one round trip; slots past the count are dropped.  (8 slots a round keep
+  // the kernel at two CTAs per SM: 256 sequences' merges in one wave.)
+  constexpr int kRound = 8;
+  int st[kRound];
+  float2 ml[kRound];
+  float4 v[kRound];
+#pragma unroll
+  for (int i = 0; i < kRound; ++i) {
+    if (i < p.max_parts) {
+      st[i] = stops[i];
+      ml[i] = reinterpret_cast<const float2*>(p.ws_ml)[base + i];
+      v[i] = reinterpret_cast<const float4*>(p.ws_o + (base + i) * 64)[d4];
+    }
+  }
+  const int ctx = p.context_lens[row];
+  const int pieces = min(p.ws_pieces[pair], p.max_parts);
+  if (ctx <= 0 || pieces <= 1) return;   // no blocks (row left untouched) or not split
   int use = pieces;
   float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int q0 = 0; q0 < use; q0 += kRound) {
-    int st[kRound];
-    float2 ml[kRound];
-    float4 v[kRound];
 #pragma unroll
     for (int i = 0; i < kRound; ++i) {
       const int q = q0 + i;
-      if (q < use) {
+      if (q0 > 0 && q < use) {
         st[i] = stops[q];
         ml[i] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
         v[i] = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64)[d4];
-      } else {
+      } else if (q >= use) {
         st[i] = 0;
         ml[i] = make_float2(-INFINITY, 0.f);
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
     int n = min(kRound, use - q0);          // this round's pieces, up to the first stop
+    bool stopped = false;
 #pragma unroll
     for (int i = kRound - 1; i >= 0; --i)
-      if (i < n && st[i]) n = i + 1;
-    use = min(use, q0 + n);
+      if (i < n && st[i]) { n = i + 1; stopped = true; }
+    if (stopped) use = q0 + n;              // no later round: the stop ends the unit's pieces
     float Mr = M;
 #pragma unroll
     for (int i = 0; i < kRound; ++i)
@@ -1387,6 +1401,96 @@ merge_pieces_kernel(Params p, int units, int nheads) {
     }
     M = Mr;
   }
+  const float inv = 1.f / L;               // L == 0 -> NaN (attention.cu:150)
+  T* dst = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride +
+           (int64_t)(unit * nheads + h) * 64 + d4 * 4;
+  uint2 u;
+  u.x = Elem<T>::pack2(acc.x * inv, acc.y * inv);
+  u.y = Elem<T>::pack2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+// Merge for units cut into more than 16 pieces (small batches): one CTA per (sequence, unit,
+// query head of the unit), 16 threads per 4 dims, each taking every 16th piece, so that all of
+// a unit's partials (up to kV5MaxPiecesSmall) arrive in one round of loads instead of rounds of
+// 16.  Pieces are used up to and including the first that stopped at a negative block-table
+// entry; each thread folds its pieces into (max, sum, O) and the 16 are combined by shuffles in
+// a fixed tree (deterministic).
+constexpr int kWideLanes = 16;
+constexpr int kWidePer = (kV5MaxPiecesSmall + kWideLanes - 1) / kWideLanes;   // pieces / thread
+template <typename T>
+__global__ void __launch_bounds__(256)
+merge_pieces_wide_kernel(Params p, int units, int nheads) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pair = blockIdx.x, h = blockIdx.y;
+  const int row = pair / units, unit = pair % units;
+  const int d4 = threadIdx.x >> 4, j = threadIdx.x & 15;   // the 16 piece lanes are adjacent
+  const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
+  const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
+  int st[kWidePer];
+  float2 ml[kWidePer];
+  float4 v[kWidePer];
+  // every slot of the unit (max_parts of them) loaded with the context length and the piece
+  // count in one round trip; slots past the count are dropped
+#pragma unroll
+  for (int i = 0; i < kWidePer; ++i) {
+    const int q = j + kWideLanes * i;
+    if (q < p.max_parts) {
+      st[i] = stops[q];
+      ml[i] = reinterpret_cast<const float2*>(p.ws_ml)[base + q];
+      v[i] = reinterpret_cast<const float4*>(p.ws_o + (base + q) * 64)[d4];
+    }
+  }
+  const int ctx = p.context_lens[row];
+  const int pieces = min(p.ws_pieces[pair], p.max_parts);
+  if (ctx <= 0 || pieces <= 1) return;   // whole CTA: no blocks, or the unit was not split
+  int first_stop = pieces;               // index of this thread's first stopped piece
+#pragma unroll
+  for (int i = 0; i < kWidePer; ++i) {
+    if (j + kWideLanes * i >= pieces) {
+      st[i] = 0;
+      ml[i] = make_float2(-INFINITY, 0.f);
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int i = kWidePer - 1; i >= 0; --i)
+    if (st[i] && j + kWideLanes * i < first_stop) first_stop = j + kWideLanes * i;
+#pragma unroll
+  for (int o = 1; o < kWideLanes; o <<= 1)
+    first_stop = min(first_stop, __shfl_xor_sync(0xffffffffu, first_stop, o));
+  float M = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kWidePer; ++i)
+    if (j + kWideLanes * i <= first_stop) M = fmaxf(M, ml[i].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kWidePer; ++i) {
+    if (j + kWideLanes * i <= first_stop && ml[i].x != -INFINITY) {
+      const float f = fast_exp2(ml[i].x - M);
+      L += ml[i].y * f;
+      acc.x += f * v[i].x; acc.y += f * v[i].y; acc.z += f * v[i].z; acc.w += f * v[i].w;
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < kWideLanes; o <<= 1) {   // combine the 16 lanes' (M, L, acc)
+    const float Mo = __shfl_xor_sync(0xffffffffu, M, o);
+    const float Lo = __shfl_xor_sync(0xffffffffu, L, o);
+    const float ax = __shfl_xor_sync(0xffffffffu, acc.x, o);
+    const float ay = __shfl_xor_sync(0xffffffffu, acc.y, o);
+    const float az = __shfl_xor_sync(0xffffffffu, acc.z, o);
+    const float aw = __shfl_xor_sync(0xffffffffu, acc.w, o);
+    const float Mn = fmaxf(M, Mo);
+    const float fa = M == -INFINITY ? 0.f : fast_exp2(M - Mn);
+    const float fb = Mo == -INFINITY ? 0.f : fast_exp2(Mo - Mn);
+    L = L * fa + Lo * fb;
+    acc.x = acc.x * fa + ax * fb; acc.y = acc.y * fa + ay * fb;
+    acc.z = acc.z * fa + az * fb; acc.w = acc.w * fa + aw * fb;
+    M = Mn;
+  }
+  if (j != 0) return;
   const float inv = 1.f / L;               // L == 0 -> NaN (attention.cu:150)
   T* dst = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride +
            (int64_t)(unit * nheads + h) * 64 + d4 * 4;
@@ -1484,8 +1588,14 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
   }
-  pdl_wait();
-  pdl_launch_dependents();
+  // early (TI_ATTN_EARLY_KV): the plan and all blocks but each unit's last are final before
+  // the previous kernel started, so the plan load and the producer's first loads run before the
+  // wait for it; every thread waits before it reads q or a unit's last block, or writes.
+  const bool early = PLANNED && p.early;
+  if (!early) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   using C = CfgV5;
   constexpr int kSlots = kV5Pairs * kV5Stages;
   extern __shared__ uint8_t smem_raw[];
@@ -1519,17 +1629,19 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
         reinterpret_cast<const uint8_t*>(pl) + plan_vtok_byte(batch, gridDim.x) +
         (int64_t)blockIdx.x * kV5IdCap);
     constexpr int n_ids = kV5FirstRound / 4, n_vt = kV5FirstRound / 16;
+    // L2-coherent loads (ld.global.cg): an early call reads the plan before its wait
     for (int i = tid; i < n_off + n_ids + n_vt; i += kV5Threads) {
-      if (i < n_off) reinterpret_cast<int4*>(s_off)[i] = g_off[i];
-      else if (i < n_off + n_ids) reinterpret_cast<int4*>(ids)[i - n_off] = g_ids[i - n_off];
-      else reinterpret_cast<int4*>(vtok)[i - n_off - n_ids] = g_vt[i - n_off - n_ids];
+      if (i < n_off) reinterpret_cast<int4*>(s_off)[i] = __ldcg(g_off + i);
+      else if (i < n_off + n_ids) reinterpret_cast<int4*>(ids)[i - n_off] = __ldcg(g_ids + i - n_off);
+      else reinterpret_cast<int4*>(vtok)[i - n_off - n_ids] = __ldcg(g_vt + i - n_off - n_ids);
     }
     if (tid == 0) {
-      const bool ok = pl[3] == batch && pl[2] == (int)gridDim.x * kV5Pairs &&
-                      pl[1] > 0 && (int64_t)pl[1] * kV5Pairs <= kV5IdCap;
+      const int4 h = __ldcg(reinterpret_cast<const int4*>(pl));
+      const bool ok = h.w == batch && h.z == (int)gridDim.x * kV5Pairs &&
+                      h.y > 0 && (int64_t)h.y * kV5Pairs <= kV5IdCap;
       if (!ok) raise_device_error(TI_DEVERR_ATTN_PLAN);   // a plan of another batch / grid
-      s_hdr[0] = ok ? pl[0] : 0;
-      s_hdr[1] = ok ? pl[1] : 1;
+      s_hdr[0] = ok ? h.x : 0;
+      s_hdr[1] = ok ? h.y : 1;
     }
     __syncthreads();
     chunk = s_hdr[1];
@@ -1539,9 +1651,9 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     if (ce - cb > kV5FirstRound) {   // the same for every thread of the CTA; ce - cb <= kV5IdCap
       const int n_ids2 = (ce - cb + 3) / 4, n_vt2 = (ce - cb + 15) / 16;
       for (int i = n_ids + tid; i < n_ids2; i += kV5Threads)
-        reinterpret_cast<int4*>(ids)[i] = g_ids[i];
+        reinterpret_cast<int4*>(ids)[i] = __ldcg(g_ids + i);
       for (int i = n_vt + tid; i < n_vt2; i += kV5Threads)
-        reinterpret_cast<int4*>(vtok)[i] = g_vt[i];
+        reinterpret_cast<int4*>(vtok)[i] = __ldcg(g_vt + i);
       __syncthreads();
     }
   } else {
@@ -1570,6 +1682,24 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     const int iend = min(ce, ip + chunk);
     while (ip < iend && ids[ip - cb] < 0) ip = min(iend, unit_end(ip));
     int issued = 0, idle = 0;
+    if (early) {
+      // first uses of the pair's stages, up to the first block that is the last of its unit
+      // (it holds the token the previous kernel appended)
+      while (ip < iend && issued < kV5Stages && ip + 1 < unit_end(ip)) {
+        const int slot = lane * kV5Stages + issued;
+        const uint32_t fb = full0 + 8 * slot;
+        const uint32_t dst = smem_u32(smem + slot * C::kStage);
+        mbar_arrive_expect_tx(fb, C::kStage);
+        const int y = ids[ip - cb];
+        tma_load_2d_hint(dst, &kmap, fb, 0, y, pol);
+        tma_load_2d_hint(dst + C::kTile, &vmap, fb, 0, y, pol);
+        ++issued;
+        ++ip;
+        while (ip < iend && ids[ip - cb] < 0) ip = min(iend, unit_end(ip));
+      }
+      pdl_wait();
+      pdl_launch_dependents();
+    }
     long long t0 = clock64();
     while (ip < iend) {
       const int st = issued % kV5Stages;
@@ -1599,6 +1729,10 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   }
 
   // ---- consumers
+  if (early) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   const int cw = warp - 1, pr = cw >> 1, sub = cw & 1;
   int pos = min(ce, cb + pr * chunk);
   const int end = min(ce, pos + chunk);
@@ -1718,6 +1852,10 @@ static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& 
                          p, batch);
   if (rc) return rc;
   const int units = p.num_kv_heads / 2;
+  if (p.max_parts > kV2MaxPieces)   // small batches: up to kV5MaxPiecesSmall pieces per unit
+    return launch_kernel("paged attention merge launch", merge_pieces_wide_kernel<T>,
+                         dim3(batch * units, 2 * p.group), dim3(256), 0, stream, 1, p, units,
+                         2 * p.group);
   return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
                        dim3(batch * units), dim3(256), 0, stream, 1, p, units, 2 * p.group);
 }
@@ -1845,7 +1983,7 @@ static int decode_impl(
     const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
     int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
     int partition_blocks, void* workspace, size_t workspace_bytes, void* stream,
-    const int32_t* plan) {
+    const int32_t* plan, int flags = 0) {
   clear_error();
   if (batch == 0) return TI_OK;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens)
@@ -1862,6 +2000,10 @@ static int decode_impl(
     return set_error(TI_ERR_UNSUPPORTED, "paged attention: dtype must be bf16 or fp16");
   if (max_blocks_per_seq <= 0 || num_blocks <= 0)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: empty pool or block table");
+  // the split limit and the workspace follow the caller's partition argument (0: the default,
+  // under which small v5 batches are cut finer), exactly as ti_paged_attention_workspace_bytes
+  // and ti_paged_attention_plan see it
+  const int req_partition = partition_blocks;
   if (partition_blocks <= 0) partition_blocks = attn::default_partition(max_blocks_per_seq);
   if (partition_blocks > attn::kMaxPart)
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: partition_blocks must be <= 16");
@@ -1872,9 +2014,9 @@ static int decode_impl(
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: q/out must be 4-byte aligned with even row strides");
   const bool v2 = attn::use_v2(head_dim, batch);
   const int max_parts = (int)split_parts(batch, num_heads, num_kv_heads, head_dim,
-                                         max_blocks_per_seq, partition_blocks);
+                                         max_blocks_per_seq, req_partition);
   const size_t need = ti_paged_attention_workspace_bytes(batch, num_heads, num_kv_heads, head_dim,
-                                                          max_blocks_per_seq, partition_blocks);
+                                                          max_blocks_per_seq, req_partition);
   if (max_parts > 1 && (!workspace || workspace_bytes < need))
     return set_error(TI_ERR_WORKSPACE, "paged attention: workspace too small");
   if (max_parts > 1 && (int64_t)batch * num_kv_heads > attn::kMaxCounters)
@@ -1921,6 +2063,7 @@ static int decode_impl(
     const int forced = attn::forced_kernel();
     if (v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
       p.plan = plan;
+      p.early = plan && (flags & TI_ATTN_EARLY_KV) ? 1 : 0;
       if (plan)
         return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, true>(p, km, vm, batch, s)
                                       : attn::launch_v5<__half, true>(p, km, vm, batch, s);
@@ -1999,12 +2142,12 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
                        reinterpret_cast<int32_t*>(plan));
 }
 
-extern "C" int ti_paged_attention_decode_planned(
+extern "C" int ti_paged_attention_decode_planned_ex(
     void* out, int64_t out_seq_stride, const void* q, int64_t q_seq_stride, const void* k_cache,
     const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int64_t bt_stride,
     const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
     int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
-    void* workspace, size_t workspace_bytes, const void* plan, void* stream) {
+    void* workspace, size_t workspace_bytes, const void* plan, int flags, void* stream) {
   if (!plan) {
     clear_error();
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: null plan");
@@ -2013,8 +2156,24 @@ extern "C" int ti_paged_attention_decode_planned(
     clear_error();
     return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: plan must be 16-byte aligned");
   }
+  if (flags & ~TI_ATTN_EARLY_KV) {
+    clear_error();
+    return set_error(TI_ERR_INVALID_ARGUMENT, "paged attention: unknown flags");
+  }
   return decode_impl(out, out_seq_stride, q, q_seq_stride, k_cache, v_cache, num_blocks,
                      block_tables, bt_stride, row_index, context_lens, batch, num_heads,
                      num_kv_heads, head_dim, block_size, max_blocks_per_seq, dtype, 0, workspace,
-                     workspace_bytes, stream, reinterpret_cast<const int32_t*>(plan));
+                     workspace_bytes, stream, reinterpret_cast<const int32_t*>(plan), flags);
+}
+
+extern "C" int ti_paged_attention_decode_planned(
+    void* out, int64_t out_seq_stride, const void* q, int64_t q_seq_stride, const void* k_cache,
+    const void* v_cache, int64_t num_blocks, const int32_t* block_tables, int64_t bt_stride,
+    const int32_t* row_index, const int32_t* context_lens, int batch, int num_heads,
+    int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq, int dtype,
+    void* workspace, size_t workspace_bytes, const void* plan, void* stream) {
+  return ti_paged_attention_decode_planned_ex(
+      out, out_seq_stride, q, q_seq_stride, k_cache, v_cache, num_blocks, block_tables, bt_stride,
+      row_index, context_lens, batch, num_heads, num_kv_heads, head_dim, block_size,
+      max_blocks_per_seq, dtype, workspace, workspace_bytes, plan, 0, stream);
 }

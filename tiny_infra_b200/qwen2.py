@@ -74,6 +74,9 @@ class Qwen2ForCausalLM:
         # hidden states and greedy streams, ~13 % slower decode steps); False: every K slice
         # adds into the residual stream on its own (fastest; the last bits vary between runs).
         self.deterministic = False
+        # True: decode attention after the first layer starts streaming the KV blocks that no
+        # kernel of the step writes while the QKV GEMM still runs (TI_ATTN_EARLY_KV; same output)
+        self.early_attention = True
 
     # ---- weights -------------------------------------------------------------------------
     def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
@@ -313,11 +316,15 @@ class Qwen2ForCausalLM:
                 pb.positions.data_ptr(), kv_cache.block_size, dt, stream))
             mark(li, "qkv")
             if pb.decode:
-                N.check(lib.ti_paged_attention_decode_planned(
+                # after the first layer the plan (written before it) and every KV block but each
+                # sequence's last (the one the QKV epilogue appends to) are final before the QKV
+                # GEMM starts: the attention streams them while that GEMM still runs
+                early = self.early_attention and li > first_layer
+                N.check(lib.ti_paged_attention_decode_planned_ex(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
                     bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
                     pb.num_seqs, NH, KVH, D, kv_cache.block_size, maxb, dt, ws.data_ptr(),
-                    ws.numel(), plan.data_ptr(), stream))
+                    ws.numel(), plan.data_ptr(), N.TI_ATTN_EARLY_KV if early else 0, stream))
             else:
                 N.check(lib.ti_paged_prefill_attention(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
