@@ -155,26 +155,38 @@ gemv_argmax_kernel(const __grid_constant__ CUtensorMap xmap,
     if constexpr (I8) {
       // converters: thread = weight row (the TMEM lane its warp may access: warp w reaches lanes
       // 32 (w % 4) ..); its 64 int8 of stage g -> 32 columns of tensor-memory slot g % CS
+      // Pipelined by one stage: stage g is loaded and converted while the tensor-memory store
+      // of stage g - 1 completes; its slot is announced only then.
       const int r = (warp & 3) * 32 + lane;
       const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+      int pend = -1;                                  // stage whose store is in flight
       for (int g = 0; g < total; ++g) {
         const int s = g % S, c = g % CS;
         if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (g / S) & 1, TI_DEVERR_GEMM_WAIT)))
           break;
+        uint32_t w[32];
+        convert_int8_row<T>(wbase + s * kW, r, w);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);   // the int8 stage may be refilled
+        if (pend >= 0) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(cfull0 + 8 * (pend % CS));   // slot of stage g - 1 ready
+          pend = -1;
+        }
         if (g >= CS && !__all_sync(0xffffffffu, mbar_wait(cempty0 + 8 * c, ((g / CS) & 1) ^ 1,
                                                           TI_DEVERR_GEMM_WAIT)))
           break;
         tc_fence_after();
-        uint32_t w[32];
-        convert_int8_row<T>(wbase + s * kW, r, w);
         tmem_st32_u(tmem + lane_base + (uint32_t)(C::kAccCols + c * (kBK / 2)), w);
+        pend = g;
+      }
+      if (pend >= 0) {
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(empty0 + 8 * s);            // the int8 stage may be refilled
-          mbar_arrive(cfull0 + 8 * c);            // the converted slot is ready
-        }
+        if (lane == 0) mbar_arrive(cfull0 + 8 * (pend % CS));
       }
     }
   } else if (warp == 1) {
