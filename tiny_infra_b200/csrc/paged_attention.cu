@@ -1410,22 +1410,24 @@ merge_pieces_kernel(Params p, int units, int nheads) {
   *reinterpret_cast<uint2*>(dst) = u;
 }
 
-// Merge for units cut into more than 16 pieces (small batches): one CTA per (sequence, unit,
-// query head of the unit), 16 threads per 4 dims, each taking every 16th piece, so that all of
-// a unit's partials (up to kV5MaxPiecesSmall) arrive in one round of loads instead of rounds of
-// 16.  Pieces are used up to and including the first that stopped at a negative block-table
-// entry; each thread folds its pieces into (max, sum, O) and the 16 are combined by shuffles in
+// Merge for units cut into more than 16 pieces (small batches): one CTA of 128 threads per
+// (sequence, unit, query head of the unit), 8 threads per 4 dims, each taking every 8th piece,
+// so that all of a unit's partials (up to kV5MaxPiecesSmall) arrive in one round of loads
+// instead of rounds of 16, and small CTAs put every merge of a small batch on the SMs in one
+// wave.  Pieces are used up to and including the first that stopped at a negative block-table
+// entry; each thread folds its pieces into (max, sum, O) and the 8 are combined by shuffles in
 // a fixed tree (deterministic).
-constexpr int kWideLanes = 16;
+constexpr int kWideLanes = 8;
+constexpr int kWideThreads = 16 * kWideLanes;
 constexpr int kWidePer = (kV5MaxPiecesSmall + kWideLanes - 1) / kWideLanes;   // pieces / thread
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kWideThreads)
 merge_pieces_wide_kernel(Params p, int units, int nheads) {
   pdl_wait();
   pdl_launch_dependents();
   const int pair = blockIdx.x, h = blockIdx.y;
   const int row = pair / units, unit = pair % units;
-  const int d4 = threadIdx.x >> 4, j = threadIdx.x & 15;   // the 16 piece lanes are adjacent
+  const int d4 = threadIdx.x / kWideLanes, j = threadIdx.x % kWideLanes;   // piece lanes adjacent
   const int32_t* stops = p.ws_stop + (int64_t)pair * p.max_parts;
   const int64_t base = ((int64_t)row * p.num_heads + unit * nheads + h) * p.max_parts;
   int st[kWidePer];
@@ -1475,7 +1477,7 @@ merge_pieces_wide_kernel(Params p, int units, int nheads) {
     }
   }
 #pragma unroll
-  for (int o = 1; o < kWideLanes; o <<= 1) {   // combine the 16 lanes' (M, L, acc)
+  for (int o = 1; o < kWideLanes; o <<= 1) {   // combine the lanes' (M, L, acc)
     const float Mo = __shfl_xor_sync(0xffffffffu, M, o);
     const float Lo = __shfl_xor_sync(0xffffffffu, L, o);
     const float ax = __shfl_xor_sync(0xffffffffu, acc.x, o);
@@ -1834,7 +1836,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
 
 template <typename T, bool PLANNED>
 static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
-                     cudaStream_t stream) {
+                     int ctas, cudaStream_t stream) {
   using C = CfgV5;
   static int set_dev = -1;
   int dev = 0;
@@ -1848,14 +1850,14 @@ static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& 
   }
   if (batch > C::kMaxBatch) return set_error(TI_ERR_UNSUPPORTED, "paged attention v5: batch too large");
   int rc = launch_kernel("paged attention v5 launch", decode_kernel_v5<T, PLANNED>,
-                         dim3(sm_count()), dim3(kV5Threads), C::total(batch), stream, 1, km, vm,
-                         p, batch);
+                         dim3(ctas), dim3(kV5Threads), C::total(batch), stream, 1, km, vm, p,
+                         batch);
   if (rc) return rc;
   const int units = p.num_kv_heads / 2;
   if (p.max_parts > kV2MaxPieces)   // small batches: up to kV5MaxPiecesSmall pieces per unit
     return launch_kernel("paged attention merge launch", merge_pieces_wide_kernel<T>,
-                         dim3(batch * units, 2 * p.group), dim3(256), 0, stream, 1, p, units,
-                         2 * p.group);
+                         dim3(batch * units, 2 * p.group), dim3(kWideThreads), 0, stream, 1, p,
+                         units, 2 * p.group);
   return launch_kernel("paged attention merge launch", merge_pieces_kernel<T>,
                        dim3(batch * units), dim3(256), 0, stream, 1, p, units, 2 * p.group);
 }
@@ -1963,6 +1965,27 @@ extern "C" size_t ti_paged_attention_workspace_bytes(int batch, int num_heads, i
   return bytes + 256;
 }
 
+// CTAs of the v5 kernel and of its plan for a batch of this shape, 0 when v5 cannot take it:
+// the largest chunk any batch of the shape can get (the piece floor at 17 pieces is the larger
+// one) must fit a CTA's id window.  Batches of at most kV5SmallBatch sequences run on half the
+// SMs when that still fits: in a decode step the QKV GEMM before the attention holds the other
+// half (72 CTAs at these batch sizes), so every attention CTA becomes resident while the GEMM
+// runs and streams its first blocks early (TI_ATTN_EARLY_KV), instead of the half behind the
+// GEMM starting only when it ends and setting the launch's length.
+static int v5_ctas(int batch, int num_kv_heads, int max_blocks) {
+  const int64_t worst = (int64_t)batch * (num_kv_heads / 2) * max_blocks;
+  auto fits = [&](int ctas) {
+    return (int64_t)attn::v2_chunk(worst, ctas * attn::kV5Pairs, max_blocks, attn::kV2MaxPieces) *
+               attn::kV5Pairs <= attn::kV5IdCap;
+  };
+  const int sms = attn::sm_count();
+#ifndef TI_V5_HALF_MAX_BATCH
+#define TI_V5_HALF_MAX_BATCH attn::kV5SmallBatch
+#endif
+  if (batch <= TI_V5_HALF_MAX_BATCH && fits(sms / 2)) return sms / 2;
+  return fits(sms) ? sms : 0;
+}
+
 // Whether a decode call of this shape runs the v5 kernel (and can use a plan).
 static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks) {
   if (!attn::use_v2(head_dim, batch) || num_kv_heads <= 0 || num_heads % num_kv_heads) return false;
@@ -1970,11 +1993,7 @@ static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, in
   const int forced = attn::forced_kernel();
   if (forced != 0 && forced != 5) return false;
   if (batch > attn::CfgV5::kMaxBatch) return false;
-  // the largest chunk any batch of this shape can get (the piece floor at 17 pieces is the
-  // larger one) must fit a CTA's id window
-  const int64_t worst = (int64_t)batch * (num_kv_heads / 2) * max_blocks;
-  return (int64_t)attn::v2_chunk(worst, attn::sm_count() * attn::kV5Pairs, max_blocks,
-                                 attn::kV2MaxPieces) * attn::kV5Pairs <= attn::kV5IdCap;
+  return v5_ctas(batch, num_kv_heads, max_blocks) > 0;
 }
 
 static int decode_impl(
@@ -2064,11 +2083,13 @@ static int decode_impl(
     if (v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
       p.plan = plan;
       p.early = plan && (flags & TI_ATTN_EARLY_KV) ? 1 : 0;
+      const int ctas = v5_ctas(batch, num_kv_heads, max_blocks_per_seq);
       if (plan)
-        return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, true>(p, km, vm, batch, s)
-                                      : attn::launch_v5<__half, true>(p, km, vm, batch, s);
-      return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, false>(p, km, vm, batch, s)
-                                    : attn::launch_v5<__half, false>(p, km, vm, batch, s);
+        return dtype == TI_DTYPE_BF16
+                   ? attn::launch_v5<__nv_bfloat16, true>(p, km, vm, batch, ctas, s)
+                   : attn::launch_v5<__half, true>(p, km, vm, batch, ctas, s);
+      return dtype == TI_DTYPE_BF16 ? attn::launch_v5<__nv_bfloat16, false>(p, km, vm, batch, ctas, s)
+                                    : attn::launch_v5<__half, false>(p, km, vm, batch, ctas, s);
     }
     const int64_t chunk_ub = attn::v2_chunk(worst, sms * attn::kV4Warps, max_blocks_per_seq,
                                             max_parts);
@@ -2137,8 +2158,9 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
   p.num_heads = num_heads; p.num_kv_heads = num_kv_heads; p.group = num_heads / num_kv_heads;
   p.max_blocks = max_blocks_per_seq; p.num_blocks = num_blocks;
   p.max_parts = (int)split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq, 0);
-  return launch_kernel("attention plan launch", attn::plan_kernel<512>, dim3(attn::sm_count()),
-                       dim3(512), 0, reinterpret_cast<cudaStream_t>(stream), 1, p, batch,
+  return launch_kernel("attention plan launch", attn::plan_kernel<512>,
+                       dim3(v5_ctas(batch, num_kv_heads, max_blocks_per_seq)), dim3(512), 0,
+                       reinterpret_cast<cudaStream_t>(stream), 1, p, batch,
                        reinterpret_cast<int32_t*>(plan));
 }
 
