@@ -465,7 +465,7 @@ def run_ours(a, rank, world, local):
         dist.barrier()
     clocks = sampler.stop()
     secs = replicas.max_over_ranks(e0.elapsed_time(e1) / 1e3)
-    launches = engine.launches_per_step.get((rows, False), 0) * a.steps
+    launches = engine.launches_per_step.get((rows, False, False), 0) * a.steps
     value = world * SEQS * a.steps / secs
 
     # ---- e2e through the public per-step API (host tokens in/out) ----

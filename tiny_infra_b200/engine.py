@@ -117,15 +117,31 @@ class DecodeEngine:
                                      self.ntiles, rows, self.next_tok.data_ptr(),
                                      self.d_in[1].data_ptr(), kv.seq_len.data_ptr(), 1, s))
 
-    def _replay(self, rows: int, sampled: bool = False) -> None:
+    def _copy_in(self, rows: int, sampled: bool) -> None:
+        # row by row: each [i, :rows] slice of the pinned staging buffers is contiguous (a
+        # [:, :rows] slice is not, and would be copied through an unpinned temporary)
+        for i in range(self.d_in.shape[0]):
+            self.d_in[i, :rows].copy_(self.h_in[i, :rows], non_blocking=True)
+        if sampled:
+            for i in range(self.d_params.shape[0]):
+                self.d_params[i, :rows].copy_(self.h_params[i, :rows], non_blocking=True)
+
+    def _replay(self, rows: int, sampled: bool = False, io: bool = False) -> None:
+        """Run one decode step: the kernels alone, or with ``io`` the host->device copy of the
+        staged inputs before them and the device->host copy of the tokens after them, all in one
+        graph replay (pinned host buffers), so a host-driven step costs one launch."""
         if sampled and self.logits is None:
             c = self.model.config
             self.logits = torch.empty(self.max_rows, c.vocab_size, dtype=self.model.dtype,
                                       device=self.model.device)
         if not self.use_graphs:
+            if io:
+                self._copy_in(rows, sampled)
             self._launch(rows, sampled)
+            if io:
+                self.h_out[:rows].copy_(self.next_tok[:rows], non_blocking=True)
             return
-        key = (rows, sampled)
+        key = (rows, sampled, io)
         g = self.graphs.get(key)
         if g is None:
             # one eager run sets kernel attributes / tensor-map caches outside the capture; it
@@ -140,15 +156,20 @@ class DecodeEngine:
             torch.cuda.current_stream().synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
+                if io:
+                    self._copy_in(rows, sampled)
                 self._launch(rows, sampled)
+                if io:
+                    self.h_out[:rows].copy_(self.next_tok[:rows], non_blocking=True)
             self.d_in.copy_(saved)
             self.kv.seq_len.copy_(seq_saved)
             self.graphs[key] = g
         g.replay()
 
-    def stage(self, slots, tokens) -> int:
-        """Plan block allocation for one new token per slot and copy the step's inputs to the
-        device (asynchronously); returns the padded row count."""
+    def stage(self, slots, tokens, copy: bool = True) -> int:
+        """Plan block allocation for one new token per slot and stage the step's inputs in
+        pinned host memory (and, with ``copy``, copy them to the device asynchronously); returns
+        the padded row count."""
         n = len(slots)
         if n > self.max_rows:
             raise ValueError(f"decode batch {n} exceeds the engine's {self.max_rows} rows")
@@ -163,7 +184,9 @@ class DecodeEngine:
         h[0, n:rows] = 0
         h[1, n:rows] = -1
         h[2, n:rows] = -1
-        self.d_in[:, :rows].copy_(self.h_in[:, :rows], non_blocking=True)
+        if copy:
+            for i in range(self.d_in.shape[0]):
+                self.d_in[i, :rows].copy_(self.h_in[i, :rows], non_blocking=True)
         return rows
 
     def step(self, slots, tokens, params=None) -> np.ndarray:
@@ -178,7 +201,7 @@ class DecodeEngine:
         if n == 0:
             return np.zeros(0, np.int32)
         slots = np.asarray(slots, np.int32)
-        rows = self.stage(slots, tokens)
+        rows = self.stage(slots, tokens, copy=False)
         sampled = params is not None and not params.all_greedy
         if sampled:
             h = self.h_params.numpy()
@@ -187,9 +210,7 @@ class DecodeEngine:
             h[1, n:rows] = 0.0
             h[2, n:rows] = 1.0
             h[3, n:rows] = 0.0
-            self.d_params[:, :rows].copy_(self.h_params[:, :rows], non_blocking=True)
-        self._replay(rows, sampled)
-        self.h_out[:n].copy_(self.next_tok[:n], non_blocking=True)
+        self._replay(rows, sampled, io=True)   # inputs in, the step, tokens out: one replay
         self.kv.advance(slots, 1)      # host mirror, while the step runs (the device advances
         torch.cuda.current_stream().synchronize()   # its own copy in the step's last kernel)
         return self.h_out[:n].numpy().copy()

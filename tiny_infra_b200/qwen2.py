@@ -7,10 +7,10 @@ for every layer, ``seq_len`` is NOT advanced -- the caller does that, engine/sch
 decode attends over seq_len + 1 tokens, models/qwen_25.py:115), and weights load from the
 reference's state-dict names (``load_reference_state_dict``).
 
-Per layer the forward is 7 kernel launches:
-  rmsnorm -> QKV GEMM (+bias, RoPE, KV append) -> paged attention (decode or prefill, split-K
-  merged inside the decode kernel) -> O GEMM (+residual, split-K) -> rmsnorm
-  -> gate/up GEMM (+SwiGLU) -> down GEMM (+residual)
+Per layer the decode forward is 8 kernel launches:
+  rmsnorm -> QKV GEMM (+bias, RoPE, KV append) -> paged attention -> its split-K merge
+  -> O GEMM (+residual, split-K) -> rmsnorm -> gate/up GEMM (+SwiGLU) -> down GEMM (+residual)
+(prefill: one ragged prefill-attention launch instead of the attention and its merge)
 with the residual stream kept in float32 (the reference keeps it in the model dtype; float32
 is closer to the float32 oracle).  The lm_head runs only on the rows whose logits are needed
 and, for greedy decoding, reduces to one token per row inside the GEMM epilogue.
@@ -74,8 +74,8 @@ class Qwen2ForCausalLM:
         # hidden states and greedy streams, ~13 % slower decode steps); False: every K slice
         # adds into the residual stream on its own (fastest; the last bits vary between runs).
         self.deterministic = False
-        # True: decode attention after the first layer starts streaming the KV blocks that no
-        # kernel of the step writes while the QKV GEMM still runs (TI_ATTN_EARLY_KV; same output)
+        # True: decode attention starts streaming the KV blocks that no kernel of the step writes
+        # while the QKV GEMM still runs (TI_ATTN_EARLY_KV; same output)
         self.early_attention = True
 
     # ---- weights -------------------------------------------------------------------------
@@ -316,10 +316,11 @@ class Qwen2ForCausalLM:
                 pb.positions.data_ptr(), kv_cache.block_size, dt, stream))
             mark(li, "qkv")
             if pb.decode:
-                # after the first layer the plan (written before it) and every KV block but each
-                # sequence's last (the one the QKV epilogue appends to) are final before the QKV
-                # GEMM starts: the attention streams them while that GEMM still runs
-                early = self.early_attention and li > first_layer
+                # the plan and every KV block but each sequence's last (the one the QKV epilogue
+                # appends to) are final before the QKV GEMM starts (the RMSNorm before it lets it
+                # launch only once the plan kernel has completed): the attention streams them
+                # while that GEMM still runs
+                early = self.early_attention
                 N.check(lib.ti_paged_attention_decode_planned_ex(
                     attn.data_ptr(), NH * D, qkv.data_ptr(), QKV, kc.data_ptr(), vc.data_ptr(), nb,
                     bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
