@@ -5,38 +5,12 @@
 
 #include "capi_internal.h"
 #include "common.cuh"
+#include "rmsnorm_row.cuh"
 
 namespace ti {
 namespace ew {
 
 constexpr int kThreads = 256;
-
-template <typename T>
-struct Vec8 {   // 8 elements of a 16-bit type in one 16-byte register group
-  uint4 raw;
-  __device__ __forceinline__ void load(const T* p) { raw = *reinterpret_cast<const uint4*>(p); }
-  __device__ __forceinline__ void store(T* p) const { *reinterpret_cast<uint4*>(p) = raw; }
-  __device__ __forceinline__ void to_float(float* f) const {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 v = Elem<T>::unpack2(u[i]);
-      f[2 * i] = v.x;
-      f[2 * i + 1] = v.y;
-    }
-  }
-  __device__ __forceinline__ void from_float(const float* f) {
-    uint32_t* u = reinterpret_cast<uint32_t*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = Elem<T>::pack2(f[2 * i], f[2 * i + 1]);
-  }
-};
-
-__device__ __forceinline__ void load8f(const float* p, float* f) {
-  float4 a = *reinterpret_cast<const float4*>(p);
-  float4 b = *reinterpret_cast<const float4*>(p + 4);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
 
 // Rotate 8 dims of the first half (x1) with the matching 8 dims of the second half (x2)
 // (reference src/fused_rope.cu:37-50).
@@ -175,51 +149,13 @@ __global__ void rmsnorm_reg_kernel(T* __restrict__ out, const TX* __restrict__ x
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   float wf[NC][8];
-#pragma unroll
-  for (int k = 0; k < NC; ++k) {
-    const int c = lane * 8 + k * 256;
-    if (c < H) {
-      Vec8<T> wv;
-      wv.load(w + c);
-      wv.to_float(wf[k]);
-    }
-  }
+  rms_load_weight<T, NC>(w, H, lane, wf);
+  // Dependents launch only after this wait: the decode step relies on it (the attention two
+  // kernels later reads the plan written before this kernel without waiting, TI_ATTN_EARLY_KV).
   pdl_wait();
   pdl_launch_dependents();
-  for (int r = warp; r < rows; r += nwarps) {
-    const TX* xr = x + (int64_t)r * H;
-    float f[NC][8];
-#pragma unroll
-    for (int k = 0; k < NC; ++k) {
-      const int c = lane * 8 + k * 256;
-      if (c < H) {
-        if constexpr (sizeof(TX) == 4) load8f(reinterpret_cast<const float*>(xr) + c, f[k]);
-        else { Vec8<TX> v; v.load(xr + c); v.to_float(f[k]); }
-      }
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < NC; ++k) {
-      if (lane * 8 + k * 256 < H) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += f[k][j] * f[k][j];
-      }
-    }
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / (float)H + eps);
-#pragma unroll
-    for (int k = 0; k < NC; ++k) {
-      const int c = lane * 8 + k * 256;
-      if (c < H) {
-        float o8[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o8[j] = wf[k][j] * Elem<T>::to_f(Elem<T>::from_f(f[k][j] * rstd));
-        Vec8<T> o;
-        o.from_float(o8);
-        o.store(out + (int64_t)r * H + c);
-      }
-    }
-  }
+  for (int r = warp; r < rows; r += nwarps)
+    rms_row<TX, T, NC>(out + (int64_t)r * H, x + (int64_t)r * H, wf, eps, H, lane);
 }
 
 template <typename TX, typename T>
