@@ -107,6 +107,19 @@ int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_stride,
                             const int32_t* row_index, const int32_t* context_lens, int batch,
                             int num_heads, int num_kv_heads, int head_dim, int max_blocks_per_seq,
                             int64_t num_blocks, void* plan, size_t plan_bytes, void* stream);
+/* The plan with flags.  TI_ATTN_PLAN_AFTER_QKV: every attention call that reads the plan comes
+ * right after ti_gemm_qkv_rope of the same `batch` rows (hidden size qkv_hidden, dtype), as in
+ * a decode layer.  That GEMM holds some SMs when the attention grid launches, so the CTAs that
+ * wait for them start a few microseconds late; the plan gives those CTAs fewer KV blocks (how
+ * many fewer from the batch's KV bytes) so that all CTAs end together.  The output differs from
+ * the unskewed plan's only by the float32 summation order of the split sequences. */
+#define TI_ATTN_PLAN_AFTER_QKV 1
+int ti_paged_attention_plan_ex(const int32_t* block_tables, int64_t bt_stride,
+                               const int32_t* row_index, const int32_t* context_lens, int batch,
+                               int num_heads, int num_kv_heads, int head_dim,
+                               int max_blocks_per_seq, int64_t num_blocks, void* plan,
+                               size_t plan_bytes, int flags, int qkv_hidden, int dtype,
+                               void* stream);
 int ti_paged_attention_decode_planned(void* out, int64_t out_seq_stride, const void* q,
                                       int64_t q_seq_stride, const void* k_cache,
                                       const void* v_cache, int64_t num_blocks,

@@ -285,3 +285,72 @@ def test_small_batch_many_pieces(cuda_device):
         want = (p @ vv).reshape(NH, D)
         err = (got[b].float() - want).abs()
         assert (err <= 2e-3 + 2.0 ** -9 * want.abs()).all(), (b, float(err.max()))
+
+
+def _planned_ex(lib, N, q, k, v, bt_np, ctx_np, mb, flags):
+    dev = q.device
+    B, NH, D = q.shape
+    NB, KVH = k.shape[0], k.shape[1]
+    bt, ctx = torch.from_numpy(bt_np).to(dev), torch.from_numpy(ctx_np).to(dev)
+    s = torch.cuda.current_stream().cuda_stream
+    need = lib.ti_paged_attention_workspace_bytes(B, NH, KVH, D, mb, 0)
+    ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    plan = torch.zeros(lib.ti_paged_attention_plan_bytes(B), dtype=torch.uint8, device=dev)
+    N.check(lib.ti_paged_attention_plan_ex(bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), B,
+                                           NH, KVH, D, mb, NB, plan.data_ptr(), plan.numel(),
+                                           flags, 896, N.dtype_code(q.dtype), s))
+    got = torch.full_like(q, 3.0)
+    N.check(lib.ti_paged_attention_decode_planned(*_args(q, k, v, bt, ctx, mb, got),
+                                                  N.dtype_code(q.dtype), ws.data_ptr(), need,
+                                                  plan.data_ptr(), s))
+    torch.cuda.synchronize()
+    return got, plan[:32].view(torch.int32).cpu().numpy()
+
+
+@pytest.mark.parametrize("case", [(31, 256, 128, 2048, True), (32, 200, 64, 1024, True),
+                                  (33, 256, 8192, 32768, False)])
+def test_plan_after_qkv_skews_late_ctas(cuda_device, case):
+    """TI_ATTN_PLAN_AFTER_QKV: the CTAs that start behind the QKV GEMM's SMs take fewer KV blocks
+    (header word 7 < 8 streams, word 6 = CTAs with all 8) when the batch's loop is short enough
+    for the few microseconds they start late to matter, and none otherwise (long contexts: the
+    unskewed plan, bit for bit).  Skewed output: the plain call's up to the float32 summation
+    order (2e-3 + half a bf16 ulp), and an fp32 torch reference on three rows."""
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    seed, B, lo, hi, skewed = case
+    NH, KVH, D = 14, 2, 64
+    rng = np.random.default_rng(seed)
+    ctx_np = rng.integers(lo, hi + 1, B).astype(np.int32)
+    nblk = (ctx_np + 15) // 16
+    NB = int(nblk.sum()) + 16
+    mb = (hi + 15) // 16
+    perm = rng.permutation(NB).astype(np.int32)
+    bt_np = np.full((B, mb), -1, np.int32)
+    off = 0
+    for b in range(B):
+        bt_np[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += int(nblk[b])
+    g = torch.Generator(device=cuda_device).manual_seed(seed)
+    q = torch.randn(B, NH, D, device=cuda_device, generator=g).bfloat16()
+    k = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    v = torch.randn(NB, KVH, 16, D, device=cuda_device, generator=g).bfloat16()
+    ref, _, _ = _plain_and_planned(lib, N, q, k, v, bt_np, ctx_np, mb)
+    got, hdr = _planned_ex(lib, N, q, k, v, bt_np, ctx_np, mb, N.TI_ATTN_PLAN_AFTER_QKV)
+    assert N.device_status() == 0
+    if skewed:
+        assert hdr[7] < 8 and 0 < hdr[6] < hdr[2] // 8, hdr
+        a, b2 = got.float(), ref.float()
+        assert ((a - b2).abs() <= 2e-3 + 2.0 ** -9 * b2.abs()).all(), float((a - b2).abs().max())
+    else:
+        assert hdr[7] == 8 and hdr[6] == hdr[2] // 8, hdr
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    for b in (0, B // 2, B - 1):
+        n = int(ctx_np[b])
+        ids = torch.from_numpy(bt_np[b, :nblk[b]].astype(np.int64)).to(cuda_device)
+        kk = k[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        vv = v[ids].float().permute(1, 0, 2, 3).reshape(KVH, -1, D)[:, :n]
+        qq = q[b].float().view(KVH, NH // KVH, D)
+        p = torch.softmax(qq @ kk.transpose(1, 2) / 8.0, dim=-1)
+        want = (p @ vv).reshape(NH, D)
+        err = (got[b].float() - want).abs()
+        assert (err <= 2e-3 + 2.0 ** -9 * want.abs()).all(), (b, float(err.max()))

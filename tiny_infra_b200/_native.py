@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple] = {
     "ti_sample": (I32, [P, I64, I32, I32, I32, P, P, P, P, P, P, P, I32, P]),
     "ti_paged_attention_plan_bytes": (SZ, [I32]),
     "ti_paged_attention_plan": (I32, [P, I64, P, P, I32, I32, I32, I32, I32, I64, P, SZ, P]),
+    "ti_paged_attention_plan_ex": (I32, [P, I64, P, P, I32, I32, I32, I32, I32, I64, P, SZ, I32,
+                                         I32, I32, P]),
     "ti_paged_attention_decode_planned": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, I32, I32,
                                                 I32, I32, I32, I32, I32, P, SZ, P, P]),
     "ti_paged_attention_decode_planned_ex": (I32, [P, I64, P, I64, P, P, I64, P, I64, P, P, I32,
@@ -63,8 +65,9 @@ TI_EPI_RESIDUAL_DET = 6
 # device status bits (ti_device_status)
 TI_DEVERR_ATTN_WAIT, TI_DEVERR_GEMM_WAIT, TI_DEVERR_PREFILL_WAIT, TI_DEVERR_ATTN_PLAN = 1, 2, 4, 8
 TI_DEVERR_BAD_INPUT = 16
-# ti_paged_attention_decode_planned_ex flags
+# ti_paged_attention_decode_planned_ex / ti_paged_attention_plan_ex flags
 TI_ATTN_EARLY_KV = 1
+TI_ATTN_PLAN_AFTER_QKV = 1
 
 _lib = None
 _lock = threading.Lock()

@@ -71,6 +71,9 @@ int gemv_argmax(const void* A, int64_t lda, const void* B, int64_t ldb, bool int
                 const float* scale, int M, int N, int K, float* aux_val, int32_t* aux_idx,
                 int dtype, cudaStream_t s);
 
+// CTAs of ti_gemm_qkv_rope's launch for M rows of a hidden size K into N = (NH+2KVH)*64 outputs.
+int gemm_qkv_ctas(int M, int N, int K, int dtype);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 int encode_tensor_map_2d(CUtensorMap* out, CUtensorMapDataType type, void* base,
                          const cuuint64_t* dims, const cuuint64_t* strides_bytes,

@@ -980,6 +980,19 @@ static int max_clusters() {
   }
 }
 
+// Cluster size of a nonlinear-epilogue GEMM: the largest of 8 / 4 / 2 (at most `cl`) whose
+// clusters for all output tiles are resident at once and that leaves at least two K blocks per
+// split; else 1.
+template <typename T, int BN, int STAGES, int KIND>
+static int pick_cl(int cl, int M, int N, int K) {
+  const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
+  const int nkb = K / BK;
+  if (cl >= 8 && nkb >= 16 && tiles <= max_clusters<T, BN, STAGES, KIND, 8>()) return 8;
+  if (cl >= 4 && nkb >= 8 && tiles <= max_clusters<T, BN, STAGES, KIND, 4>()) return 4;
+  if (cl >= 2 && nkb >= 4 && tiles <= max_clusters<T, BN, STAGES, KIND, 2>()) return 2;
+  return 1;
+}
+
 // split-K factor -> cluster size: 1, 2, 4 or 8 (the largest power of two <= split, at most 8)
 static int cluster_for(int split) {
   return split >= 8 ? 8 : split >= 4 ? 4 : split >= 2 ? 2 : 1;
@@ -1004,15 +1017,12 @@ static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int
     while (z > 1 && tiles * z > 148) --z;
     return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s, z);
   } else {
-    const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
-    const int nkb = K / BK;
-    if (cl >= 8 && nkb >= 16 && tiles <= max_clusters<T, BN, STAGES, KIND, 8>())
-      return launch_t<T, BN, STAGES, KIND, 8>(am, bm, M, N, K, e, s);
-    if (cl >= 4 && nkb >= 8 && tiles <= max_clusters<T, BN, STAGES, KIND, 4>())
-      return launch_t<T, BN, STAGES, KIND, 4>(am, bm, M, N, K, e, s);
-    if (cl >= 2 && nkb >= 4 && tiles <= max_clusters<T, BN, STAGES, KIND, 2>())
-      return launch_t<T, BN, STAGES, KIND, 2>(am, bm, M, N, K, e, s);
-    return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
+    switch (pick_cl<T, BN, STAGES, KIND>(cl, M, N, K)) {
+      case 8: return launch_t<T, BN, STAGES, KIND, 8>(am, bm, M, N, K, e, s);
+      case 4: return launch_t<T, BN, STAGES, KIND, 4>(am, bm, M, N, K, e, s);
+      case 2: return launch_t<T, BN, STAGES, KIND, 2>(am, bm, M, N, K, e, s);
+      default: return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
+    }
   }
 }
 
@@ -1061,6 +1071,17 @@ static int launch_qkv(const CUtensorMap& am, const CUtensorMap& bm, int M, int N
   return M <= kDeepRingMaxM
              ? dispatch_cl<T, 64, TI_GEMM_STAGES_QKV, TI_EPI_QKV_ROPE>(TI_QKV_MAX_SPLIT, am, bm, M, N, K, e, s)
              : dispatch_cl<T, 64, 4, TI_EPI_QKV_ROPE>(8, am, bm, M, N, K, e, s);
+}
+
+// CTAs of the QKV GEMM's launch for M rows (the decode attention plan uses it: the SMs this
+// grid holds are the ones on which the attention's CTAs start late).
+template <typename T>
+static int qkv_ctas_t(int M, int N, int K) {
+  const int64_t tiles = (int64_t)(N / 64) * ((M + BM - 1) / BM);
+  const int cl = M <= kDeepRingMaxM
+                     ? pick_cl<T, 64, TI_GEMM_STAGES_QKV, TI_EPI_QKV_ROPE>(TI_QKV_MAX_SPLIT, M, N, K)
+                     : pick_cl<T, 64, 4, TI_EPI_QKV_ROPE>(8, M, N, K);
+  return (int)std::min<int64_t>(tiles * cl, 1 << 30);
 }
 
 #ifndef TI_GEMM_STAGES_80
@@ -1112,6 +1133,12 @@ static int launch_swiglu16(int bn, const CUtensorMap& am, const CUtensorMap& bm,
 }
 
 }  // namespace gemm
+
+int gemm_qkv_ctas(int M, int N, int K, int dtype) {
+  return dtype == TI_DTYPE_BF16 ? gemm::qkv_ctas_t<__nv_bfloat16>(M, N, K)
+                                : gemm::qkv_ctas_t<__half>(M, N, K);
+}
+
 }  // namespace ti
 
 using namespace ti;

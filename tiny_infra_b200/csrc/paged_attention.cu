@@ -78,6 +78,10 @@ struct Params {
   const int32_t* plan;      // v5: the batch's stream resolved once (ti_paged_attention_plan)
   int early;                // v5 planned: plan and all but each unit's last block are final
                             // before the previous kernel (TI_ATTN_EARLY_KV)
+  // v5 plan for a call behind another kernel (TI_ATTN_PLAN_AFTER_QKV): CTAs skew_full.. start
+  // about skew_lead_us later (their SMs are held by that kernel) and take fewer streams
+  int skew_full;
+  float skew_lead_us;
 };
 
 // SM count of the current device (the persistent kernels' grid), cached per device.
@@ -457,6 +461,9 @@ constexpr int kV2MaxPieces = 17;                           // pieces per unit (b
 // Small decode batches (the v5 kernel): units may be cut into up to this many pieces, so that a
 // few sequences still spread over every SM (the merge reads their partials in rounds of 16).
 constexpr int kV5MaxPiecesSmall = 65;
+// Stream positions of one v5 CTA held in shared memory (pool row and valid tokens of each):
+// 4096 cover 256 sequences of up to 32k tokens (the long-context replica workload).
+constexpr int kV5IdCap = 4096;
 constexpr int kV5SmallBatch = 64;
 
 struct PieceV2 {
@@ -1077,6 +1084,32 @@ constexpr int kV4IdCap = 2048;
 //    negative or out-of-pool block-table entry) and vtok[] (valid tokens of the block).
 // Returns false (uniformly) when the CTA has no positions.  The leading __syncthreads also
 // publishes barrier initialisation done by the caller before the call.
+// Skewed split for a call behind another kernel: CTAs 0 .. skew_full-1 start on the SMs that
+// kernel leaves free, the others only when it ends, about skew_lead_us later.  The late CTAs
+// then take nl < streams chunks (their last streams stay idle) so that both groups end
+// together: nl = streams * (1 - lead / expected loop time), the loop time estimated from the
+// stream's KV bytes at the HBM rate (kSkewUsPerPos per position), in [5/8, 1] of streams, and
+// only while the early CTAs' larger ranges still fit their id windows.  No skew otherwise.
+constexpr float kSkewUsPerPos = 8192.f / 6.4e6f;   // one block of two kv heads at 6.4 TB/s (us)
+__device__ __forceinline__ int late_streams(int total, int streams, int ctas, const Params& p) {
+  if (p.skew_lead_us <= 0.f || p.skew_full <= 0 || p.skew_full >= ctas) return streams;
+  const float loop_us = fmaxf((float)total * kSkewUsPerPos, 1.f);
+  int nl = streams - __float2int_rn((float)streams * p.skew_lead_us / loop_us);
+  nl = max((streams * 5 + 7) / 8, min(streams, nl));
+  if (nl == streams) return streams;
+  const int units = p.skew_full * streams + (ctas - p.skew_full) * nl;
+  if ((int64_t)v2_chunk(total, units, p.max_blocks, p.max_parts) * streams > kV5IdCap)
+    return streams;
+  return nl;
+}
+// Stream range of CTA b: the first `full` CTAs take `streams` chunks each, the rest nl.
+__host__ __device__ __forceinline__ void cta_range(int b, int full, int streams, int nl, int chunk,
+                                                   int total, int& cb, int& ce) {
+  const int first = b < full ? b * streams : full * streams + (b - full) * nl;
+  cb = first * chunk;
+  ce = min(total, cb + (b < full ? streams : nl) * chunk);
+}
+
 template <int HP, int NT>
 __device__ __forceinline__ bool resolve_stream(const Params& p, int batch, int streams, int* s_off,
                                                int* ids, uint8_t* vtok, int* s_wsum, int& chunk,
@@ -1113,10 +1146,12 @@ __device__ __forceinline__ bool resolve_stream(const Params& p, int batch, int s
   }
   __syncthreads();
   const int total = s_off[batch];
-  chunk = v2_chunk(total, gridDim.x * streams, p.max_blocks, p.max_parts);
-  cb = blockIdx.x * streams * chunk;
+  const int nl = late_streams(total, streams, (int)gridDim.x, p);
+  const int full = nl < streams ? p.skew_full : (int)gridDim.x;
+  chunk = v2_chunk(total, full * streams + ((int)gridDim.x - full) * nl, p.max_blocks,
+                   p.max_parts);
+  cta_range((int)blockIdx.x, full, streams, nl, chunk, total, cb, ce);
   if (cb >= total) return false;
-  ce = min(total, cb + streams * chunk);
   for (int q = tid; q < ce - cb; q += NT) {
     const int pos = cb + q;
     int lo = 0, hi = batch;
@@ -1518,9 +1553,6 @@ constexpr int kV5Pairs = 8;
 constexpr int kV5Stages = 3;
 constexpr int kV5Threads = (1 + 2 * kV5Pairs) * 32;
 
-// Stream positions of one v5 CTA held in shared memory (pool row and valid tokens of each):
-// 4096 cover 256 sequences of up to 32k tokens (the long-context replica workload).
-constexpr int kV5IdCap = 4096;
 // Positions the planned call loads with the plan header in its first round (the whole range of
 // a 256-sequence batch of contexts up to ~2k tokens); longer ranges take a second round.
 constexpr int kV5FirstRound = 2048;
@@ -1543,7 +1575,8 @@ struct CfgV5 {
 
 // Plan layout (int32 words; base 16-byte aligned), written by plan_kernel for the v5 chunking:
 //   [0] total positions  [1] chunk  [2] consumers (CTAs x kV5Pairs)  [3] batch
-//   [4] ids word offset  [5] vtok byte offset  [6] kV5Pairs  [7] kV5IdCap
+//   [4] ids word offset  [5] vtok byte offset  [6] CTAs with kV5Pairs streams (the rest: late)
+//   [7] streams of a late CTA (kV5Pairs: no skew)
 //   [8 ..) s_off[0 .. batch] (padded to 4 words), then per CTA a kV5IdCap slot of ids (int32)
 //   and, after all id slots, per CTA a kV5IdCap slot of vtok (bytes).
 __host__ __device__ inline int64_t plan_ids_word(int batch) { return 8 + (batch + 1 + 3) / 4 * 4; }
@@ -1568,6 +1601,7 @@ plan_kernel(Params p, int batch, int32_t* plan) {
   int chunk = 0, cb = 0, ce = 0;
   resolve_stream<2, NT>(p, batch, kV5Pairs, s_off, ids, vtok, s_wsum, chunk, cb, ce);
   if (blockIdx.x == 0) {
+    const int nl = late_streams(s_off[batch], kV5Pairs, (int)gridDim.x, p);
     for (int r = threadIdx.x; r <= batch; r += NT) plan[8 + r] = s_off[r];
     if (threadIdx.x == 0) {
       plan[0] = s_off[batch];
@@ -1576,8 +1610,8 @@ plan_kernel(Params p, int batch, int32_t* plan) {
       plan[3] = batch;
       plan[4] = (int)plan_ids_word(batch);
       plan[5] = (int)plan_vtok_byte(batch, gridDim.x);
-      plan[6] = kV5Pairs;
-      plan[7] = kV5IdCap;
+      plan[6] = nl < kV5Pairs ? p.skew_full : (int)gridDim.x;
+      plan[7] = nl;
     }
   }
 }
@@ -1621,7 +1655,7 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   if constexpr (PLANNED) {
     // one round of loads: header, s_off and the first kV5FirstRound positions of this CTA's id
     // and vtok slots; a longer range loads the rest in a second round once the header is known
-    __shared__ int s_hdr[2];
+    __shared__ int s_hdr[4];
     const int32_t* pl = p.plan;
     const int n_off = (batch + 1 + 3) / 4;
     const int4* g_off = reinterpret_cast<const int4*>(pl + 8);
@@ -1639,17 +1673,20 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
     }
     if (tid == 0) {
       const int4 h = __ldcg(reinterpret_cast<const int4*>(pl));
+      const int4 h2 = __ldcg(reinterpret_cast<const int4*>(pl) + 1);
       const bool ok = h.w == batch && h.z == (int)gridDim.x * kV5Pairs &&
-                      h.y > 0 && (int64_t)h.y * kV5Pairs <= kV5IdCap;
+                      h.y > 0 && (int64_t)h.y * kV5Pairs <= kV5IdCap && h2.z >= 0 &&
+                      h2.z <= (int)gridDim.x && h2.w >= 1 && h2.w <= kV5Pairs;
       if (!ok) raise_device_error(TI_DEVERR_ATTN_PLAN);   // a plan of another batch / grid
       s_hdr[0] = ok ? h.x : 0;
       s_hdr[1] = ok ? h.y : 1;
+      s_hdr[2] = ok ? h2.z : (int)gridDim.x;
+      s_hdr[3] = ok ? h2.w : kV5Pairs;
     }
     __syncthreads();
     chunk = s_hdr[1];
-    cb = blockIdx.x * kV5Pairs * chunk;
+    cta_range((int)blockIdx.x, s_hdr[2], kV5Pairs, s_hdr[3], chunk, s_hdr[0], cb, ce);
     if (cb >= s_hdr[0]) return;
-    ce = min(s_hdr[0], cb + kV5Pairs * chunk);
     if (ce - cb > kV5FirstRound) {   // the same for every thread of the CTA; ce - cb <= kV5IdCap
       const int n_ids2 = (ce - cb + 3) / 4, n_vt2 = (ce - cb + 15) / 16;
       for (int i = n_ids + tid; i < n_ids2; i += kV5Threads)
@@ -2130,11 +2167,17 @@ extern "C" size_t ti_paged_attention_plan_bytes(int batch) {
   return batch < 0 ? 0 : attn::plan_bytes(batch, attn::sm_count());
 }
 
-extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_stride,
-                                       const int32_t* row_index, const int32_t* context_lens,
-                                       int batch, int num_heads, int num_kv_heads, int head_dim,
-                                       int max_blocks_per_seq, int64_t num_blocks, void* plan,
-                                       size_t plan_bytes, void* stream) {
+// How long the QKV GEMM before a decode step's attention keeps its SMs after the attention
+// grid launched (in-kernel traces at 32-256 rows: ~6 us); the skewed plan uses it.
+#ifndef TI_QKV_LEAD_US
+#define TI_QKV_LEAD_US 6.f
+#endif
+constexpr float kQkvLeadUs = TI_QKV_LEAD_US;
+
+static int plan_impl(const int32_t* block_tables, int64_t bt_stride, const int32_t* row_index,
+                     const int32_t* context_lens, int batch, int num_heads, int num_kv_heads,
+                     int head_dim, int max_blocks_per_seq, int64_t num_blocks, void* plan,
+                     size_t plan_bytes, int flags, int qkv_hidden, int dtype, void* stream) {
   clear_error();
   if (batch == 0) return TI_OK;
   if (!block_tables || !context_lens || !plan)
@@ -2143,6 +2186,8 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
     return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: negative batch or empty pool");
   if (reinterpret_cast<uintptr_t>(plan) & 15)
     return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: buffer must be 16-byte aligned");
+  if (flags & ~TI_ATTN_PLAN_AFTER_QKV)
+    return set_error(TI_ERR_INVALID_ARGUMENT, "attention plan: unknown flags");
   if (!v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
     // the planned decode takes the unplanned path for this shape (a zero header: chunk 0)
     if (plan_bytes < 32)
@@ -2158,10 +2203,40 @@ extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_s
   p.num_heads = num_heads; p.num_kv_heads = num_kv_heads; p.group = num_heads / num_kv_heads;
   p.max_blocks = max_blocks_per_seq; p.num_blocks = num_blocks;
   p.max_parts = (int)split_parts(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq, 0);
-  return launch_kernel("attention plan launch", attn::plan_kernel<512>,
-                       dim3(v5_ctas(batch, num_kv_heads, max_blocks_per_seq)), dim3(512), 0,
+  const int ctas = v5_ctas(batch, num_kv_heads, max_blocks_per_seq);
+  if ((flags & TI_ATTN_PLAN_AFTER_QKV) && qkv_hidden > 0 && ctas == attn::sm_count()) {
+    // the QKV GEMM of these rows holds gemm_qkv_ctas SMs when the attention grid launches
+    const int held = gemm_qkv_ctas(batch, (num_heads + 2 * num_kv_heads) * head_dim, qkv_hidden,
+                                   dtype);
+    if (held > 0 && held < ctas) {
+      p.skew_full = ctas - held;
+      p.skew_lead_us = kQkvLeadUs;
+    }
+  }
+  return launch_kernel("attention plan launch", attn::plan_kernel<512>, dim3(ctas), dim3(512), 0,
                        reinterpret_cast<cudaStream_t>(stream), 1, p, batch,
                        reinterpret_cast<int32_t*>(plan));
+}
+
+extern "C" int ti_paged_attention_plan(const int32_t* block_tables, int64_t bt_stride,
+                                       const int32_t* row_index, const int32_t* context_lens,
+                                       int batch, int num_heads, int num_kv_heads, int head_dim,
+                                       int max_blocks_per_seq, int64_t num_blocks, void* plan,
+                                       size_t plan_bytes, void* stream) {
+  return plan_impl(block_tables, bt_stride, row_index, context_lens, batch, num_heads,
+                   num_kv_heads, head_dim, max_blocks_per_seq, num_blocks, plan, plan_bytes, 0, 0,
+                   TI_DTYPE_BF16, stream);
+}
+
+extern "C" int ti_paged_attention_plan_ex(const int32_t* block_tables, int64_t bt_stride,
+                                          const int32_t* row_index, const int32_t* context_lens,
+                                          int batch, int num_heads, int num_kv_heads,
+                                          int head_dim, int max_blocks_per_seq,
+                                          int64_t num_blocks, void* plan, size_t plan_bytes,
+                                          int flags, int qkv_hidden, int dtype, void* stream) {
+  return plan_impl(block_tables, bt_stride, row_index, context_lens, batch, num_heads,
+                   num_kv_heads, head_dim, max_blocks_per_seq, num_blocks, plan, plan_bytes, flags,
+                   qkv_hidden, dtype, stream);
 }
 
 extern "C" int ti_paged_attention_decode_planned_ex(

@@ -77,6 +77,9 @@ class Qwen2ForCausalLM:
         # True: decode attention starts streaming the KV blocks that no kernel of the step writes
         # while the QKV GEMM still runs (TI_ATTN_EARLY_KV; same output)
         self.early_attention = True
+        # True: the per-step attention plan gives the attention CTAs that start behind the QKV
+        # GEMM's SMs fewer KV blocks (TI_ATTN_PLAN_AFTER_QKV; float32 summation order only)
+        self.skewed_plan = True
 
     # ---- weights -------------------------------------------------------------------------
     def load_reference_state_dict(self, sd: dict) -> "Qwen2ForCausalLM":
@@ -288,9 +291,12 @@ class Qwen2ForCausalLM:
             if plan is None:
                 plan = self._plan_ws.get(self.device,
                                          lib.ti_paged_attention_plan_bytes(pb.num_seqs))
-            N.check(lib.ti_paged_attention_plan(
+            # each layer's attention follows its QKV GEMM: the CTAs behind that GEMM's SMs start
+            # late, so they get fewer KV blocks (TI_ATTN_PLAN_AFTER_QKV)
+            N.check(lib.ti_paged_attention_plan_ex(
                 bt.data_ptr(), bt.stride(0), pb.seq_slots.data_ptr(), pb.ctx_lens.data_ptr(),
-                pb.num_seqs, NH, KVH, D, maxb, nb, plan.data_ptr(), plan.numel(), stream))
+                pb.num_seqs, NH, KVH, D, maxb, nb, plan.data_ptr(), plan.numel(),
+                N.TI_ATTN_PLAN_AFTER_QKV if self.skewed_plan else 0, H, dt, stream))
         split_o = self._splits(NH * D)
         split_d = self._splits(I)
         residual = N.TI_EPI_RESIDUAL_DET if self.deterministic else N.TI_EPI_RESIDUAL
