@@ -5,6 +5,10 @@ Tolerance: fp32 accumulation in a different order, then one rounding of the outp
 |err| <= 2^-8 |ref| + 1e-3 * rms(ref) (bf16 outputs); float32 outputs (residual epilogue):
 |err| <= 1e-4 * rms(ref) + 1e-6.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 import torch
@@ -90,7 +94,7 @@ def test_swiglu_epilogue(cuda_device, bn):
     _close_bf16(out.float().cpu().numpy(), g / (1 + np.exp(-g)) * u)
 
 
-@pytest.mark.parametrize("M,I,dt", [(256, 4864, "bf16"), (200, 4864, "bf16"),
+@pytest.mark.parametrize("M,I,dt", [(256, 4864, "bf16"), (200, 4864, "bf16"), (129, 4864, "bf16"),
                                     (100, 1032, "bf16"), (256, 1032, "bf16"),
                                     (4096, 4864, "bf16"), (300, 1032, "bf16"), (1, 4864, "bf16"),
                                     (32, 4864, "bf16"), (37, 4864, "bf16"), (64, 4864, "fp16"),
@@ -120,12 +124,16 @@ def test_swiglu16_epilogue(cuda_device, M, I, dt):
     assert (got[:, I:] == 7.0).all()
 
 
-@pytest.mark.parametrize("split,bn", [(1, 64), (2, 64), (3, 64), (5, 64), (8, 128), (16, 128)])
-def test_residual_split_k(cuda_device, split, bn):
+@pytest.mark.parametrize("M,split,bn", [(256, 1, 64), (256, 2, 64), (256, 3, 64), (256, 5, 64),
+                                        (256, 8, 128), (256, 16, 128), (129, 10, 128),
+                                        (200, 5, 64)])
+def test_residual_split_k(cuda_device, M, split, bn):
     """x_f32 += A W^T with each split-K slice adding its partial tile into x (red.add); a second
-    run agrees up to the fp32 rounding of the (varying) order of the slices' additions."""
+    run agrees up to the fp32 rounding of the (varying) order of the slices' additions.  129-256
+    rows run on CTA pairs (M = 256 MMAs over two SMs; at 129 / 200 the odd CTA's rows are
+    mostly or partly past M)."""
     from tiny_infra_b200 import _native as N_
-    M, N, K = 256, 896, 4864
+    N, K = 896, 4864
     a, b = _operands(5, M, N, K, wstd=0.02)
     x0 = np.random.default_rng(6).standard_normal((M, N)).astype(np.float32)
     x = torch.from_numpy(x0).cuda()
@@ -241,3 +249,17 @@ def test_argmax_persistent_lm_head(cuda_device, M):
     assert (got[clear] == np.argmax(ref, axis=1)[clear]).all()
     assert got[M - 1] == 77
     assert (ix >= 0).all() and (ix < N).all()
+
+
+def test_pairs_at_decode_sizes(cuda_device):
+    """The SwiGLU16 and residual cases again with CTA pairs (M = 256 MMAs on two SMs) for every
+    batch above 128 rows (TI_GEMM_PAIR=1; by default only batches above 256 rows use them), in
+    a child process because the library reads the switch once."""
+    if os.environ.get("TI_GEMM_PAIR") == "1":
+        pytest.skip("this process already runs with pairs at every size")
+    env = dict(os.environ, TI_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.abspath(__file__), "-q", "-x",
+                        "-m", "gpu", "-k", "swiglu16 or residual_split"],
+                       env=env, capture_output=True, text=True, timeout=900,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -22,11 +22,11 @@ void count_launch(unsigned n = 1);
 // On by default; the environment variable TI_PDL=0 turns it off (plain stream ordering).
 bool pdl_enabled();
 
-// Launch `kern` on stream `s` (PDL attribute when enabled; a cluster of `cluster_z` CTAs along
-// grid z when > 1) and count it.  Returns TI_OK or TI_ERR_CUDA with `what` in the message.
+// Launch `kern` on stream `s` (PDL attribute when enabled; clusters of shape `cluster` when it
+// has more than one CTA) and count it.  Returns TI_OK or TI_ERR_CUDA with `what` in the message.
 template <typename... KArgs, typename... Args>
-int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                  cudaStream_t s, int cluster_z, Args&&... args) {
+int launch_kernel_cl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t s, dim3 cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -39,11 +39,11 @@ int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
     at[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
   }
-  if (cluster_z > 1) {
+  if (cluster.x * cluster.y * cluster.z > 1) {
     at[n].id = cudaLaunchAttributeClusterDimension;
-    at[n].val.clusterDim.x = 1;
-    at[n].val.clusterDim.y = 1;
-    at[n].val.clusterDim.z = (unsigned)cluster_z;
+    at[n].val.clusterDim.x = cluster.x;
+    at[n].val.clusterDim.y = cluster.y;
+    at[n].val.clusterDim.z = cluster.z;
     ++n;
   }
   cfg.attrs = at;
@@ -55,6 +55,15 @@ int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
     return set_cuda_error(e, what);
   }
   return 0;
+}
+
+// As launch_kernel_cl with a cluster of `cluster_z` CTAs along grid z (none when <= 1).
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t s, int cluster_z, Args&&... args) {
+  return launch_kernel_cl(what, kern, grid, block, smem, s,
+                          dim3(1, 1, cluster_z > 1 ? (unsigned)cluster_z : 1u),
+                          std::forward<Args>(args)...);
 }
 
 // Split-K slots per (sequence, query head) that ti_paged_attention_decode uses with the default

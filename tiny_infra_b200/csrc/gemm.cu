@@ -411,10 +411,15 @@ constexpr int kMaxSmem = 227 * 1024;
 // still reads 128 rows: the rows past AR come from the rest of the stage and are garbage that
 // only reaches accumulator rows >= M, which are never stored), so that a stage is small enough
 // for the ring to hold every K block of the tile at once.
-template <int BN, int STAGES, int CL, int AR = BM>
+// PAIR: the tile is computed by a CTA pair (a cluster of two consecutive CTAs along grid x)
+// with M = 256 MMAs (cta_group::2): each CTA loads its own 128 rows of A and half of the tile's
+// BN rows of B, so each SM streams a quarter fewer bytes per output than a 1-SM tile of the same
+// width.
+template <int BN, int STAGES, int CL, int AR = BM, bool PAIR = false>
 struct Cfg {
   static constexpr int kABytes = AR * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;   // B rows this CTA loads per stage
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
   // the last stage's 128-row A read reaches this far past the ring
   static constexpr int kAOver = (BM - AR) * BK * 2 > kBBytes ? (BM - AR) * BK * 2 - kBBytes : 0;
@@ -449,24 +454,27 @@ struct Cfg {
   static_assert(kStages >= 2, "a ring of at least two stages");
   static_assert(AR == BM || (CL == 1 && AR % 8 == 0 && kABytes % 1024 == 0),
                 "short activation boxes: unsplit tiles, 1024-byte aligned stages");
+  static_assert(!PAIR || (CL == 1 && AR == BM && kBRows % 8 == 0 && kBBytes % 1024 == 0),
+                "CTA pairs: no split-K cluster, full activation boxes, whole 8-row B groups");
   static_assert(kSmem <= kMaxSmem, "shared memory");
 };
 
 // Whether the staged output tile fits the drained stage ring.
-template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM, bool PAIR = false>
 constexpr bool ring_fits() {
-  using C = Cfg<BN, STAGES, CL, AR>;
+  using C = Cfg<BN, STAGES, CL, AR, PAIR>;
   return C::kStageOff + C::kRows * Out<T, BN, KIND>::kBytes <= C::kRing;
 }
 
-// One 128 x BN output tile per cluster of CL CTAs (CL = split-K factor along grid z).
-template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
+// One 128 x BN output tile per cluster of CL CTAs (CL = split-K factor along grid z); PAIR: a
+// 256 x BN tile per CTA pair, each CTA finishing its own 128 rows.
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
             const __grid_constant__ CUtensorMap xmap, int K, int kb_per_split, EpiArgs e) {
-  using C = Cfg<BN, STAGES, CL, AR>;
+  using C = Cfg<BN, STAGES, CL, AR, PAIR>;
   constexpr int S = C::kStages;   // ring depth (a cluster kernel's receive buffer takes stages)
-  static_assert(ring_fits<T, BN, STAGES, KIND, CL, AR>(), "staged tile fits the ring");
+  static_assert(ring_fits<T, BN, STAGES, KIND, CL, AR, PAIR>(), "staged tile fits the ring");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -479,8 +487,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   const uint32_t recv = sbase + C::kRing + C::kRecvOff;   // cluster receive buffer (CL > 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x;
-  const int n0 = tile_n * BN, m0 = blockIdx.y * BM;
+  // a CTA pair is two consecutive CTAs along grid x (the 128-row M tiles); else x runs over N
+  const int tile_n = PAIR ? blockIdx.y : blockIdx.x;
+  const int n0 = tile_n * BN, m0 = (PAIR ? blockIdx.x : blockIdx.y) * BM;
   const int nkb = K / BK;
   const int kb0 = blockIdx.z * kb_per_split;
   const int kb1 = min(nkb, kb0 + kb_per_split);
@@ -498,7 +507,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       prefetch_tensormap(&bmap);
     }
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    if constexpr (PAIR) tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+    else tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -506,6 +516,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   const uint32_t tmem = *tmem_slot;
   // All on-chip resources are held: the next kernel may be scheduled.
   pdl_launch_dependents();
+  // CTA pair: both CTAs' barriers and TMEM exist before the odd CTA's loads complete on the even
+  // CTA's barriers and the even CTA's MMAs and commits reach the odd one.
+  const uint32_t prank = PAIR ? cluster_rank() : 0u;
+  if constexpr (PAIR) cluster_sync();
   // Cluster barrier phase 1 (arrive now, wait before the first push): every CTA of the
   // cluster has started, so its shared memory may be written.
   if constexpr (CL > 1) cluster_arrive_relaxed();
@@ -522,20 +536,38 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   bool ok = true;
 
   if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BN, std::is_same<T, __nv_bfloat16>::value);
+    // the MMA issuer: lane 0 (of the even CTA of a pair, for both)
+    if (lane == 0 && prank == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      constexpr uint32_t idesc = PAIR ? idesc_f16(2 * BM, BN, kBf16, false, false)
+                                      : instr_desc(BN, kBf16);
+      // a pair's commits arrive on the barrier at the same offset in both CTAs
+      const uint32_t odd = PAIR ? map_peer(full0, 1u) - full0 : 0u;
       for (int it = 0; it < nk; ++it) {
         const int s = it % S;
         if (!mbar_wait(full0 + 8 * s, (it / S) & 1, TI_DEVERR_GEMM_WAIT)) break;
         tc_fence_after();
         const uint32_t sa = sbase + s * C::kStage;
         const uint64_t da = smem_desc(sa), db = smem_desc(sa + C::kABytes);
+        if constexpr (PAIR) {
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)   // +32 bytes along K inside the swizzle atom
-          tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
-        tc_commit(empty0 + 8 * s);
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_pair(tmem, da + 2 * k, db + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(empty0 + 8 * s);
+          tc_commit_pair(empty0 + 8 * s + odd);
+        } else {
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)   // +32 bytes along K inside the swizzle atom
+            tc_mma(tmem, da + 2 * k, db + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
+          tc_commit(empty0 + 8 * s);
+        }
       }
-      tc_commit(accum);
+      if constexpr (PAIR) {
+        tc_commit_pair(accum);
+        tc_commit_pair(accum + odd);
+      } else {
+        tc_commit(accum);
+      }
     }
     __syncwarp();
   } else if (warp >= 2) {
@@ -550,26 +582,36 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       const int p = warp - 2;
       const uint64_t pol_a = l2_policy_evict_last();    // activations: re-read by many CTAs
       const uint64_t pol_b = l2_policy_evict_first();   // weights: streamed once
+      // A pair's loads all complete on the even CTA's full barriers, which expect both CTAs'
+      // bytes; each CTA loads its own B rows (the second half of the tile for the odd CTA).
+      const uint32_t fullx = PAIR ? map_peer(full0, 0u) : full0;
+      const int nb = n0 + (int)prank * C::kBRows;
+      auto expect = [&](int s) {
+        if (prank == 0) mbar_arrive_expect_tx(full0 + 8 * s, PAIR ? 2 * C::kStage : C::kStage);
+      };
+      auto load = [&](uint32_t dst, const CUtensorMap* map, int s, int x, int y, uint64_t pol) {
+        if constexpr (PAIR) tma_load_2d_pair(dst, map, fullx + 8 * s, x, y, pol);
+        else tma_load_2d_hint(dst, map, full0 + 8 * s, x, y, pol);
+      };
       // Weights do not depend on earlier kernels: fetch the first stages' B tiles before
       // waiting for the producer of the activations.
       const int pre_n = min(nk, S);
       for (int it = p; it < pre_n; it += kProd) {
-        mbar_arrive_expect_tx(full0 + 8 * it, C::kStage);
-        tma_load_2d_hint(sbase + it * C::kStage + C::kABytes, &bmap, full0 + 8 * it,
-                         (kb0 + it) * BK, n0, pol_b);
+        expect(it);
+        load(sbase + it * C::kStage + C::kABytes, &bmap, it, (kb0 + it) * BK, nb, pol_b);
       }
       pdl_wait();
       for (int it = p; it < pre_n; it += kProd)
-        tma_load_2d_hint(sbase + it * C::kStage, &amap, full0 + 8 * it, (kb0 + it) * BK, m0, pol_a);
+        load(sbase + it * C::kStage, &amap, it, (kb0 + it) * BK, m0, pol_a);
       for (int it = p; it < nk; it += kProd) {
         if (it < pre_n) continue;
         const int s = it % S;
         if (!mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1, TI_DEVERR_GEMM_WAIT)) break;
-        mbar_arrive_expect_tx(full0 + 8 * s, C::kStage);
+        expect(s);
         const uint32_t sa = sbase + s * C::kStage;
         const int kx = (kb0 + it) * BK;
-        tma_load_2d_hint(sa, &amap, full0 + 8 * s, kx, m0, pol_a);
-        tma_load_2d_hint(sa + C::kABytes, &bmap, full0 + 8 * s, kx, n0, pol_b);
+        load(sa, &amap, s, kx, m0, pol_a);
+        load(sa + C::kABytes, &bmap, s, kx, nb, pol_b);
       }
     }
     __syncwarp();
@@ -677,9 +719,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   }
   tc_fence_before();
   __syncthreads();
+  // CTA pair: neither CTA frees its TMEM or exits while the other may still use its barriers
+  if constexpr (PAIR) cluster_sync();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, C::kTmemCols);
+    else tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -909,14 +954,14 @@ static int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols
   return tile_map(m, p, tma_type(dtype), rows, cols, ld * 2, BK, box_rows);
 }
 
-template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM>
+template <typename T, int BN, int STAGES, int KIND, int CL, int AR = BM, bool PAIR = false>
 static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
                     const EpiArgs& e, cudaStream_t s, int zsplits = 1) {
-  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL, AR>()) {
+  if constexpr (!ring_fits<T, BN, STAGES, KIND, CL, AR, PAIR>()) {
     return set_error(TI_ERR_UNSUPPORTED, "gemm: this tile width and epilogue do not fit the stage ring");
   } else {
-    using C = Cfg<BN, STAGES, CL, AR>;
-    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL, AR>;
+    using C = Cfg<BN, STAGES, CL, AR, PAIR>;
+    auto kern = gemm_kernel<T, BN, STAGES, KIND, CL, AR, PAIR>;
     if (AR < BM && M > AR)
       return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: short activation box for a taller batch");
     static int set_dev = -1;
@@ -930,7 +975,10 @@ static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, 
     const int nkb = K / BK;
     const int zs = CL > 1 ? CL : zsplits;
     const int per = (nkb + zs - 1) / zs;   // a split may be empty (it contributes zeros)
-    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, CL > 1 ? CL : (nkb + per - 1) / per);
+    // a pair covers 256 rows: an even number of 128-row tiles, along x (clusters of 2 x 1 x 1)
+    const int mt = PAIR ? (M + 2 * BM - 1) / (2 * BM) * 2 : (M + BM - 1) / BM;
+    const int nt = (N + BN - 1) / BN, zt = CL > 1 ? CL : (nkb + per - 1) / per;
+    const dim3 grid = PAIR ? dim3(mt, nt, zt) : dim3(nt, mt, zt);
     // residual: tensor map over x (fp32) for the bulk reduce-add of staged tiles
     CUtensorMap xm = am;
     if constexpr (KIND == TI_EPI_RESIDUAL && TI_RESIDUAL_TMA_REDUCE) {
@@ -938,8 +986,61 @@ static int launch_t(const CUtensorMap& am, const CUtensorMap& bm, int M, int N, 
                               C::kRows);
       if (rc) return rc;
     }
-    return launch_kernel("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s, CL, am, bm, xm,
-                         K, per, e);
+    return launch_kernel_cl("gemm launch", kern, grid, dim3(kThreads), C::kSmem, s,
+                            dim3(PAIR ? 2 : 1, 1, CL > 1 ? CL : 1), am, bm, xm, K, per, e);
+  }
+}
+
+// Which batches run on CTA pairs (2-SM MMAs): TI_GEMM_PAIR=1 every batch of more than 128 rows,
+// =0 none, unset only those above kDeepRingMaxM rows (prefill).  At 256 decode rows each pair
+// launch measured ~1 us slower than the 1-SM tiles (gate/up 9.2 -> 10.1, down 7.1 -> 8.0, o_proj
+// 3.7 -> 4.8 us): those GEMMs wait on load round trips, not on the bytes each SM streams.
+constexpr int kDeepRingMaxM = 256;
+static int pair_mode() {
+  static const int mode = [] {
+    const char* v = getenv("TI_GEMM_PAIR");
+    return v && v[0] == '0' ? 0 : v && v[0] == '1' ? 1 : 2;
+  }();
+  return mode;
+}
+inline bool pair_rows(int M) {
+  const int mode = pair_mode();
+  return mode == 1 ? M > BM : mode == 2 ? M > kDeepRingMaxM : false;
+}
+
+// Clusters of one CTA pair of this kernel the GPU keeps resident at once; cached per device.
+template <typename T, int BN, int STAGES, int KIND>
+static int max_pairs() {
+  if constexpr (!ring_fits<T, BN, STAGES, KIND, 1, BM, true>()) {
+    return 0;
+  } else {
+    static int cached_dev = -1, value = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cached_dev != dev) {
+      using C = Cfg<BN, STAGES, 1, BM, true>;
+      auto kern = gemm_kernel<T, BN, STAGES, KIND, 1, BM, true>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = C::kSmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = 0;   // unknown: no pairs
+      }
+      value = n;
+      cached_dev = dev;
+    }
+    return value;
   }
 }
 
@@ -1004,9 +1105,16 @@ constexpr int kMaxResidualSplit = 16;
 // per split.
 // DET (residual only): split K over a cluster and sum the slices in a fixed order instead of
 // letting every slice red.add on its own, so that `x` is bit-reproducible.
-template <typename T, int BN, int STAGES, int KIND, bool DET = false>
+// Ring depth of a pair tile: decode batches (one wave) 8 stages; above kDeepRingMaxM rows
+// (many waves) rings of ~96 KB, two CTAs per SM as for the 1-SM tiles.
+constexpr int kPairStagesDeep = 8;
+template <int BN>
+constexpr int pair_stages_shallow() { return BN <= 128 ? 4 : 3; }
+
+// PSTAGES: the ring depth of the pair variant of this tile.
+template <typename T, int BN, int STAGES, int KIND, bool DET = false, int PSTAGES = kPairStagesDeep>
 static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N, int K,
-                       const EpiArgs& e, cudaStream_t s) {
+                       const EpiArgs& e, cudaStream_t s, const CUtensorMap* bm_pair = nullptr) {
   if constexpr (KIND == TI_EPI_ARGMAX) {   // argmax tiles are never split
     return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s);
   } else if constexpr (KIND == TI_EPI_RESIDUAL && !DET) {
@@ -1015,6 +1123,10 @@ static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int
     const int64_t tiles = (int64_t)(N / BN) * ((M + BM - 1) / BM);
     int z = std::max(1, std::min(cl, K / BK / 2));
     while (z > 1 && tiles * z > 148) --z;
+    // pairs: one wave of them at decode sizes; any number of waves above
+    const int64_t pairs = tiles * z / 2, room = max_pairs<T, BN, PSTAGES, KIND>();
+    if (bm_pair && pair_rows(M) && room > 0 && (M > kDeepRingMaxM || pairs <= room))
+      return launch_t<T, BN, PSTAGES, KIND, 1, BM, true>(am, *bm_pair, M, N, K, e, s, z);
     return launch_t<T, BN, STAGES, KIND, 1>(am, bm, M, N, K, e, s, z);
   } else {
     switch (pick_cl<T, BN, STAGES, KIND>(cl, M, N, K)) {
@@ -1039,18 +1151,20 @@ static int dispatch_cl(int cl, const CUtensorMap& am, const CUtensorMap& bm, int
 // 192 KB of loads in flight for the one CTA on the SM; above (prefill: many waves) ~96 KB rings,
 // so two CTAs share an SM and one's epilogue runs under the other's main loop (measured at 4096
 // tokens: gate/up 780 -> 933 TFLOP/s; at 256 tokens the deep rings are 5 % faster per step).
-constexpr int kDeepRingMaxM = 256;
 template <typename T, int KIND, bool DET = false>
 static int dispatch_bn(int bn, int cl, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
-                       int K, const EpiArgs& e, cudaStream_t s) {
+                       int K, const EpiArgs& e, cudaStream_t s,
+                       const CUtensorMap* bm_pair = nullptr) {
   const bool deep = M <= kDeepRingMaxM;
   switch (bn) {
     case 64:
-      return deep ? dispatch_cl<T, 64, TI_GEMM_STAGES_64, KIND, DET>(cl, am, bm, M, N, K, e, s)
-                  : dispatch_cl<T, 64, 4, KIND, DET>(cl, am, bm, M, N, K, e, s);
+      return deep ? dispatch_cl<T, 64, TI_GEMM_STAGES_64, KIND, DET>(cl, am, bm, M, N, K, e, s, bm_pair)
+                  : dispatch_cl<T, 64, 4, KIND, DET, pair_stages_shallow<64>()>(cl, am, bm, M, N,
+                                                                              K, e, s, bm_pair);
     case 128:
-      return deep ? dispatch_cl<T, 128, TI_GEMM_STAGES_128, KIND, DET>(cl, am, bm, M, N, K, e, s)
-                  : dispatch_cl<T, 128, 3, KIND, DET>(cl, am, bm, M, N, K, e, s);
+      return deep ? dispatch_cl<T, 128, TI_GEMM_STAGES_128, KIND, DET>(cl, am, bm, M, N, K, e, s, bm_pair)
+                  : dispatch_cl<T, 128, 3, KIND, DET, pair_stages_shallow<128>()>(cl, am, bm, M,
+                                                                                N, K, e, s, bm_pair);
     case 256:   // never split
       return deep ? launch_t<T, 256, TI_GEMM_STAGES_256, KIND, 1>(am, bm, M, N, K, e, s)
                   : launch_t<T, 256, 2, KIND, 1>(am, bm, M, N, K, e, s);
@@ -1118,7 +1232,16 @@ static int swiglu16_box_rows(int M, int K, int bn) {
 }
 template <typename T>
 static int launch_swiglu16(int bn, const CUtensorMap& am, const CUtensorMap& bm, int M, int N,
-                           int K, const EpiArgs& e, cudaStream_t s) {
+                           int K, const EpiArgs& e, cudaStream_t s,
+                           const CUtensorMap* bm_pair = nullptr) {
+  if (bm_pair && pair_rows(M)) {
+    if (bn == 144 && (N + 143) / 144 <= max_pairs<T, 144, kPairStagesDeep, TI_EPI_SWIGLU16>())
+      return launch_t<T, 144, kPairStagesDeep, TI_EPI_SWIGLU16, 1, BM, true>(am, *bm_pair, M, N, K,
+                                                                              e, s);
+    constexpr int kPs = pair_stages_shallow<256>();
+    if (bn == 256 && M > kDeepRingMaxM && max_pairs<T, 256, kPs, TI_EPI_SWIGLU16>() > 0)
+      return launch_t<T, 256, kPs, TI_EPI_SWIGLU16, 1, BM, true>(am, *bm_pair, M, N, K, e, s);
+  }
   const int ar = swiglu16_box_rows(M, K, bn);
   if (ar == 32) return launch_t<T, 80, 14, TI_EPI_SWIGLU16, 1, 32>(am, bm, M, N, K, e, s);
   if (ar == 64) return launch_t<T, 80, 12, TI_EPI_SWIGLU16, 1, 64>(am, bm, M, N, K, e, s);
@@ -1204,6 +1327,15 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
   if (rc) return rc;
   rc = gemm::operand_map(&bm, B, N, K, ldb, block_n, dtype);
   if (rc) return rc;
+  // CTA pairs load half of each B tile per CTA (bf16 / fp16 SwiGLU16 and residual epilogues)
+  CUtensorMap bm2;
+  const CUtensorMap* bm_pair = nullptr;
+  if (gemm::pair_rows(M) &&
+      (epilogue == TI_EPI_SWIGLU16 || epilogue == TI_EPI_RESIDUAL)) {
+    rc = gemm::operand_map(&bm2, B, N, K, ldb, block_n / 2, dtype);
+    if (rc) return rc;
+    bm_pair = &bm2;
+  }
   gemm::EpiArgs e{};
   e.out = out; e.ldo = ldo; e.bias = bias; e.aux_val = aux_val; e.aux_idx = aux_idx;
   e.M = M; e.N = N; e.ntiles = N / block_n;
@@ -1212,11 +1344,13 @@ extern "C" int ti_gemm(int epilogue, const void* A, int64_t lda, const void* B, 
   switch (epilogue) {                                                                         \
     case TI_EPI_STORE: return gemm::dispatch_bn<T, TI_EPI_STORE>(block_n, cl, am, bm, M, N, K, e, s); \
     case TI_EPI_SWIGLU: return gemm::dispatch_bn<T, TI_EPI_SWIGLU>(block_n, cl, am, bm, M, N, K, e, s); \
-    case TI_EPI_RESIDUAL: return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, cl, am, bm, M, N, K, e, s); \
+    case TI_EPI_RESIDUAL:                                                                     \
+      return gemm::dispatch_bn<T, TI_EPI_RESIDUAL>(block_n, cl, am, bm, M, N, K, e, s, bm_pair); \
     case TI_EPI_RESIDUAL_DET:                                                                 \
       return gemm::dispatch_bn<T, TI_EPI_RESIDUAL, true>(block_n, cl, am, bm, M, N, K, e, s);   \
     case TI_EPI_ARGMAX: return gemm::dispatch_bn<T, TI_EPI_ARGMAX>(block_n, 1, am, bm, M, N, K, e, s); \
-    case TI_EPI_SWIGLU16: return gemm::launch_swiglu16<T>(block_n, am, bm, M, N, K, e, s);   \
+    case TI_EPI_SWIGLU16:                                                                     \
+      return gemm::launch_swiglu16<T>(block_n, am, bm, M, N, K, e, s, bm_pair);               \
     default: return set_error(TI_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue");             \
   }
   if (dtype == TI_DTYPE_BF16) { TI_GEMM_KIND(__nv_bfloat16) }
