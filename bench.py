@@ -79,6 +79,9 @@ def _args():
     ap.add_argument("--case", choices=["256", "config1", "long"], default="256",
                     help="attention case: one layer of the 256-sequence workload, or the "
                          "8-sequence ctx U[1,512] paged-attention op")
+    ap.add_argument("--rows", type=int, default=4096,
+                    help="rmsnorm kernel: rows per launch (4096: a prefill chunk; 256: one decode "
+                         "step's batch)")
     return ap.parse_args()
 
 
@@ -788,13 +791,15 @@ def run_projection_kernel(a):
 
 
 def run_rmsnorm_kernel(a):
-    """RMSNorm of the fused-elementwise workload: 4096 tokens x hidden 896, float32 residual
-    stream in, bf16 out, eps 1e-6, cycling over 12 inputs (176 MB > L2); GB/s of its
-    algorithmic bytes (x read once, out written once, the weight)."""
+    """RMSNorm of the fused-elementwise workload: 4096 tokens x hidden 896 (``--rows``: 256 for
+    one decode step's batch), float32 residual stream in, bf16 out, eps 1e-6, cycling over
+    enough inputs to exceed L2 (>= 147 MB); GB/s of its algorithmic bytes (x read once, out
+    written once, the weight)."""
     import torch
     from tiny_infra_b200 import _native as N
     dev = torch.device("cuda:0")
-    T, H, L = 4096, 896, 12
+    T, H = a.rows, 896
+    L = max(12, -(-160 * 2 ** 20 // (T * H * 4)))
     g = torch.Generator(device=dev)
     g.manual_seed(a.seed)
     xs = [torch.randn(T, H, device=dev, generator=g) for _ in range(L)]

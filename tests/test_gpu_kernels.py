@@ -264,11 +264,12 @@ def test_rmsnorm(cuda_device, T):
     assert (np.abs(_f32(out) - ref) <= tol * np.abs(ref) + 1e-5).all()
 
 
-@pytest.mark.parametrize("T", [300, 40, 2048])
+@pytest.mark.parametrize("T", [300, 40, 2048, 32, 17])
 def test_qkv_rope_append_gemm(cuda_device, T):
     """QKV projection with RoPE and the KV append fused in the tcgen05 GEMM epilogue: q and the
     pool's k/v equal the float32 x W^T + b, rotated, rounded once to bf16 (one ulp allowed for
-    accumulation order).  300 and 40 tokens run split-K over a cluster of 4, 2048 unsplit."""
+    accumulation order).  300, 40, 32 and 17 tokens run split-K over a cluster of 4 (17: the last
+    rows of the 128-row tile past M), 2048 unsplit."""
     from tiny_infra_b200 import _native as N
     rng = np.random.default_rng(9)
     H, NH, KVH, D, bs = 896, 14, 2, 64, 16

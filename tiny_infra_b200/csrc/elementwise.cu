@@ -11,6 +11,11 @@ namespace ti {
 namespace ew {
 
 constexpr int kThreads = 256;
+#ifndef TI_RMS_SMALL_THREADS
+#define TI_RMS_SMALL_THREADS 64
+#endif
+constexpr int kRmsSmallRows = 2048;                   // up to here: the small-CTA RMSNorm grid
+constexpr int kRmsSmallThreads = TI_RMS_SMALL_THREADS;
 
 // Rotate 8 dims of the first half (x1) with the matching 8 dims of the second half (x2)
 // (reference src/fused_rope.cu:37-50).
@@ -335,10 +340,13 @@ extern "C" int ti_rmsnorm(void* out, const void* x, int x_dtype, const void* wei
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int g = ew::grid_for(work);
   if (hidden <= 1024) {   // the row in registers: one read of x
+    // decode batches: CTAs of 2 rows, so the rows spread over many SMs (each SM's share of the
+    // rows arrives in one L2 round trip); prefill chunks: 8 rows per CTA
+    const int bt = num_tokens <= ew::kRmsSmallRows ? ew::kRmsSmallThreads : ew::kThreads;
+    const int gr = (int)std::max<int64_t>(1, std::min<int64_t>((work + bt - 1) / bt, 148 * 32));
 #define TI_RMS_REG(TX, T)                                                                      \
-  return launch_kernel("rmsnorm launch", ew::rmsnorm_reg_kernel<TX, T, 4>, dim3(g),              \
-                       dim3(ew::kThreads), 0, s, 1, (T*)out, (const TX*)x, (const T*)weight, eps, \
-                       num_tokens, hidden)
+  return launch_kernel("rmsnorm launch", ew::rmsnorm_reg_kernel<TX, T, 4>, dim3(gr), dim3(bt),   \
+                       0, s, 1, (T*)out, (const TX*)x, (const T*)weight, eps, num_tokens, hidden)
     if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_FP32) TI_RMS_REG(float, __nv_bfloat16);
     if (dtype == TI_DTYPE_BF16 && x_dtype == TI_DTYPE_BF16) TI_RMS_REG(__nv_bfloat16, __nv_bfloat16);
     if (dtype == TI_DTYPE_FP16 && x_dtype == TI_DTYPE_FP32) TI_RMS_REG(float, __half);
