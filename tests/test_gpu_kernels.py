@@ -163,6 +163,68 @@ def test_attention_each_kernel(cuda_device, monkeypatch, kernel):
     assert ok, err
 
 
+def _decode_direct(lib, out, q, k, v, bt, ctx, ws=None, ws_bytes=0):
+    """ti_paged_attention_decode through the C ABI (partition 0: the library's choice)."""
+    B, NH, D = q.shape
+    NB, KVH = k.shape[0], k.shape[1]
+    dt = 1 if q.dtype == torch.float16 else 0
+    return lib.ti_paged_attention_decode(
+        out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), NB,
+        bt.data_ptr(), bt.stride(0), None, ctx.data_ptr(), B, NH, KVH, D, 16, bt.shape[1], dt, 0,
+        ws, ws_bytes, torch.cuda.current_stream().cuda_stream)
+
+
+def test_attention_unit_kernel(cuda_device, monkeypatch):
+    """Calls whose sequences all fit 32 blocks (ctx <= 512) and whose units (a sequence's pair
+    of kv heads) fit one wave of CTAs run one CTA per unit: a single launch, no workspace, no
+    plan.  Against the oracle: 148 units of ctx U[1, 512] (the wave limit); four kv heads in
+    groups of 4 (two units per sequence); a GQA group of 8; fp16; contexts longer than the
+    table (clamped to its 512 tokens, as the other kernels); the edge cases (ctx 0 untouched,
+    -1 entries truncate, a leading -1 gives NaN, ids past the pool count as -1).  The same
+    batch forced through v5 (split-K pieces and the merge kernel) agrees within the tolerance."""
+    from tiny_infra_b200 import _native as N
+    lib = N.lib()
+    cases = [((10, 148, 14, 2, 64, 148 * 32, 1, 512), torch.bfloat16),
+             ((11, 20, 16, 4, 64, 800, 1, 512), torch.bfloat16),
+             ((12, 16, 16, 2, 64, 600, 1, 500), torch.bfloat16),
+             ((13, 8, 14, 2, 64, 512, 1, 512), torch.float16),
+             ((14, 6, 14, 2, 64, 600, 520, 700), torch.bfloat16)]
+    for c, dt in cases:
+        q, k, v, bt, ctx = _attn_case(*c)
+        bt = np.ascontiguousarray(bt[:, :32])     # the last case: contexts past the table
+        qt, kt, vt = (_to_dev(x, dt, cuda_device) for x in (q, k, v))
+        btd, ctxd = torch.from_numpy(bt).to(cuda_device), torch.from_numpy(ctx).to(cuda_device)
+        out = torch.zeros_like(qt)
+        n0 = lib.ti_launch_count()
+        assert _decode_direct(lib, out, qt, kt, vt, btd, ctxd) == 0, lib.ti_last_error()
+        assert lib.ti_launch_count() - n0 == 1          # one launch, no workspace given
+        torch.cuda.synchronize()
+        ref = np.zeros(q.shape, np.float32)
+        OK.paged_attention(ref, *(_f32(x) for x in (qt, kt, vt)), bt, ctx, 16)
+        ok, err = _attn_ok(_f32(out), ref, dt)
+        assert ok, (c, err)
+    # edge cases
+    q, k, v, bt, ctx = _attn_case(15, 6, 14, 2, 64, 300, 100, 512)
+    ctx[0] = 0
+    bt[1, 3] = -1
+    bt[2, 20] = -1
+    bt[3, 0] = -1
+    bt[4, 5] = 300 + 7
+    out, ref = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx, init=7.0)
+    assert (out[0] == 7.0).all()
+    assert np.isnan(out[3]).all() and np.isnan(ref[3]).all()
+    ok, err = _attn_ok(out[[0, 1, 2, 4, 5]], ref[[0, 1, 2, 4, 5]])
+    assert ok, err
+    # the same batch through v5 (which splits the sequences and merges) agrees
+    q, k, v, bt, ctx = _attn_case(16, 40, 14, 2, 64, 40 * 32, 1, 512)
+    unit, _ = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx)
+    monkeypatch.setenv("TI_PAGED_ATTN_KERNEL", "v5")
+    v5, ref = _run_attn(cuda_device, torch.bfloat16, q, k, v, bt, ctx)
+    ok, err = _attn_ok(unit, v5)
+    assert ok, err
+    assert N.device_status() == 0
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 def test_rope_inplace(cuda_device, dtype):
     """custom_rope.apply_inplace on a packed ragged batch: T=4096, positions in [0, 32768)."""

@@ -1871,6 +1871,215 @@ decode_kernel_v5(const __grid_constant__ CUtensorMap kmap,
   }
 }
 
+// ==========================================================================================
+// Unit kernel: one CTA per unit (a sequence's pair of kv heads) for calls whose sequences are
+// all short (at most kUnitMaxBlocks blocks) and whose units fit one wave of CTAs.  The producer
+// warp and the 8 warp pairs stream the unit's blocks as v5's do (the pairs split the blocks into
+// 8 contiguous chunks); the pairs' partials (max, sum, O) are combined in shared memory in a
+// fixed order and normalised by the CTA itself: one launch, no split-K workspace, no merge
+// kernel.  head_dim 64, even numbers of kv heads, GQA groups <= 8.  Reference semantics as v5
+// (attention.cu:54-154): ctx 0 leaves the row untouched, reading stops at the first negative
+// (or out-of-pool) block-table entry, a sequence without a readable token gets NaN.
+// ==========================================================================================
+constexpr int kUnitMaxBlocks = 32;   // context length <= 512 tokens
+
+struct CfgUnit {
+  static constexpr int kIds = kUnitMaxBlocks * 4;
+  static constexpr int kSmem = CfgV5::kRing + CfgV5::kBars + kIds + kUnitMaxBlocks + 1024;
+  // a pair's partial over its drained ring: O [sub][head][dim], then (m, l) [sub][head]
+  static constexpr int kPartO = 2 * 8 * 64;
+  static constexpr int kPartBytes = (kPartO + 2 * 8 * 2) * 4;
+  static_assert(kPartBytes <= kV5Stages * CfgV5::kStage, "a pair's partial fits its ring");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kV5Threads, 1)
+decode_kernel_unit(const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, Params p) {
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  using C = CfgV5;
+  constexpr int kSlots = kV5Pairs * kV5Stages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t full0 = smem_u32(smem + C::kRing);   // [pair][stage]
+  const uint32_t empty0 = full0 + kSlots * 8;
+  int* ids = reinterpret_cast<int*>(smem + C::kRing + C::kBars);
+  uint8_t* vtok = smem + C::kRing + C::kBars + CfgUnit::kIds;
+  __shared__ int s_nb, s_stop, s_ctx;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KVU = p.num_kv_heads / 2;
+  const int row = (int)blockIdx.x / KVU, unit = (int)blockIdx.x % KVU;
+  const int G = p.group;
+  if (tid < kSlots) {
+    mbar_init(full0 + 8 * tid, 1);    // the producer's arrive + the two tiles' bytes
+    mbar_init(empty0 + 8 * tid, 2);   // one arrive per consumer warp of the pair
+    fence_mbar_init();
+  }
+  if (tid == 0) {
+    const int ctx = p.context_lens[row];
+    s_ctx = ctx;
+    s_nb = ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
+    s_stop = 1 << 30;
+  }
+  __syncthreads();
+  const int nb = s_nb;
+  const int brow = p.row_index ? p.row_index[row] : row;
+  const int32_t* bt = p.block_tables + (int64_t)brow * p.bt_stride;
+  for (int j = tid; j < nb; j += kV5Threads) {   // reading stops at the first bad entry
+    const int phys = bt[j];
+    if (phys < 0 || (int64_t)phys >= p.num_blocks) atomicMin(&s_stop, j);
+  }
+  __syncthreads();
+  const int nbe = min(nb, s_stop);
+  for (int j = tid; j < nbe; j += kV5Threads) {
+    ids[j] = (bt[j] * p.num_kv_heads + unit * 2) * kBlock;
+    vtok[j] = (uint8_t)min(kBlock, s_ctx - j * kBlock);
+  }
+  __syncthreads();
+  const int chunk = (nbe + kV5Pairs - 1) / kV5Pairs;
+  // consumer state (pair pr, warp sub: kv head 2 unit + sub), kept across the barriers below
+  const int cw = warp - 1, pr = cw >> 1, sub = cw & 1;
+  const int g = lane >> 2, t4 = lane & 3;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, o[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+  if (warp == 0) {
+    // ---- producer: lane i issues pair i's loads, a load whenever the pair's next stage is free
+    if (lane < kV5Pairs) {
+      const uint64_t pol = l2_policy_evict_first();
+      int ip = min(nbe, lane * chunk);
+      const int iend = min(nbe, ip + chunk);
+      int issued = 0, idle = 0;
+      long long t0 = clock64();
+      while (ip < iend) {
+        const int st = issued % kV5Stages;
+        const int use = issued / kV5Stages;
+        const int slot = lane * kV5Stages + st;
+        if (use == 0 || mbar_test_wait(empty0 + 8 * slot, (use - 1) & 1)) {
+          const uint32_t fb = full0 + 8 * slot;
+          const uint32_t dst = smem_u32(smem + slot * C::kStage);
+          mbar_arrive_expect_tx(fb, C::kStage);
+          tma_load_2d_hint(dst, &kmap, fb, 0, ids[ip], pol);
+          tma_load_2d_hint(dst + C::kTile, &vmap, fb, 0, ids[ip], pol);
+          ++issued;
+          ++ip;
+          t0 = clock64();
+          idle = 0;
+        } else if (clock64() - t0 > kWaitCycles) {
+          raise_device_error(TI_DEVERR_ATTN_WAIT);   // the pair's consumers time out as well
+          break;
+        } else if (++idle > 64) {
+          __nanosleep(32);
+        }
+      }
+    }
+  } else {
+    // ---- consumers: pair pr, warp sub computes kv head 2 unit + sub over the pair's chunk
+    int pos = min(nbe, pr * chunk);
+    const int end = min(nbe, pos + chunk);
+    if (pos < end) {
+      const int head0 = (unit * 2 + sub) * G;
+      uint32_t qb[4][2];
+      const T* qh = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.q_stride +
+                    (int64_t)(head0 + g) * 64;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qb[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t4) : 0u;
+        qb[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t4) : 0u;
+      }
+      uint8_t* ring = smem + pr * kV5Stages * C::kStage;
+      const uint32_t fullp = full0 + pr * kV5Stages * 8, emptyp = empty0 + pr * kV5Stages * 8;
+      uint32_t phase = 0;
+      for (int consumed = 0; pos < end; ++pos, ++consumed) {
+        const int st = consumed % kV5Stages;
+        if (!mbar_wait(fullp + 8 * st, (phase >> st) & 1u, TI_DEVERR_ATTN_WAIT)) break;
+        phase ^= 1u << st;
+        uint8_t* kt = ring + st * C::kStage + sub * kBlock * 128;
+        uint8_t* vt = ring + st * C::kStage + C::kTile + sub * kBlock * 128;
+        swapped_block<T>(smem_u32(kt), smem_u32(vt), vt, vtok[pos], lane, qb, p.scale_log2, m, l,
+                         o);
+        __syncwarp();                    // every lane is done with the stage before it is released
+        if (lane == 0) mbar_arrive(emptyp + 8 * st);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) l[j] += __shfl_xor_sync(0xffffffffu, l[j], off);
+    }
+  }
+  __syncthreads();   // every warp is done with the rings (all loads were consumed)
+  if (warp > 0) {
+    // the pair's partial over its drained ring (an empty pair: (-inf, 0) and zeros)
+    float* po = reinterpret_cast<float*>(smem + pr * kV5Stages * C::kStage);
+    float* pml = po + CfgUnit::kPartO;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int hl = 2 * t4 + j;
+      if (hl >= G) continue;
+      float* oh = po + (sub * 8 + hl) * 64;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        oh[mt * 16 + g] = o[mt][j];
+        oh[mt * 16 + g + 8] = o[mt][2 + j];
+      }
+      if (g == 0) {
+        pml[(sub * 8 + hl) * 2] = m[j];
+        pml[(sub * 8 + hl) * 2 + 1] = l[j];
+      }
+    }
+  }
+  __syncthreads();   // every pair's partial is in shared memory
+  if (s_ctx <= 0) return;   // ctx 0: the row is left as it was
+  // ---- combine the 8 pairs in a fixed order, normalise, store: task = (sub, head, dim)
+  T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.out_stride;
+  for (int t = tid; t < 2 * G * 64; t += kV5Threads) {
+    const int sb = t / (G * 64), hl = (t / 64) % G, d = t % 64;
+    const int hi = sb * 8 + hl;
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kV5Pairs; ++q) {
+      const float* pq = reinterpret_cast<const float*>(smem + q * kV5Stages * C::kStage);
+      M = fmaxf(M, pq[CfgUnit::kPartO + hi * 2]);
+    }
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int q = 0; q < kV5Pairs; ++q) {
+      const float* pq = reinterpret_cast<const float*>(smem + q * kV5Stages * C::kStage);
+      const float mq = pq[CfgUnit::kPartO + hi * 2];
+      if (mq == -INFINITY) continue;
+      const float f = fast_exp2(mq - M);
+      L += pq[CfgUnit::kPartO + hi * 2 + 1] * f;
+      O += pq[hi * 64 + d] * f;
+    }
+    outp[(int64_t)((unit * 2 + sb) * G + hl) * 64 + d] = Elem<T>::from_f(O / L);   // L 0: NaN
+  }
+}
+
+template <typename T>
+static int launch_unit(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int units,
+                       cudaStream_t stream) {
+  static int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel_unit<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, CfgUnit::kSmem);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(paged attention unit)");
+    set_dev = dev;
+  }
+  return launch_kernel("paged attention unit launch", decode_kernel_unit<T>, dim3(units),
+                       dim3(kV5Threads), CfgUnit::kSmem, stream, 1, km, vm, p);
+}
+
 template <typename T, bool PLANNED>
 static int launch_v5(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int batch,
                      int ctas, cudaStream_t stream) {
@@ -1943,11 +2152,16 @@ static int launch_v2(const Params& p, const CUtensorMap& km, const CUtensorMap& 
                        dim3(C::kWarps * 32), C::kTotal, stream, 1, km, vm, p, batch);
 }
 
-// TI_PAGED_ATTN_KERNEL=v2|v4|v5 restricts the choice among the equivalent head_dim-64 kernels
-// (for comparisons and tests; a kernel that cannot serve the call is still skipped).
+// TI_PAGED_ATTN_KERNEL=v2|v4|v5|unit restricts the choice among the equivalent head_dim-64
+// kernels (for comparisons and tests; a kernel that cannot serve the call is still skipped).
 static int forced_kernel() {
   const char* e = getenv("TI_PAGED_ATTN_KERNEL");
-  return !e ? 0 : !strcmp(e, "v2") ? 2 : !strcmp(e, "v4") ? 4 : !strcmp(e, "v5") ? 5 : 0;
+  return !e ? 0
+            : !strcmp(e, "v2") ? 2
+            : !strcmp(e, "v4") ? 4
+            : !strcmp(e, "v5") ? 5
+            : !strcmp(e, "unit") ? 6
+                                 : 0;
 }
 
 // Partition size (KV blocks per split-K CTA of the v1 kernel) used when the caller passes 0.
@@ -1970,11 +2184,25 @@ static int64_t attn_parts(int batch, int head_dim, int max_blocks, int partition
 
 static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks);
 
-// Split-K slots per (sequence, query head) of a call: the v5 kernel at <= kV5SmallBatch
-// sequences cuts units finer (kV5MaxPiecesSmall pieces at most), so a small batch's blocks
-// spread over every SM; otherwise as attn_parts.
+// Whether a decode call of this shape runs the unit kernel: head_dim 64, pairs of kv heads with
+// GQA groups <= 8, every sequence at most kUnitMaxBlocks blocks and one CTA per unit fitting one
+// wave.  Such a call splits no sequence: one launch, no workspace, no plan.
+static bool unit_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks) {
+  if (!attn::use_v2(head_dim, batch) || num_kv_heads <= 0 || num_heads % num_kv_heads) return false;
+  if (num_kv_heads % 2 || num_heads / num_kv_heads > 8 || max_blocks <= 0) return false;
+  const int forced = attn::forced_kernel();
+  if (forced != 0 && forced != 6) return false;
+  return max_blocks <= attn::kUnitMaxBlocks &&
+         (int64_t)batch * (num_kv_heads / 2) <= attn::sm_count();
+}
+
+// Split-K slots per (sequence, query head) of a call: 1 for the unit kernel; the v5 kernel at
+// <= kV5SmallBatch sequences cuts units finer (kV5MaxPiecesSmall pieces at most), so a small
+// batch's blocks spread over every SM; otherwise as attn_parts.
 static int64_t split_parts(int batch, int num_heads, int num_kv_heads, int head_dim,
                            int max_blocks, int partition_blocks) {
+  if (partition_blocks <= 0 && unit_path(batch, num_heads, num_kv_heads, head_dim, max_blocks))
+    return 1;
   if (batch <= attn::kV5SmallBatch && partition_blocks <= 0 &&
       v5_path(batch, num_heads, num_kv_heads, head_dim, max_blocks))
     return attn::kV5MaxPiecesSmall;
@@ -2026,6 +2254,7 @@ static int v5_ctas(int batch, int num_kv_heads, int max_blocks) {
 // Whether a decode call of this shape runs the v5 kernel (and can use a plan).
 static bool v5_path(int batch, int num_heads, int num_kv_heads, int head_dim, int max_blocks) {
   if (!attn::use_v2(head_dim, batch) || num_kv_heads <= 0 || num_heads % num_kv_heads) return false;
+  if (unit_path(batch, num_heads, num_kv_heads, head_dim, max_blocks)) return false;
   if (num_kv_heads % 2 || num_heads / num_kv_heads > 8 || max_blocks <= 0) return false;
   const int forced = attn::forced_kernel();
   if (forced != 0 && forced != 5) return false;
@@ -2106,6 +2335,13 @@ static int decode_impl(
   rc = attn::kv_tensor_map(&vm, v_cache, rows, head_dim, dtype, hp * attn::kBlock);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (req_partition <= 0 &&
+      unit_path(batch, num_heads, num_kv_heads, head_dim, max_blocks_per_seq)) {
+    // short sequences: one CTA per unit, no split (a plan, if given, is not read)
+    const int units = batch * (num_kv_heads / 2);
+    return dtype == TI_DTYPE_BF16 ? attn::launch_unit<__nv_bfloat16>(p, km, vm, units, s)
+                                  : attn::launch_unit<__half>(p, km, vm, units, s);
+  }
   if (v2) {
     // v4 needs its CTA's whole stream range in shared memory: check the worst case here
     static int sms = 0;
