@@ -1891,18 +1891,13 @@ struct CfgUnit {
   static constexpr int kPartBytes = (kPartO + 2 * 8 * 2) * 4;
   static_assert(kPartBytes <= kV5Stages * CfgV5::kStage, "a pair's partial fits its ring");
   static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(kUnitMaxBlocks <= kV5Threads, "one thread per table entry");
 };
 
 template <typename T>
 __global__ void __launch_bounds__(kV5Threads, 1)
 decode_kernel_unit(const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, Params p) {
-  if (threadIdx.x == 0) {
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
-  }
-  pdl_wait();
-  pdl_launch_dependents();
   using C = CfgV5;
   constexpr int kSlots = kV5Pairs * kV5Stages;
   extern __shared__ uint8_t smem_raw[];
@@ -1918,30 +1913,38 @@ decode_kernel_unit(const __grid_constant__ CUtensorMap kmap,
   const int KVU = p.num_kv_heads / 2;
   const int row = (int)blockIdx.x / KVU, unit = (int)blockIdx.x % KVU;
   const int G = p.group;
+  // set-up that reads nothing an earlier kernel writes, before the wait for it
+  if (tid == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    s_stop = 1 << 30;
+  }
   if (tid < kSlots) {
     mbar_init(full0 + 8 * tid, 1);    // the producer's arrive + the two tiles' bytes
     mbar_init(empty0 + 8 * tid, 2);   // one arrive per consumer warp of the pair
     fence_mbar_init();
   }
+  pdl_wait();
+  pdl_launch_dependents();
+  // one round of loads: the context length and the whole table row (at most kUnitMaxBlocks
+  // entries, one per thread), read together rather than the row after the length
+  const int brow = p.row_index ? p.row_index[row] : row;
+  const int32_t* bt = p.block_tables + (int64_t)brow * p.bt_stride;
+  const int phys = tid < p.max_blocks ? bt[tid] : -1;
   if (tid == 0) {
     const int ctx = p.context_lens[row];
     s_ctx = ctx;
     s_nb = ctx > 0 ? min((ctx + kBlock - 1) / kBlock, p.max_blocks) : 0;
-    s_stop = 1 << 30;
   }
   __syncthreads();
   const int nb = s_nb;
-  const int brow = p.row_index ? p.row_index[row] : row;
-  const int32_t* bt = p.block_tables + (int64_t)brow * p.bt_stride;
-  for (int j = tid; j < nb; j += kV5Threads) {   // reading stops at the first bad entry
-    const int phys = bt[j];
-    if (phys < 0 || (int64_t)phys >= p.num_blocks) atomicMin(&s_stop, j);
-  }
+  // reading stops at the first bad entry (negative or past the pool)
+  if (tid < nb && (phys < 0 || (int64_t)phys >= p.num_blocks)) atomicMin(&s_stop, tid);
   __syncthreads();
   const int nbe = min(nb, s_stop);
-  for (int j = tid; j < nbe; j += kV5Threads) {
-    ids[j] = (bt[j] * p.num_kv_heads + unit * 2) * kBlock;
-    vtok[j] = (uint8_t)min(kBlock, s_ctx - j * kBlock);
+  if (tid < nbe) {
+    ids[tid] = (phys * p.num_kv_heads + unit * 2) * kBlock;
+    vtok[tid] = (uint8_t)min(kBlock, s_ctx - tid * kBlock);
   }
   __syncthreads();
   const int chunk = (nbe + kV5Pairs - 1) / kV5Pairs;
