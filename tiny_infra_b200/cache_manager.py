@@ -113,16 +113,18 @@ class BlockAllocator:
         new_block = np.full(len(sl), -1, np.int32)
         if len(sl) == 0:
             return new_block
-        pos = self.seq_len[sl].astype(np.int64)
-        over = np.nonzero(pos >= self.max_seq_len)[0]
-        stop = int(over[0]) if len(over) else len(sl)
-        lb = pos[:stop] // bs
-        need = np.nonzero(self.block_tables[sl[:stop], lb] == -1)[0]
+        pos = self.seq_len[sl]
+        stop = len(sl)
+        if pos.max() >= self.max_seq_len:
+            stop = int(np.argmax(pos >= self.max_seq_len))
+        # table entries of the slots' current logical blocks, by flat index (one gather)
+        flat = sl[:stop] * self.block_tables.shape[1] + pos[:stop] // bs
+        need = np.flatnonzero(np.take(self.block_tables, flat) == -1)
         take = min(len(need), len(self.free_blocks))
         if take:
             phys = np.fromiter((self.free_blocks.popleft() for _ in range(take)), np.int32, take)
             idx = need[:take]
-            self.block_tables[sl[idx], lb[idx]] = phys
+            np.put(self.block_tables, flat[idx], phys)
             new_block[idx] = phys
         if take < len(need):
             raise RuntimeError("OOM : No free physical blocks available for allocation.")
