@@ -10,7 +10,8 @@ reference's state-dict names (``load_reference_state_dict``).
 Per layer the decode forward is 8 kernel launches:
   rmsnorm -> QKV GEMM (+bias, RoPE, KV append) -> paged attention -> its split-K merge
   -> O GEMM (+residual, split-K) -> rmsnorm -> gate/up GEMM (+SwiGLU) -> down GEMM (+residual)
-(prefill: one ragged prefill-attention launch instead of the attention and its merge)
+(no merge when every sequence fits 32 blocks: the attention then finishes each sequence in one
+CTA; prefill: one ragged prefill-attention launch instead of the attention and its merge)
 with the residual stream kept in float32 (the reference keeps it in the model dtype; float32
 is closer to the float32 oracle).  The lm_head runs only on the rows whose logits are needed
 and, for greedy decoding, reduces to one token per row inside the GEMM epilogue.
