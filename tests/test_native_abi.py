@@ -68,3 +68,18 @@ def test_library_calls_without_gpu(native):
     rc = lib.ti_gemm(native.TI_EPI_SWIGLU16, fake, 896, fake, 896, 256, 9720, 896, fake,
                      4864, None, None, None, native.TI_DTYPE_BF16, 0, 1, None)
     assert rc != 0 and b"N % 16" in lib.ti_last_error()
+
+
+def test_attention_workspace_follows_kernel_choice(native):
+    """The size query mirrors the kernel choice: sequences of at most 32 blocks whose units (a
+    sequence's pair of kv heads) fit one wave of CTAs run one CTA per unit and need no split-K
+    slots, so the size does not grow with the table width; one block more per sequence, or one
+    unit more than the 148 SMs, and the split-K slots appear."""
+    lib = native.lib()
+
+    def ws(batch, max_blocks):
+        return lib.ti_paged_attention_workspace_bytes(batch, 14, 2, 64, max_blocks, 0)
+
+    assert ws(8, 16) == ws(8, 32)
+    assert ws(8, 33) > 4 * ws(8, 32)
+    assert ws(149, 32) > 4 * ws(148, 32)
